@@ -1,0 +1,304 @@
+/*
+ * CPU restatement of the reference's FP8 AdamW kernels.  TEST INFRASTRUCTURE ONLY:
+ * the product never links, imports or calls this file; tests, the smoke check and
+ * the CPU-baseline leg of the benchmark do, as the checker.
+ *
+ * It follows, statement by statement,
+ *   coat/optimizer/kernels/fp8_adamw_expand_cuda_kernel.cu:42-202  (expansion)
+ *   coat/optimizer/kernels/fp8_adamw_cuda_kernel.cu:38-124         (plain)
+ * with one CPU "thread" per element and one 128-thread "block" per group,
+ * including the shfl_down reduction trees (lane by lane), the zero-skipping
+ * minimum, the double-typed QUANT_MIN_VAL additions and the saturating
+ * round-to-nearest-even FP8 cast.  The plain-C AdamW update of the reference's
+ * stand-alone harness (csrc_expand_quantize/nvcc_qoptim.cu:39-57) is the same
+ * arithmetic and is what adamw_update() restates.
+ *
+ * Parity level: the transcendental calls (powf, log2f) go to the host libm here
+ * and to libdevice on the GPU; the two may differ in the last place, so agreement
+ * with a GPU kernel is at tolerance level for the expansion kernel (the
+ * reference's own test uses rtol 1e-4, tests/test_fp8_adamw_expand.py:296-308)
+ * and bit level for everything that does not pass through them.  Multiply-adds
+ * the CUDA compiler contracts are written as explicit fmaf(); build with
+ * -ffp-contract=off so the C compiler adds none of its own.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define QGROUP 128
+#define WARPSIZE 32
+
+/* ---- FP8 codecs (OCP E4M3 "fn" and E5M2), RNE, saturate-to-finite ------------- */
+
+float oracle_e4m3_to_float(uint8_t c) {
+    int s = c >> 7, e = (c >> 3) & 0xf, m = c & 7;
+    float v;
+    if (e == 0xf && m == 7) return NAN;
+    if (e == 0) v = ldexpf((float)m, -9);            /* subnormal: m * 2^-3 * 2^-6 */
+    else v = ldexpf((float)(8 + m), e - 7 - 3);
+    return s ? -v : v;
+}
+
+float oracle_e5m2_to_float(uint8_t c) {
+    int s = c >> 7, e = (c >> 2) & 0x1f, m = c & 3;
+    float v;
+    if (e == 0x1f) return m ? NAN : (s ? -INFINITY : INFINITY);
+    if (e == 0) v = ldexpf((float)m, -16);           /* m * 2^-2 * 2^-14 */
+    else v = ldexpf((float)(4 + m), e - 15 - 2);
+    return s ? -v : v;
+}
+
+/* Generic encoder: `mbits` mantissa bits, exponent bias, largest finite value and
+ * its code.  Round to nearest, ties to even, on the exact real value of x;
+ * |x| above the largest finite value (and infinities) saturate; NaN -> NaN code. */
+static uint8_t encode_fp8(float x, int mbits, int bias, float maxv, uint8_t maxcode, uint8_t nancode) {
+    uint8_t sign = signbit(x) ? 0x80 : 0;
+    if (isnan(x)) return sign | nancode;
+    float a = fabsf(x);
+    if (a >= maxv) return sign | maxcode;   /* includes +-inf; values between max and the
+                                               next grid point round down or saturate: same code */
+    if (a == 0.0f) return sign;
+    int e;
+    (void)frexpf(a, &e);                    /* a = f * 2^e, f in [0.5,1) -> exponent of 1.x form is e-1 */
+    int ex = e - 1;
+    int emin = 1 - bias;                    /* exponent of the smallest normal */
+    if (ex < emin) ex = emin;               /* subnormal range shares the spacing of emin */
+    /* spacing of representable values at this exponent: 2^(ex - mbits) */
+    float q = ldexpf(a, mbits - ex);        /* exact: a / spacing */
+    float r = nearbyintf(q);                /* default rounding mode: ties to even */
+    int iq = (int)r;
+    /* iq in [0, 2^(mbits+1)]; 2^(mbits+1) means carry into the next exponent */
+    int expfield, mant;
+    if (iq >= (1 << (mbits + 1))) { ex += 1; iq >>= 1; }
+    if (iq < (1 << mbits)) { expfield = 0; mant = iq; }           /* subnormal (or zero) */
+    else { expfield = ex + bias; mant = iq - (1 << mbits); }
+    uint8_t code = (uint8_t)((expfield << mbits) | mant);
+    if (code > maxcode) code = maxcode;     /* rounding carried past the largest finite value */
+    return sign | code;
+}
+
+uint8_t oracle_float_to_e4m3(float x) { return encode_fp8(x, 3, 7, 448.0f, 0x7e, 0x7f); }
+uint8_t oracle_float_to_e5m2(float x) { return encode_fp8(x, 2, 15, 57344.0f, 0x7b, 0x7f); }
+
+/* ---- bf16 ---------------------------------------------------------------------- */
+static float bf16_to_float(uint16_t b) { uint32_t u = (uint32_t)b << 16; float f; memcpy(&f, &u, 4); return f; }
+static uint16_t float_to_bf16(float f) {
+    uint32_t u; memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fff;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+uint16_t oracle_float_to_bf16(float f) { return float_to_bf16(f); }
+
+static float load_param(const void* base, int64_t i, int dtype) {
+    return dtype == 0 ? ((const float*)base)[i] : bf16_to_float(((const uint16_t*)base)[i]);
+}
+static void store_param(void* base, int64_t i, int dtype, float x) {
+    if (dtype == 0) ((float*)base)[i] = x; else ((uint16_t*)base)[i] = float_to_bf16(x);
+}
+
+/* ---- the AdamW update of one element (nvcc_qoptim.cu:46-56; .cu:52-64) -------- */
+/* fused_p: 1 if the final  p - lr*update  is evaluated as one fused multiply-add.  The
+ * CUDA compiler emits an unrounded mul/sub pair there, which its assembler contracts;
+ * the fused form is the one that matches the reference kernel bit for bit on sm_100
+ * (measured: 0 differing weights on a plain first step), so it is the default. */
+static float adamw_update(float* m, float* v, float p, float g, float beta1, float beta2, float lr,
+                          float wd, float eps, float correction1, float correction2_sqrt, int fused_p) {
+    float om1 = 1 - beta1, om2 = 1 - beta2;
+    float fm = fmaf(beta1, *m, om1 * g);                 /* beta1*m + (1-beta1)*g          */
+    float fv = fmaf(beta2, *v, (om2 * g) * g);           /* beta2*v + (1-beta2)*g*g        */
+    float denom = (sqrtf(fv) / correction2_sqrt + eps) * correction1;
+    float update = fmaf(wd, p, fm / denom);              /* m/denom + wd*p                 */
+    *m = fm; *v = fv;
+    return fused_p ? fmaf(-lr, update, p) : p - lr * update;
+}
+
+/* ---- shfl_down trees of the reference (.cu:89-103, :119-137) ------------------ */
+static void shfl_down_max_min(float* mx, float* mn, int with_min) {
+    /* mx/mn: 32 lanes.  shfl_down by i: lane l reads lane l+i, or itself if l+i >= 32 */
+    for (int i = WARPSIZE / 2; i > 0; i /= 2) {
+        float nmx[WARPSIZE], nmn[WARPSIZE];
+        for (int l = 0; l < WARPSIZE; ++l) {
+            int src = l + i < WARPSIZE ? l + i : l;
+            nmx[l] = fmaxf(mx[l], fabsf(mx[src]));
+            if (with_min) {
+                float a = fabsf(mn[src]);
+                nmn[l] = (a > 0) ? fminf(mn[l], a) : mn[l];
+            }
+        }
+        memcpy(mx, nmx, sizeof nmx);
+        if (with_min) memcpy(mn, nmn, sizeof nmn);
+    }
+}
+
+/* block-level |max| and zero-skipping |min| of 128 per-thread values */
+static void block_stats(const float* val, const int* in_range, int with_min, float* out_max, float* out_min) {
+    float smax[4], smin[4];
+    for (int w = 0; w < 4; ++w) {
+        float mx[WARPSIZE], mn[WARPSIZE];
+        for (int l = 0; l < WARPSIZE; ++l) {
+            mx[l] = fabsf(val[w * 32 + l]);
+            mn[l] = in_range[w * 32 + l] ? fabsf(val[w * 32 + l]) : 3.4028234663852886e38f;
+        }
+        shfl_down_max_min(mx, mn, with_min);
+        smax[w] = mx[0]; smin[w] = mn[0];
+    }
+    float mx[WARPSIZE], mn[WARPSIZE];
+    for (int l = 0; l < WARPSIZE; ++l) {
+        mx[l] = l < 4 ? smax[l] : 0.0f;
+        mn[l] = l < 4 ? smin[l] : 1e9f;
+    }
+    shfl_down_max_min(mx, mn, with_min);
+    *out_max = mx[0];
+    if (with_min) *out_min = mn[0];
+}
+
+/* flags */
+#define ORACLE_UNFUSED_P 1
+
+/* coat/optimizer/kernels/fp8_adamw_expand_cuda_kernel.cu:21-203, one call = one launch */
+void oracle_fp8_adamw_expand_step(void* params, const void* grads, uint8_t* exp_avg, float* scale_exp_avg,
+                                  float* expand_exp_avg, float* sqrtminmax_exp_avg, uint8_t* exp_avg_sq,
+                                  float* scale_exp_avg_sq, float* expand_exp_avg_sq,
+                                  float* sqrtminmax_exp_avg_sq, float beta1, float beta2, float lr, float wd,
+                                  float eps, int step, int qgroup_size, int expand_min, int64_t total_elements,
+                                  int p_dtype, int flags) {
+    (void)qgroup_size;
+    const int64_t groups = (total_elements + QGROUP - 1) / QGROUP;
+    const float correction1 = 1.0f - powf(beta1, (float)step);
+    const float correction2_sqrt = sqrtf(1.0f - powf(beta2, (float)step));
+    const float fexpand_min = (float)expand_min;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < groups; ++b) {
+        float fm[QGROUP], fv[QGROUP];
+        int in_range[QGROUP];
+        for (int t = 0; t < QGROUP; ++t) {
+            int64_t idx = b * QGROUP + t;
+            in_range[t] = idx < total_elements;
+            if (in_range[t]) {
+                float m = oracle_e4m3_to_float(exp_avg[idx]) * scale_exp_avg[b];
+                int sign = 1 - 2 * (signbit(m) ? 1 : 0);
+                m = (float)sign * powf(fabsf(m), 1 / expand_exp_avg[b]) * sqrtminmax_exp_avg[b];
+                float v = oracle_e4m3_to_float(exp_avg_sq[idx]) * scale_exp_avg_sq[b];
+                v = powf(v, 1 / expand_exp_avg_sq[b]) * sqrtminmax_exp_avg_sq[b];
+                float p = load_param(params, idx, p_dtype), g = load_param(grads, idx, p_dtype);
+                p = adamw_update(&m, &v, p, g, beta1, beta2, lr, wd, eps, correction1, correction2_sqrt,
+                                 !(flags & ORACLE_UNFUSED_P));
+                store_param(params, idx, p_dtype, p);
+                fm[t] = m; fv[t] = v;
+            } else {
+                fm[t] = 0.0f; fv[t] = 0.0f;
+            }
+        }
+        float mmax, mmin, vmax, vmin;
+        block_stats(fm, in_range, 1, &mmax, &mmin);
+        block_stats(fv, in_range, 1, &vmax, &vmin);
+
+        const float fp8MaxVal = 448;
+        float firstMaxVal = (float)((double)mmax + 1e-30);
+        float firstMinVal = (float)((double)mmin + 1e-30);
+        float secondMaxVal = (float)((double)vmax + 1e-30);
+        float secondMinVal = (float)((double)vmin + 1e-30);
+        float firstRatio = firstMaxVal / firstMinVal;
+        float secondRatio = secondMaxVal / secondMinVal;
+        float firstSqrtMinMax = sqrtf(firstMaxVal) * sqrtf(firstMinVal);
+        float secondSqrtMinMax = sqrtf(secondMaxVal) * sqrtf(secondMinVal);
+        float ratioUpperBound = fp8MaxVal * fp8MaxVal / 2;
+        float firstExp = floorf((log2f(ratioUpperBound) / log2f(firstRatio)) * fexpand_min) / fexpand_min;
+        float secondExp = floorf((log2f(ratioUpperBound) / log2f(secondRatio)) * fexpand_min) / fexpand_min;
+        float new_scale_exp_avg = powf(firstMaxVal / firstSqrtMinMax, firstExp) / fp8MaxVal;
+        float new_scale_exp_avg_sq = powf(secondMaxVal / secondSqrtMinMax, secondExp) / fp8MaxVal;
+
+        for (int t = 0; t < QGROUP; ++t) {
+            if (!in_range[t]) continue;
+            int64_t idx = b * QGROUP + t;
+            int sign = 1 - 2 * (signbit(fm[t]) ? 1 : 0);
+            float m = (float)sign * powf(fabsf(fm[t]) / firstSqrtMinMax, firstExp);
+            float v = powf(fv[t] / secondSqrtMinMax, secondExp);
+            exp_avg[idx] = oracle_float_to_e4m3(m / new_scale_exp_avg);
+            exp_avg_sq[idx] = oracle_float_to_e4m3(v / new_scale_exp_avg_sq);
+        }
+        scale_exp_avg[b] = new_scale_exp_avg;
+        scale_exp_avg_sq[b] = new_scale_exp_avg_sq;
+        expand_exp_avg[b] = firstExp;
+        expand_exp_avg_sq[b] = secondExp;
+        sqrtminmax_exp_avg[b] = firstSqrtMinMax;
+        sqrtminmax_exp_avg_sq[b] = secondSqrtMinMax;
+    }
+}
+
+/* coat/optimizer/kernels/fp8_adamw_cuda_kernel.cu:21-125.  The reference lets all 128
+ * threads add 1e-20 to the shared maximum without synchronisation (:105-106); this
+ * restatement applies the addition once, which is what the race yields whenever the
+ * maximum is large enough to absorb 1e-20 (any maximum above about 2e-13). */
+void oracle_fp8_adamw_step(void* params, const void* grads, uint8_t* exp_avg, float* scale_exp_avg,
+                           uint8_t* exp_avg_sq, float* scale_exp_avg_sq, float beta1, float beta2, float lr,
+                           float wd, float eps, int step, int qgroup_size, int64_t total_elements, int p_dtype,
+                           int flags) {
+    (void)qgroup_size;
+    const int64_t groups = (total_elements + QGROUP - 1) / QGROUP;
+    const float correction1 = 1.0f - powf(beta1, (float)step);
+    const float correction2_sqrt = sqrtf(1.0f - powf(beta2, (float)step));
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < groups; ++b) {
+        float fm[QGROUP], fv[QGROUP];
+        int in_range[QGROUP];
+        for (int t = 0; t < QGROUP; ++t) {
+            int64_t idx = b * QGROUP + t;
+            in_range[t] = idx < total_elements;
+            fm[t] = 0.0f; fv[t] = 0.0f;
+            if (in_range[t]) {
+                float m = oracle_e4m3_to_float(exp_avg[idx]) * scale_exp_avg[b];
+                float v = oracle_e4m3_to_float(exp_avg_sq[idx]) * scale_exp_avg_sq[b];
+                float p = load_param(params, idx, p_dtype), g = load_param(grads, idx, p_dtype);
+                p = adamw_update(&m, &v, p, g, beta1, beta2, lr, wd, eps, correction1, correction2_sqrt,
+                                 !(flags & ORACLE_UNFUSED_P));
+                store_param(params, idx, p_dtype, p);
+                fm[t] = m; fv[t] = v;
+            }
+        }
+        float mmax, vmax, unused;
+        block_stats(fm, in_range, 0, &mmax, &unused);
+        block_stats(fv, in_range, 0, &vmax, &unused);
+        const float fp8MaxVal = 448;
+        float a = (float)((double)mmax + 1e-20);
+        float c = (float)((double)vmax + 1e-20);
+        float new_scale_exp_avg = a / fp8MaxVal;
+        float new_scale_exp_avg_sq = c / fp8MaxVal;
+        for (int t = 0; t < QGROUP; ++t) {
+            if (!in_range[t]) continue;
+            int64_t idx = b * QGROUP + t;
+            exp_avg[idx] = oracle_float_to_e4m3(fm[t] / new_scale_exp_avg);
+            exp_avg_sq[idx] = oracle_float_to_e4m3(fv[t] / new_scale_exp_avg_sq);
+        }
+        scale_exp_avg[b] = new_scale_exp_avg;
+        scale_exp_avg_sq[b] = new_scale_exp_avg_sq;
+    }
+}
+
+/* Dequantise a state tensor back to fp32 (what the next step's :44-49 would read):
+ * used by tests to compare states at value level. */
+void oracle_fp8_adamw_dequant(const uint8_t* codes, const float* scale, const float* expand,
+                              const float* sqrtminmax, float* out, int64_t total_elements, int is_second) {
+    for (int64_t idx = 0; idx < total_elements; ++idx) {
+        int64_t b = idx / QGROUP;
+        float x = oracle_e4m3_to_float(codes[idx]) * scale[b];
+        if (expand) {
+            if (is_second) x = powf(x, 1 / expand[b]) * sqrtminmax[b];
+            else {
+                int sign = 1 - 2 * (signbit(x) ? 1 : 0);
+                x = (float)sign * powf(fabsf(x), 1 / expand[b]) * sqrtminmax[b];
+            }
+        }
+        out[idx] = x;
+    }
+}
+
+/* Bulk codecs for the python side of the test-suite. */
+void oracle_encode_fp8(const float* x, uint8_t* out, int64_t n, int fmt) {
+    for (int64_t i = 0; i < n; ++i) out[i] = fmt == 0 ? oracle_float_to_e4m3(x[i]) : oracle_float_to_e5m2(x[i]);
+}
+void oracle_decode_fp8(const uint8_t* c, float* out, int64_t n, int fmt) {
+    for (int64_t i = 0; i < n; ++i) out[i] = fmt == 0 ? oracle_e4m3_to_float(c[i]) : oracle_e5m2_to_float(c[i]);
+}
