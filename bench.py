@@ -1,0 +1,332 @@
+#!/usr/bin/env python
+"""Benchmark of the COAT quantization hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Headline workload ("step"): one fused FP8-AdamW step with Dynamic Range Expansion over the full
+Llama-2-7B parameter set (291 tensors, 6 738 415 616 fp32 master weights, synthetic N(0,1e-3)
+gradients, E4M3 moments in groups of 128), sharded ZeRO-style over the N GPUs on 128-element
+boundaries and followed by the all-gather of the updated bf16 weights.  Total work is fixed, so
+scaling is "strong".  Rank 0 prints ONE JSON line.
+
+`--impl reference` times the CPU restatement of the reference kernel (oracle/, OpenMP over groups) on
+the host cores, on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fp8_adamw_expand_params_per_s"
+UNIT = "params/s"
+BYTES_PER_PARAM = 16.375      # read p4 g4 m1 v1, write p4 m1 v1, 12 fp32 per 128-group
+BYTES_PER_PARAM_BF16 = 18.375  # + the bf16 weight copy for the all-gather
+HYPER = dict(lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+
+
+def llama2_7b_shapes():
+    H, I, V, L = 4096, 11008, 32000, 32
+    layer = [(H, H)] * 4 + [(I, H), (I, H), (H, I), (H,), (H,)]
+    return [(V, H)] + layer * L + [(H,), (V, H)]
+
+
+def numel(shape):
+    n = 1
+    for s in shape:
+        n *= s
+    return n
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, col in (("hw_slowdown", 5), ("hw_thermal_slowdown", 6), ("sw_thermal_slowdown", 7),
+                              ("sw_power_cap", 8)):
+                if r[col].lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the C restatement of the reference kernel on the host cores
+# ------------------------------------------------------------------------------------------------
+
+def cpu_reference_steps(n_params, min_seconds, min_steps=2, seed=0):
+    """Time oracle.fp8_adamw_expand_step on `n_params` fp32 params; returns (params/s, steps, cores)."""
+    import torch
+    from oracle import adamw as O
+    gen = torch.Generator().manual_seed(seed)
+    G = (n_params + 127) // 128
+    p = torch.randn(n_params, generator=gen) * 0.02
+    g = torch.randn(n_params, generator=gen) * 1e-3
+    m = torch.zeros(n_params, dtype=torch.uint8)
+    v = torch.zeros(n_params, dtype=torch.uint8)
+    vec = [torch.zeros(G), torch.ones(G), torch.ones(G), torch.zeros(G), torch.ones(G), torch.ones(G)]
+
+    def one(step):
+        O.fp8_adamw_expand_step(p, g, m, vec[0], vec[1], vec[2], v, vec[3], vec[4], vec[5], HYPER["betas"][0],
+                                HYPER["betas"][1], HYPER["lr"], HYPER["weight_decay"], HYPER["eps"], step, 128, 16)
+
+    one(1)  # warm-up: leaves realistic (non-zero) state behind
+    steps, t0 = 0, time.perf_counter()
+    while steps < min_steps or time.perf_counter() - t0 < min_seconds:
+        one(2 + steps)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return n_params * steps / dt, steps, dt, os.cpu_count()
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    n = 4096 * 4096
+    per_step = []
+    for _ in range(max(0, args.warmup)):
+        cpu_reference_steps(n, 0.0, min_steps=1)
+    t0 = time.perf_counter()
+    total_steps = 0
+    for _ in range(max(1, args.steps)):
+        rate, steps, dt, cores = cpu_reference_steps(n, 1.0, min_steps=1)
+        per_step.append(dt / steps)
+        total_steps += steps
+    ms = 1e3 * sum(per_step) / len(per_step)
+    value = n / (ms / 1e3)
+    sample = (f"one 4096x4096 fp32 tensor (16 777 216 params) per step, C restatement of the reference kernel "
+              f"(oracle/fp8_adamw_oracle.c), OpenMP over groups")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
+        "config": {"workload": "FP8AdamW-expand step, Llama-2-7B parameter set (bounded CPU sample: one "
+                               "4096x4096 tensor per step)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------------
+
+def fill_synthetic(opt, shapes, torch):
+    """p ~ N(0, 0.02), g ~ N(0, 1e-3), seeded per tensor (seed 100+i), generated on the device piece by
+    piece (the full set is 27 GB per array; there are no checkpoints or datasets on the box)."""
+    gen = torch.Generator(device=opt.device)
+    for pc in opt.my_pieces:
+        gen.manual_seed(100 + pc.tensor * 16 + opt.rank)
+        sl = slice(pc.offset, pc.offset + pc.numel)
+        opt.param[sl].normal_(0.0, 0.02, generator=gen)
+        opt.grad[sl].normal_(0.0, 1e-3, generator=gen)
+
+
+def e2e_public_api(torch, device, steps, warmup):
+    """params/s through the public optimizer API (CoatAdamW.step) with HOST gradients: every step copies
+    the gradients of one Llama-2-7B decoder layer (9 tensors, 202 383 360 params) from pinned host memory
+    and reads the updated fp32 weights back to pinned host memory."""
+    from coat_b200.optimizer import CoatAdamW
+    H, I = 4096, 11008
+    shapes = [(H, H)] * 4 + [(I, H), (I, H), (H, I), (H,), (H,)]
+    gen = torch.Generator().manual_seed(7)
+    params = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(device)) for s in shapes]
+    host_g = [(torch.randn(s, generator=gen) * 1e-3).pin_memory() for s in shapes]
+    host_p = [torch.empty(s).pin_memory() for s in shapes]
+    for p in params:
+        p.grad = torch.empty_like(p)
+    opt = CoatAdamW(params, **HYPER)
+    n = sum(numel(s) for s in shapes)
+
+    def one():
+        for p, hg in zip(params, host_g):
+            p.grad.copy_(hg, non_blocking=True)
+        opt.step()
+        for p, hp in zip(params, host_p):
+            hp.copy_(p.detach(), non_blocking=True)
+
+    for _ in range(max(warmup, 2)):
+        one()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    return n / (ms / 1e3), 4 * n, 4 * n, n
+
+
+def run_gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+    from coat_b200.sharded import ShardedCoatAdamW
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU path for the product)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+
+    shapes = llama2_7b_shapes()
+    numels = [numel(s) for s in shapes]
+    total = sum(numels)
+    opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, **HYPER)
+    fill_synthetic(opt, shapes, torch)
+    my_params = sum(pc.numel for pc in opt.my_pieces)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(args.warmup, 3)):
+        opt.step()
+    barrier()
+    sampler = ClockSampler(local)
+    if rank == 0:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    for _ in range(args.steps):
+        opt.step()
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # the fused kernel alone (no collective), for the roofline
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for _ in range(args.steps):
+        opt.local_step()
+    k1.record()
+    torch.cuda.synchronize(device)
+    kernel_ms = k0.elapsed_time(k1) / args.steps
+    clocks = sampler.stop() if rank == 0 else None
+
+    t = torch.tensor([ms, kernel_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kernel_ms = t.tolist()
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = my_params * BYTES_PER_PARAM_BF16 / (kernel_ms / 1e3) / 1e9
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "adamw_traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                tr = json.load(f)
+            # bytes per parameter measured by ncu on a smaller launch, scaled to this launch
+            traffic = tr["dram_bytes_per_param"] * my_params
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_kernel<float,expand,table>",
+                    "kernel_ms": kernel_ms, "algorithmic_bytes_per_param": BYTES_PER_PARAM_BF16}
+        e2e_v, h2d, d2h, e2e_n = e2e_public_api(torch, device, max(3, min(args.steps, 10)), args.warmup)
+        cpu_v, cpu_steps, cpu_dt, cores = cpu_reference_steps(4096 * 4096, 10.0) if world == 1 else (None,) * 4
+        line = {
+            "metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
+            "config": {"workload": "FP8AdamW-expand step over the full Llama-2-7B parameter set "
+                                   "(291 tensors, 6738415616 params), fp32 master weights, E4M3 moments group 128, "
+                                   "bf16 weight copy" + (" + NCCL all-gather" if world > 1 else ""),
+                       "parallelism": f"zero-shard x{world} on 128-element group boundaries",
+                       "l2": "inputs larger than L2 (>= 10 GB per GPU per step)",
+                       "hyper": {"lr": 1e-4, "betas": [0.9, 0.95], "wd": 0.1, "eps": 1e-8, "expand_min": 16}},
+            "roofline": roofline,
+            "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "workload": f"CoatAdamW.step on one decoder layer ({e2e_n} params), grads from pinned host "
+                                "memory, updated fp32 weights read back"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if cpu_v is not None:
+            line["cpu_baseline"] = {
+                "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
+                "sample": f"{cpu_steps} steps of one 4096x4096 tensor in {cpu_dt:.1f} s, C restatement of the "
+                          "reference kernel with OpenMP over groups"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

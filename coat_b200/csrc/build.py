@@ -57,7 +57,7 @@ def build(force=False, verbose=False):
     with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(run, jobs))
     if jobs or force or _stale(LIB, objs):
-        run([nvcc, "-shared", "-o", LIB] + objs + ["-lcudart", "-lcuda"])
+        run([nvcc, "-shared", "-o", LIB] + objs + ["-lcudart"])
     return LIB
 
 
