@@ -231,7 +231,7 @@ def run_gpu_arm(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=device)
 
-    shapes = llama2_7b_shapes()
+    shapes = llama2_7b_shapes() if args.workload == "llama2-7b" else [(4096, 4096)]
     numels = [numel(s) for s in shapes]
     total = sum(numels)
     opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, **HYPER)
@@ -243,8 +243,23 @@ def run_gpu_arm(args):
             dist.barrier()
         torch.cuda.synchronize(device)
 
+    # two independent gradient sets, alternated, so that the moments do not converge onto one
+    # fixed gradient (a single repeated gradient makes the requantisation unrealistically easy)
+    grads = [opt.grad, torch.empty_like(opt.grad).normal_(0.0, 1e-3)]
+    tables = []
+    for gbuf in grads:   # one device-side tensor table per gradient set, built outside the timed region
+        opt.grad = gbuf
+        opt._build_table()
+        tables.append(opt._table)
+    step_no = [0]
+
+    def one_step(local_only=False):
+        opt.grad, opt._table = grads[step_no[0] & 1], tables[step_no[0] & 1]
+        step_no[0] += 1
+        opt.local_step() if local_only else opt.step()
+
     for _ in range(max(args.warmup, 3)):
-        opt.step()
+        one_step()
     barrier()
     sampler = ClockSampler(local)
     if rank == 0:
@@ -253,7 +268,7 @@ def run_gpu_arm(args):
     barrier()
     e0.record()
     for _ in range(args.steps):
-        opt.step()
+        one_step()
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1) / args.steps
@@ -262,7 +277,7 @@ def run_gpu_arm(args):
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0.record()
     for _ in range(args.steps):
-        opt.local_step()
+        one_step(local_only=True)
     k1.record()
     torch.cuda.synchronize(device)
     kernel_ms = k0.elapsed_time(k1) / args.steps
@@ -286,17 +301,24 @@ def run_gpu_arm(args):
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_kernel<float,expand,table>",
                     "kernel_ms": kernel_ms, "algorithmic_bytes_per_param": BYTES_PER_PARAM_BF16}
-        e2e_v, h2d, d2h, e2e_n = e2e_public_api(torch, device, max(3, min(args.steps, 10)), args.warmup)
-        cpu_v, cpu_steps, cpu_dt, cores = cpu_reference_steps(4096 * 4096, 10.0) if world == 1 else (None,) * 4
+        if args.kernel_only:  # profiling runs: nothing but the fused kernel
+            e2e_v, h2d, d2h, e2e_n = None, 0, 0, 0
+            cpu_v = cpu_steps = cpu_dt = cores = None
+        else:
+            e2e_v, h2d, d2h, e2e_n = e2e_public_api(torch, device, max(3, min(args.steps, 10)), args.warmup)
+            cpu_v, cpu_steps, cpu_dt, cores = cpu_reference_steps(4096 * 4096, 10.0) if world == 1 else (None,) * 4
         line = {
             "metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
-            "config": {"workload": "FP8AdamW-expand step over the full Llama-2-7B parameter set "
-                                   "(291 tensors, 6738415616 params), fp32 master weights, E4M3 moments group 128, "
+            "config": {"workload": ("FP8AdamW-expand step over the full Llama-2-7B parameter set "
+                                    "(291 tensors, 6738415616 params)" if args.workload == "llama2-7b" else
+                                    "FP8AdamW-expand step over one 4096x4096 tensor (profiling case)") +
+                                   ", fp32 master weights, E4M3 moments group 128, "
                                    "bf16 weight copy" + (" + NCCL all-gather" if world > 1 else ""),
                        "parallelism": f"zero-shard x{world} on 128-element group boundaries",
-                       "l2": "inputs larger than L2 (>= 10 GB per GPU per step)",
+                       "l2": "inputs larger than L2 (>= 10 GB per GPU per step)" if args.workload == "llama2-7b" else
+                             "inputs larger than L2 (308 MB per step)",
                        "hyper": {"lr": 1e-4, "betas": [0.9, 0.95], "wd": 0.1, "eps": 1e-8, "expand_min": 16}},
             "roofline": roofline,
             "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -321,6 +343,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1"],
+                    help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
+    ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)

@@ -9,7 +9,7 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcoat_b200.so")
+LIB_PATH = os.environ.get("COAT_B200_LIB", os.path.join(_HERE, "libcoat_b200.so"))
 
 F32, BF16, F16 = 0, 1, 2
 E4M3, E5M2 = 0, 1
@@ -26,6 +26,8 @@ SIGNATURES = {
     "coat_fp8_adamw_expand_step": [_vp] * 10 + [_f] * 5 + [_i, _i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_step": [_vp] * 6 + [_f] * 5 + [_i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_multi_step": [_vp, _vp, _i, _i64, _i] + [_f] * 5 + [_i, _i, _i, _i, _i, _vp],
+    "coat_fp8_adamw_debug_counters": [_vp],
+    "coat_fp8_adamw_device_status": [],
 }
 
 

@@ -18,6 +18,9 @@
 
 #include <math.h>
 
+#include <cstddef>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
@@ -131,6 +134,14 @@ __device__ float ref_min_tree_128(float* buf /*[128], clobbered*/) {
     return ref_min_combine(a, b);
 }
 
+// m' = beta1*m + (1-beta1)*g and v' = beta2*v + ((1-beta2)*g)*g  (fp8_adamw_expand_cuda_kernel.cu:52-55)
+__device__ __forceinline__ float adam_first(float beta1, float m, float om_beta1, float g) {
+    return __fmaf_rn(beta1, m, __fmul_rn(om_beta1, g));
+}
+__device__ __forceinline__ float adam_second(float beta2, float v, float om_beta2, float g) {
+    return __fmaf_rn(beta2, v, __fmul_rn(__fmul_rn(om_beta2, g), g));
+}
+
 // ---- per-group scalars of the expansion ------------------------------------------
 // fp8_adamw_expand_cuda_kernel.cu:151-181.  QUANT_MIN_VAL is a double literal there, so
 // the additions are done in double and rounded back to float.
@@ -157,7 +168,7 @@ __device__ __forceinline__ void expand_group_scalars(float absmax, float absmin,
 // ---- one group, exact arithmetic ---------------------------------------------------
 // `lane` owns elements [base, base+4) of the tensor; `nvalid` of them (0..4) exist.
 template <typename scalar_t, bool EXPAND>
-__device__ __forceinline__ void process_group_exact(const TensorDesc& t, int64_t group, int lane,
+__device__ __noinline__ void process_group_exact(const TensorDesc& t, int64_t group, int lane,
                                                     const AdamwHyper& h, float om_beta1,
                                                     float om_beta2, float correction1,
                                                     float correction2_sqrt, bool vec_ok,
@@ -210,11 +221,14 @@ __device__ __forceinline__ void process_group_exact(const TensorDesc& t, int64_t
             float_exp_avg = sign_exp_avg * powf(fabsf(float_exp_avg), inv_km) * sqm;
             float_exp_avg_sq = powf(float_exp_avg_sq, inv_kv) * sqv;
         }
-        float_exp_avg = h.beta1 * float_exp_avg + om_beta1 * g[j];
-        float_exp_avg_sq = h.beta2 * float_exp_avg_sq + om_beta2 * g[j] * g[j];
-        float denom = (sqrtf(float_exp_avg_sq) / correction2_sqrt + h.eps) * correction1;
-        float update = (float_exp_avg / denom) + (h.wd * p[j]);
-        p[j] = p[j] - (h.lr * update);
+        // beta1*m + (1-beta1)*g etc. with the contractions nvcc applies to the reference's source
+        // written out (they are verified bit for bit against the reference's compiled kernel)
+        float_exp_avg = adam_first(h.beta1, float_exp_avg, om_beta1, g[j]);
+        float_exp_avg_sq = adam_second(h.beta2, float_exp_avg_sq, om_beta2, g[j]);
+        float denom = __fmul_rn(__fadd_rn(__fdiv_rn(__fsqrt_rn(float_exp_avg_sq), correction2_sqrt), h.eps),
+                                correction1);
+        float update = __fmaf_rn(h.wd, p[j], __fdiv_rn(float_exp_avg, denom));
+        p[j] = __fmaf_rn(-h.lr, update, p[j]);
         if (j >= nvalid) { float_exp_avg = 0.0f; float_exp_avg_sq = 0.0f; }
         fm[j] = float_exp_avg;
         fv[j] = float_exp_avg_sq;
@@ -348,28 +362,611 @@ __device__ __forceinline__ bool desc_vec_ok(const TensorDesc& t, int align) {
     return ((a & (uintptr_t)(align - 1)) | (c & 3) | (o & 7)) == 0;
 }
 
+// =====================================================================================
+// Guarded fast path of the expansion step
+// =====================================================================================
+// The exact step spends ~4 libdevice powf per element (dequantise m and v with x^(1/k),
+// requantise with x^k), which makes it instruction bound at ~15 % of the HBM roofline.
+// The fast path evaluates those four powers as ex2.approx(k * lg2.approx(x)) and keeps
+// the QUANTISED RESULT bit-identical to the exact step by bounding the error it makes:
+//
+//  * every approximate moment m~' carries an absolute error bound delta (from the
+//    documented MUFU error bounds, the deviation allowed to libdevice's powf, and the
+//    roundings in between; see fast_dequant_eps / requant constants below);
+//  * the group maximum and minimum decide the stored scale, exponent and sqrt(max*min),
+//    so every element whose interval [m~'-delta, m~'+delta] could hold the maximum or the
+//    minimum is recomputed with the exact routine (typically 4 elements of 128), and the
+//    group scalars are then computed exactly from exact inputs;
+//  * an FP8 code is accepted only if the lower and the upper end of the interval of the
+//    scaled value round to the same code; otherwise that element is recomputed exactly;
+//  * groups that are not in the regime the bounds were derived for (fresh state, zero /
+//    non-finite scales, a possible exact zero or sign change, exponents outside [1/64,64],
+//    NaNs, a partial last group, unaligned pointers) take the exact path as a whole.
+//
+// Only the fp32 weights differ from the exact step, by the relative error of the
+// approximate moments (a few 1e-6 of one update), since they are not quantised.
+
+__device__ __forceinline__ float fast_lg2(float x) { float r; asm("lg2.approx.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float fast_ex2(float x) { float r; asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float fast_rcp(float x) { float r; asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float fast_sqrt(float x) { float r; asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+
+constexpr float kLn2 = 0.6931472f;
+constexpr float k2m21 = 4.7683716e-07f, k2m22 = 2.3841858e-07f, k2m23 = 1.1920929e-07f, k2m24 = 5.9604645e-08f;
+// lg2.approx: absolute error <= 2^-22 for arguments in [0.5, 2], relative error <= 2^-22 elsewhere;
+// ex2.approx: relative error <= 2^-22.  libdevice powf is allowed 4 ulp (<= 2^-21) from the true value.
+constexpr float kLgErr = k2m22, kEx2Err = k2m22, kPowDev = k2m21;
+constexpr float kSafety = 1.25f;  // applied on top of every modelled bound
+constexpr float kSaneLo = 8.6736174e-19f /*2^-60*/, kSaneHi = 1.1529215e+18f /*2^60*/;
+
+struct StepConsts {
+    float om_beta1, om_beta2, correction1, correction2_sqrt;
+    float p_a, p_b;   // denom = sqrt(v)*p_a + p_b  ==  (sqrt(v)/correction2_sqrt + eps)*correction1
+};
+
+__device__ __forceinline__ bool sane_pos(float x) { return x >= kSaneLo && x <= kSaneHi; }
+
+// Relative error bound of  ex2(lg2(c*s) * ik) * r  against libdevice powf(c*s, ik) * r, for any
+// E4M3 magnitude c in [2^-9, 448]; lgs = lg2(s) (approximate is fine, 1e-3 is added).
+__device__ __forceinline__ float fast_dequant_eps(float ik, float lgs, float& tb) {
+    float lb = 9.0f + fabsf(lgs) + 1e-3f;          // |lg2(c*s)| <= lb
+    tb = ik * lb;                                   // |exponent handed to ex2| <= tb
+    return kSafety * (kLn2 * tb * (kLgErr + k2m24) + kEx2Err + kPowDev + k2m23);
+}
+
+template <int N>
+__device__ __forceinline__ float sel4(const float (&a)[N], int j) {
+    float r = a[0];
+    r = j == 1 ? a[1] : r;
+    r = j == 2 ? a[2] : r;
+    r = j == 3 ? a[3] : r;
+    return r;
+}
+
+// exact m' (or v') of one element: the statements of fp8_adamw_expand_cuda_kernel.cu:44-55
+__device__ __noinline__ float exact_moment(float x, float ik, float r, float beta, float addend, bool second) {
+    float pw = powf(fabsf(x), ik);
+    if (!second && signbit(x)) pw = -pw;            // sign_exp_avg * powf(|x|, 1/k)
+    return __fmaf_rn(beta, pw * r, addend);
+}
+// exact FP8 code of one element from its exact moment (:175-187)
+__device__ __noinline__ uint32_t exact_code(float val, float r, float k, float scale, bool second) {
+    float pw = powf(__fdiv_rn(fabsf(val), r), k);
+    if (!second && signbit(val)) pw = -pw;
+    return coat_float_to_fp8<COAT_E4M3>(__fdiv_rn(pw, scale));
+}
+
+__device__ __forceinline__ uint32_t redux_max_f(float v) { return __reduce_max_sync(COAT_FULL_MASK, __float_as_uint(v)); }
+__device__ __forceinline__ uint32_t redux_min_f(float v) { return __reduce_min_sync(COAT_FULL_MASK, __float_as_uint(v)); }
+
+// ---- tiled organisation ------------------------------------------------------------------
+// Work that is uniform over a group costs a full warp instruction whether 1 or 32 lanes are
+// busy, so a group's set-up, its exact scalars (2 log2f, a powf, sqrts, divisions) and the exact
+// recomputation of single elements must not run once per group with the other lanes idle.  A
+// warp therefore takes a TILE of kTile consecutive groups and runs in phases:
+//   0  one lane per group: locate the tensor, read the stored scalars, 1/k, error bounds, checks
+//   1  per group, lanes over elements: load, approximate dequantise, Adam, warp reductions,
+//      candidate detection, weight update and store; m' and v' go to the warp's shared tile
+//   2a candidate list, one entry per lane: exact moment, shared-memory atomic max/min
+//   2b one lane per (group, moment): exact group scalars, stored to global and to the tile
+//   3  per group, lanes over elements: requantise and store codes; an element whose interval
+//      straddles a rounding boundary is appended to a pending list that outlives the tile
+//   4  whenever 32 entries are pending (and at the end): exact moment + exact code per lane,
+//      patched into the code arrays bytewise
+#ifdef COAT_ADAMW_PROFILE
+#define PHASE_CLOCK(i) do { long long now_ = clock64(); phase_cycles[i] += now_ - phase_t; phase_t = now_; } while (0)
+#else
+#define PHASE_CLOCK(i) do { } while (0)
+#endif
+#ifndef COAT_ADAMW_TILE
+#define COAT_ADAMW_TILE 6
+#endif
+#ifndef COAT_ADAMW_TILED_THREADS
+#define COAT_ADAMW_TILED_THREADS 128
+#endif
+constexpr int kTile = COAT_ADAMW_TILE;
+constexpr int kTiledThreads = COAT_ADAMW_TILED_THREADS;
+constexpr int kTiledWarps = kTiledThreads / COAT_WARP;
+constexpr int kCandPerGroup = 16;
+constexpr int kPendCap = 64;
+constexpr float kTiny = 7.8886091e-31f;   // 2^-100: below this the flush-to-zero MUFU forms lose accuracy
+
+struct __align__(16) WarpTile {
+    // Staging buffers, filled per tile by bulk asynchronous copies (TMA, non-multicast) that complete on
+    // `mbar`: the weights, later overwritten in place by m'; the gradients, later overwritten by v';
+    // the old codes of both moments (kept: the exact recomputations read them).
+    float4 m1[kTile][32];        // p on arrival
+    float4 v1[kTile][32];        // g on arrival
+    uint32_t cw_m[kTile][32];
+    uint32_t cw_v[kTile][32];
+    float old_sc[kTile][8];      // s_m, 1/k_m, r_m, eps_dm, s_v, 1/k_v, r_v, eps_dv
+    float newc[kTile][2][8];     // r', k', s', 1/r', scale_lo, scale_hi, D (first moment), in-range flag
+    float delta[kTile][2];       // absolute error bound of |m'| and of v' in this group
+    uint32_t stat[kTile][4];     // exact max m, min m, max v, min v (float bit patterns)
+    unsigned long long ptr_p[kTile], ptr_g[kTile], ptr_m[kTile], ptr_v[kTile], ptr_bf[kTile];
+    long long local[kTile];      // group index inside its tensor
+    int ti[kTile];               // tensor index
+    uint32_t flags[kTile];       // bit 0: stored scalars are in the modelled range; bit 1: full, aligned group
+    uint16_t cand[kTile * kCandPerGroup];
+    // pending exact recomputations (structure of arrays)
+    float pe_x[kPendCap], pe_ik[kPendCap], pe_r[kPendCap], pe_g[kPendCap];
+    float pe_nr[kPendCap], pe_nk[kPendCap], pe_ns[kPendCap];
+    unsigned long long pe_dst[kPendCap];   // byte address of the code, bit 63 = second moment
+    unsigned long long mbar;               // completion barrier of the staging copies
+    uint32_t n_cand, n_pend;
+};
+
+static_assert(offsetof(WarpTile, old_sc) % 16 == 0 && offsetof(WarpTile, newc) % 16 == 0 &&
+              offsetof(WarpTile, v1) % 16 == 0 && offsetof(WarpTile, cw_m) % 16 == 0 &&
+              offsetof(WarpTile, cw_v) % 16 == 0 && offsetof(WarpTile, mbar) % 8 == 0 && sizeof(WarpTile) % 16 == 0,
+              "vector accesses and bulk copies into the tile need 16-byte aligned members");
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Bounded wait: gives up after ~2^24 polls and reports it (the caller sets the error flag and leaves).
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
+    for (int tries = 0; tries < (1 << 24); ++tries) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+// 1-D bulk copy global -> shared of this CTA, completion counted in bytes on the mbarrier.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ int g_adamw_device_status = 0;   // set to COAT_E_TIMEOUT if a bounded wait ran out
+
+// Magnitudes of four packed E4M3 codes as floats, without the conversion unit: the 7 magnitude bits of a
+// code, placed at bit 20 of a float, read as 2^(e-127)*1.mmm (or as the float subnormal 0.mmm*2^-126 when
+// e == 0), which is the code's value times 2^-120 in both cases; the multiplication by 2^120 is exact.
+// A NaN code (0x7f) would come out as 480: the caller rejects words that contain one (has_nan_code).
+__device__ __forceinline__ void e4m3x4_magnitudes(uint32_t w, float (&f)[4]) {
+    const float k2p120 = 1.3292279957849159e36f;
+    f[0] = __uint_as_float((w << 20) & 0x07f00000u) * k2p120;
+    f[1] = __uint_as_float((w << 12) & 0x07f00000u) * k2p120;
+    f[2] = __uint_as_float((w << 4) & 0x07f00000u) * k2p120;
+    f[3] = __uint_as_float((w >> 4) & 0x07f00000u) * k2p120;
+}
+// non-zero iff one of the four bytes has magnitude bits 0x7f
+__device__ __forceinline__ uint32_t has_nan_code(uint32_t w) { return ((w & 0x7f7f7f7fu) + 0x01010101u) & 0x80808080u; }
+
+__device__ __forceinline__ float lg2_ftz(float x) { float r; asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float ex2_ftz(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float rcp_ftz(float x) { float r; asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float sqrt_ftz(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float max_nan(float a, float b) { float r; asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r; }
+
+template <typename scalar_t>
+__device__ __noinline__ void flush_pending(WarpTile& w, int lane, const AdamwHyper& h, const StepConsts& c) {
+    __syncwarp();
+    const uint32_t n = w.n_pend < (uint32_t)kPendCap ? w.n_pend : (uint32_t)kPendCap;
+    for (uint32_t i = lane; i < n; i += 32) {
+        const unsigned long long d = w.pe_dst[i];
+        const bool second = d >> 63;
+        const float gj = w.pe_g[i];
+        const float addend = second ? __fmul_rn(__fmul_rn(c.om_beta2, gj), gj) : __fmul_rn(c.om_beta1, gj);
+        const float val = exact_moment(w.pe_x[i], w.pe_ik[i], w.pe_r[i], second ? h.beta2 : h.beta1, addend, second);
+        const uint32_t code = exact_code(val, w.pe_nr[i], w.pe_nk[i], w.pe_ns[i], second);
+        *reinterpret_cast<uint8_t*>(d & 0x7fffffffffffffffull) = (uint8_t)code;
+    }
+    __syncwarp();
+    if (lane == 0) w.n_pend = 0;
+    __syncwarp();
+}
+
+// Rare path of phase 3: the two ends of an element's interval round to different codes.  Queue the
+// exact recomputation of those bytes (the old codes are still in place: the calling lane overwrites
+// its word right after this returns).  If the list is full the element is recomputed on the spot and
+// patched into the word the lane is about to store.
+template <typename scalar_t>
+__device__ __noinline__ void queue_exact(WarpTile& w, int slot, int lane, uint32_t dm, uint32_t dv, uint32_t& cm,
+                                         uint32_t& cv, const AdamwHyper& h, const StepConsts& c,
+                                         unsigned long long& n_pend_total) {
+    typedef Elem4<scalar_t> E;
+    uint8_t* code_m = reinterpret_cast<uint8_t*>(w.ptr_m[slot]);
+    uint8_t* code_v = reinterpret_cast<uint8_t*>(w.ptr_v[slot]);
+    const uint32_t old_m = w.cw_m[slot][lane], old_v = w.cw_v[slot][lane];
+#pragma unroll 1
+    for (int b = 0; b < 8; ++b) {
+        const int j = b & 3;
+        const bool second = b >> 2;
+        if (!(((second ? dv : dm) >> (8 * j)) & 0xffu)) continue;
+        const float* sc = w.old_sc[slot] + (second ? 4 : 0);
+        const float* o = w.newc[slot][second];
+        const float x = coat_e4m3_to_float((uint8_t)((second ? old_v : old_m) >> (8 * j))) * sc[0];
+        const float gj = E::get(reinterpret_cast<const scalar_t*>(w.ptr_g[slot]) + lane * 4 + j);
+        uint8_t* dst = (second ? code_v : code_m) + lane * 4 + j;
+        const uint32_t pos = atomicAdd(&w.n_pend, 1u);
+        ++n_pend_total;
+        if (pos < (uint32_t)kPendCap) {
+            w.pe_x[pos] = x; w.pe_ik[pos] = sc[1]; w.pe_r[pos] = sc[2]; w.pe_g[pos] = gj;
+            w.pe_nr[pos] = o[0]; w.pe_nk[pos] = o[1]; w.pe_ns[pos] = o[2];
+            w.pe_dst[pos] = (unsigned long long)dst | (second ? (1ull << 63) : 0ull);
+        } else {
+            const float addend = second ? __fmul_rn(__fmul_rn(c.om_beta2, gj), gj) : __fmul_rn(c.om_beta1, gj);
+            const float val = exact_moment(x, sc[1], sc[2], second ? h.beta2 : h.beta1, addend, second);
+            const uint32_t code = exact_code(val, o[0], o[1], o[2], second);
+            if (second) cv = (cv & ~(0xffu << (8 * j))) | (code << (8 * j));
+            else cm = (cm & ~(0xffu << (8 * j))) | (code << (8 * j));
+        }
+    }
+}
+
+template <typename scalar_t, bool MULTI>
+__global__ void __launch_bounds__(kTiledThreads)
+fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
+                              const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
+                              AdamwHyper h, unsigned long long* dbg) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    WarpTile& w = reinterpret_cast<WarpTile*>(smem_raw)[warp];
+    float* smem_min = reinterpret_cast<float*>(smem_raw + kTiledWarps * sizeof(WarpTile)) + warp * kGroup;
+    typedef Elem4<scalar_t> E;
+
+    StepConsts c;
+    c.om_beta1 = 1 - h.beta1;
+    c.om_beta2 = 1 - h.beta2;
+    c.correction1 = 1.0f - powf(h.beta1, h.step);
+    c.correction2_sqrt = sqrtf(1.0f - powf(h.beta2, h.step));
+    c.p_a = c.correction1 / c.correction2_sqrt;
+    c.p_b = h.eps * c.correction1;
+    const float kInf = __int_as_float(0x7f800000);
+
+    const int64_t n_tiles = (total_groups + kTile - 1) / kTile;
+    const int64_t warps_total = (int64_t)gridDim.x * kTiledWarps;
+    unsigned long long n_fast = 0, n_exact = 0, n_cand_total = 0, n_pend_total = 0;
+    if (lane == 0) {
+        w.n_pend = 0;
+        w.n_cand = 0;
+        mbar_init(&w.mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    uint32_t mbar_parity = 0;
+#ifdef COAT_ADAMW_PROFILE
+    long long phase_cycles[6] = {0, 0, 0, 0, 0, 0};
+    long long phase_t = clock64();
+#endif
+
+    for (int64_t tile = (int64_t)blockIdx.x * kTiledWarps + warp; tile < n_tiles; tile += warps_total) {
+        const int64_t g0 = tile * kTile;
+        const int n_slots = (int)((total_groups - g0) < kTile ? (total_groups - g0) : kTile);
+
+        // ================= phase 0: one lane per group =================
+        // 0a: where the group lives
+        if (lane < n_slots) {
+            const int64_t gi = g0 + lane;
+            int ti = 0;
+            int64_t group = gi;
+            if (MULTI) {
+                int lo = 0, hi = n_tensors - 1;
+                while (lo < hi) {
+                    int mid = (lo + hi + 1) >> 1;
+                    if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                }
+                ti = lo;
+                group = gi - group_prefix[ti];
+            }
+            const TensorDesc& t = MULTI ? table[ti] : single;
+            const int64_t e0 = group * kGroup;
+            w.ptr_p[lane] = (unsigned long long)(reinterpret_cast<scalar_t*>(t.p) + e0);
+            w.ptr_g[lane] = (unsigned long long)(reinterpret_cast<const scalar_t*>(t.g) + e0);
+            w.ptr_m[lane] = (unsigned long long)(t.m + e0);
+            w.ptr_v[lane] = (unsigned long long)(t.v + e0);
+            w.ptr_bf[lane] = t.bf16_out ? (unsigned long long)(reinterpret_cast<__nv_bfloat16*>(t.bf16_out) + e0) : 0ull;
+            w.local[lane] = group;
+            w.ti[lane] = ti;
+            w.flags[lane] = (desc_vec_ok(t, E::kVecAlign) && (t.numel - e0 >= kGroup)) ? 2u : 0u;
+            w.stat[lane][0] = 0u; w.stat[lane][1] = 0x7f800000u; w.stat[lane][2] = 0u; w.stat[lane][3] = 0x7f800000u;
+        }
+        if (lane == 0) w.n_cand = 0;
+        fence_proxy_async();   // this lane's generic accesses to the staging buffers precede the next bulk write
+        __syncwarp();
+        // stage the tile's inputs: one bulk copy per array when the tile is one contiguous, aligned run
+        bool all_mem_ok = true;
+        for (int sl = 0; sl < n_slots; ++sl) all_mem_ok = all_mem_ok && (w.flags[sl] & 2u);
+        const bool bulk = all_mem_ok && w.ti[0] == w.ti[n_slots - 1];
+        if (bulk) {
+            if (lane == 0) {
+                const uint32_t n = (uint32_t)n_slots;
+                mbar_expect_tx(&w.mbar, n * (2u * kGroup * (uint32_t)sizeof(scalar_t) + 2u * kGroup));
+                bulk_g2s(&w.m1[0][0], reinterpret_cast<const void*>(w.ptr_p[0]), n * kGroup * (uint32_t)sizeof(scalar_t), &w.mbar);
+                bulk_g2s(&w.v1[0][0], reinterpret_cast<const void*>(w.ptr_g[0]), n * kGroup * (uint32_t)sizeof(scalar_t), &w.mbar);
+                bulk_g2s(&w.cw_m[0][0], reinterpret_cast<const void*>(w.ptr_m[0]), n * kGroup, &w.mbar);
+                bulk_g2s(&w.cw_v[0][0], reinterpret_cast<const void*>(w.ptr_v[0]), n * kGroup, &w.mbar);
+            }
+        } else {
+            for (int sl = 0; sl < n_slots; ++sl) {
+                if (!(w.flags[sl] & 2u)) continue;
+                w.m1[sl][lane] = reinterpret_cast<const float4*>(w.ptr_p[sl])[lane];
+                w.v1[sl][lane] = reinterpret_cast<const float4*>(w.ptr_g[sl])[lane];
+                w.cw_m[sl][lane] = reinterpret_cast<const uint32_t*>(w.ptr_m[sl])[lane];
+                w.cw_v[sl][lane] = reinterpret_cast<const uint32_t*>(w.ptr_v[sl])[lane];
+            }
+        }
+        // 0b: the stored scalars of each group, 1/k, error bounds, range checks (overlaps the copies)
+        if (lane < n_slots) {
+            const TensorDesc& t = MULTI ? table[w.ti[lane]] : single;
+            const int64_t group = w.local[lane];
+            const float s_m = t.s_m[group], r_m = t.r_m[group], s_v = t.s_v[group], r_v = t.r_v[group];
+            const float ik_m = __fdiv_rn(1.0f, t.k_m[group]), ik_v = __fdiv_rn(1.0f, t.k_v[group]);
+            float tb_m, tb_v;
+            const float eps_dm = fast_dequant_eps(ik_m, fast_lg2(s_m), tb_m);
+            const float eps_dv = fast_dequant_eps(ik_v, fast_lg2(s_v), tb_v);
+            const bool ok = sane_pos(s_m) && sane_pos(r_m) && sane_pos(s_v) && sane_pos(r_v) && ik_m >= 0.015625f &&
+                            ik_m <= 64.0f && ik_v >= 0.015625f && ik_v <= 64.0f && tb_m <= 60.0f && tb_v <= 60.0f;
+            float* sc = w.old_sc[lane];
+            sc[0] = s_m; sc[1] = ik_m; sc[2] = r_m; sc[3] = eps_dm; sc[4] = s_v; sc[5] = ik_v; sc[6] = r_v; sc[7] = eps_dv;
+            if (ok) w.flags[lane] |= 1u;
+        }
+        __syncwarp();
+        if (bulk) {
+            if (!mbar_wait(&w.mbar, mbar_parity)) {   // bounded; never expected
+                g_adamw_device_status = COAT_E_TIMEOUT;
+                return;
+            }
+            mbar_parity ^= 1u;
+        }
+        PHASE_CLOCK(0);
+
+        // ================= phase 1: lanes over the elements of one group =================
+        uint32_t live = 0;   // slots that stay on the fast path (warp-uniform)
+#pragma unroll 1
+        for (int slot = 0; slot < n_slots; ++slot) {
+            bool ok = (w.flags[slot] & 3u) == 3u;
+            if (ok) {
+                scalar_t* pp = reinterpret_cast<scalar_t*>(w.ptr_p[slot]) + lane * 4;
+                const float4 p4 = w.m1[slot][lane], g4 = w.v1[slot][lane];
+                float p[4] = {p4.x, p4.y, p4.z, p4.w};
+                const float g[4] = {g4.x, g4.y, g4.z, g4.w};
+                const uint32_t mw = w.cw_m[slot][lane], vw = w.cw_v[slot][lane];
+                float xm[4], xv[4], m1[4], v1[4];
+                const float4 sa = reinterpret_cast<const float4*>(w.old_sc[slot])[0];   // s_m, 1/k_m, r_m, eps_dm
+                const float4 sb = reinterpret_cast<const float4*>(w.old_sc[slot])[1];   // s_v, 1/k_v, r_v, eps_dv
+                e4m3x4_magnitudes(mw, xm);
+                e4m3x4_magnitudes(vw, xv);
+                // a NaN code, or a negative second-moment code, sends the group to the exact path (via the NaN
+                // that max_nan carries into the group maximum)
+                float mx_a = (has_nan_code(mw) | has_nan_code(vw) | (vw & 0x80808080u)) ? __int_as_float(0x7fffffff) : 0.f;
+                float mn_a = kInf, mx_am = 0.f, mx_v = 0.f, mn_v = kInf;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float xmj = xm[j] * sa.x, xvj = xv[j] * sb.x;   // magnitudes; the sign is applied below
+                    const float mt = __uint_as_float(__float_as_uint(ex2_ftz(lg2_ftz(xmj) * sa.y) * sa.z) |
+                                                     ((mw << (24 - 8 * j)) & 0x80000000u));
+                    const float vt = ex2_ftz(lg2_ftz(xvj) * sb.y) * sb.z;
+                    m1[j] = adam_first(h.beta1, mt, c.om_beta1, g[j]);
+                    v1[j] = adam_second(h.beta2, vt, c.om_beta2, g[j]);
+                    const float a1 = fabsf(m1[j]);
+                    mx_a = max_nan(mx_a, a1);   // a NaN anywhere must surface in the maxima
+                    mn_a = fminf(mn_a, a1);
+                    mx_am = fmaxf(mx_am, fabsf(h.beta1 * mt));
+                    mx_v = max_nan(mx_v, v1[j]);
+                    mn_v = fminf(mn_v, v1[j]);
+                }
+                // all five are non-negative (or NaN, which orders above everything): unsigned order == float order
+                const float MA = __uint_as_float(redux_max_f(mx_a)), mA = __uint_as_float(redux_min_f(mn_a));
+                const float MAM = __uint_as_float(redux_max_f(mx_am));
+                const float MV = __uint_as_float(redux_max_f(mx_v)), mV = __uint_as_float(redux_min_f(mn_v));
+                // error bounds of the approximate moments.  First moment (the two terms may cancel), absolute
+                // and uniform over the group: |m~' - m'| <= eps_dm*max|beta1*m~| + 2^-22*max|m'| = d_m.
+                // Second moment (both terms >= 0), relative per element: |v~' - v'| <= (eps_dv + 2^-22) * v'.
+                const float d_m = __fmaf_rn(sa.w, MAM, k2m22 * MA);
+                const float e_v = sb.w + k2m22;
+                // no possible exact zero / sign change / NaN / denormal, and nothing overflowed
+                ok = (mA - d_m > kTiny) && (mV > kTiny) && (MA <= kSaneHi) && (MV <= kSaneHi);
+                uint32_t cand = 0;
+                if (ok) {
+                    const float hi_m = MA - 2.0f * d_m, lo_m = mA + 2.0f * d_m;
+                    const float hi_v = MV * (1.0f - 2.5f * e_v), lo_v = mV * (1.0f + 2.5f * e_v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float a1 = fabsf(m1[j]);
+                        if (a1 >= hi_m || a1 <= lo_m) cand |= 1u << j;
+                        if (v1[j] >= hi_v || v1[j] <= lo_v) cand |= 16u << j;
+                    }
+                    ok = __reduce_add_sync(COAT_FULL_MASK, __popc(cand)) <= kCandPerGroup;
+                }
+                if (ok) {
+                    // weights from the approximate moments (they are not quantised)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float denom = __fmaf_rn(sqrt_ftz(v1[j]), c.p_a, c.p_b);
+                        const float update = __fmaf_rn(h.wd, p[j], m1[j] * rcp_ftz(denom));
+                        p[j] = __fmaf_rn(-h.lr, update, p[j]);
+                    }
+                    E::store(pp, p);
+                    if (w.ptr_bf[slot]) {
+                        float q[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) q[j] = E::round(p[j]);
+                        Elem4<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q);
+                    }
+                    w.m1[slot][lane] = make_float4(m1[0], m1[1], m1[2], m1[3]);
+                    w.v1[slot][lane] = make_float4(v1[0], v1[1], v1[2], v1[3]);
+                    if (lane == 0) w.delta[slot][0] = d_m;
+                    if (cand) {
+                        uint32_t pos = atomicAdd(&w.n_cand, (uint32_t)__popc(cand));
+                        while (cand) {
+                            const int b = __ffs(cand) - 1;
+                            cand &= cand - 1;
+                            w.cand[pos++] = (uint16_t)((slot << 8) | ((lane * 4 + (b & 3)) << 1) | (b >> 2));
+                        }
+                    }
+                    live |= 1u << slot;
+                }
+            }
+            if (!ok) {
+                const TensorDesc& t = MULTI ? table[w.ti[slot]] : single;
+                process_group_exact<scalar_t, true>(t, w.local[slot], lane, h, c.om_beta1, c.om_beta2, c.correction1,
+                                                    c.correction2_sqrt, desc_vec_ok(t, E::kVecAlign), smem_min);
+                ++n_exact;
+            }
+        }
+        __syncwarp();
+        PHASE_CLOCK(1);
+        if (live == 0) continue;
+        n_fast += __popc(live);
+
+        // ================= phase 2a: exact moments of the max/min candidates =================
+        {
+            const uint32_t n = w.n_cand;
+            n_cand_total += n;
+            for (uint32_t i = lane; i < n; i += 32) {
+                const uint32_t e = w.cand[i];
+                const int slot = e >> 8, elem = (e >> 1) & 127;
+                const bool second = e & 1;
+                const float* sc = w.old_sc[slot] + (second ? 4 : 0);
+                const uint8_t code = reinterpret_cast<const uint8_t*>(second ? w.cw_v[slot] : w.cw_m[slot])[elem];
+                const float gj = E::get(reinterpret_cast<const scalar_t*>(w.ptr_g[slot]) + elem);
+                const float addend = second ? __fmul_rn(__fmul_rn(c.om_beta2, gj), gj) : __fmul_rn(c.om_beta1, gj);
+                const float val = fabsf(exact_moment(coat_e4m3_to_float(code) * sc[0], sc[1], sc[2],
+                                                     second ? h.beta2 : h.beta1, addend, second));
+                if (dbg) {   // how much of the modelled error bound the approximation actually used
+                    const float approx = fabsf(reinterpret_cast<const float*>(second ? w.v1[slot] : w.m1[slot])[elem]);
+                    const float bound = second ? (sc[3] + k2m22) * val : w.delta[slot][0];
+                    atomicMax(reinterpret_cast<unsigned int*>(dbg + (second ? 7 : 6)),
+                              __float_as_uint(fabsf(approx - val) / bound));
+                }
+                atomicMax(&w.stat[slot][second ? 2 : 0], __float_as_uint(val));
+                atomicMin(&w.stat[slot][second ? 3 : 1], __float_as_uint(val));
+            }
+        }
+        __syncwarp();
+        PHASE_CLOCK(2);
+
+        // ================= phase 2b: exact group scalars, one lane per (group, moment) =================
+        if (lane < 2 * kTile && ((live >> (lane >> 1)) & 1)) {
+            const int slot = lane >> 1;
+            const bool second = lane & 1;
+            const float amax = __uint_as_float(w.stat[slot][second ? 2 : 0]);
+            const float amin = fminf(__uint_as_float(w.stat[slot][second ? 3 : 1]), 1e9f);
+            float maxv, sq, ex, ns;
+            expand_group_scalars(amax, amin, h.expand_min, maxv, sq, ex, ns);
+            const TensorDesc& t = MULTI ? table[w.ti[slot]] : single;
+            const int64_t group = w.local[slot];
+            if (second) { t.s_v[group] = ns; t.k_v[group] = ex; t.r_v[group] = sq; }
+            else { t.s_m[group] = ns; t.k_m[group] = ex; t.r_m[group] = sq; }
+            // |lg2(m'/r')| <= lg2(max/min)/2 (+ slack); the exponent handed to ex2 is k' times that
+            const float lw = fmaxf(1.0f, fabsf(fast_lg2(__fdiv_rn(maxv, sq))) + 1e-2f);
+            const float e_q = kSafety * (ex * k2m23 + kLn2 * ex * lw * (kLgErr + k2m24) + kEx2Err + kPowDev + k2m22) +
+                              ex * k2m22;
+            const float inv_s = __fdiv_rn(1.0f, ns);
+            // relative error of the input: first moment delta/|m'| per element (D * 1/|m'| below);
+            // second moment at most eps_dv + 2^-22 for every element
+            const float rel_v = second ? 1.02f * ex * (w.old_sc[slot][7] + k2m22) : 0.f;
+            const bool in_range = sane_pos(sq) && ex >= 0.015625f && ex <= 32.0f && ns >= 9.5367432e-07f &&
+                                  ns <= 1048576.0f;
+            float* o = w.newc[slot][second];
+            o[0] = sq; o[1] = ex; o[2] = ns; o[3] = __fdiv_rn(1.0f, sq);
+            o[4] = inv_s * (1.0f - e_q - rel_v); o[5] = inv_s * (1.0f + e_q + rel_v);
+            o[6] = 1.02f * ex * inv_s * w.delta[slot][0];
+            o[7] = in_range ? 1.0f : 0.0f;
+        }
+        __syncwarp();
+        PHASE_CLOCK(3);
+
+        // ================= phase 3: requantise; both ends of each interval must agree =================
+#pragma unroll 1
+        for (int slot = 0; slot < n_slots; ++slot) {
+            if (!((live >> slot) & 1)) continue;
+            const float4 qa_m = reinterpret_cast<const float4*>(w.newc[slot][0])[0];
+            const float4 qb_m = reinterpret_cast<const float4*>(w.newc[slot][0])[1];
+            const float4 qa_v = reinterpret_cast<const float4*>(w.newc[slot][1])[0];
+            const float4 qb_v = reinterpret_cast<const float4*>(w.newc[slot][1])[1];
+            const float4 m4 = w.m1[slot][lane], v4 = w.v1[slot][lane];
+            const float m1[4] = {m4.x, m4.y, m4.z, m4.w}, v1[4] = {v4.x, v4.y, v4.z, v4.w};
+            float ql[4], qh[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a1 = fabsf(m1[j]);
+                const float e = ex2_ftz(qa_m.y * lg2_ftz(a1 * qa_m.w));
+                // 2^-floor(log2 a1) >= 1/a1, from the exponent field alone (a1 is a normal number here)
+                const float ia = __uint_as_float(0x7f000000u - (__float_as_uint(a1) & 0x7f800000u));
+                ql[j] = e * __fmaf_rn(-qb_m.z, ia, qb_m.x);
+                qh[j] = e * __fmaf_rn(qb_m.z, ia, qb_m.y);
+            }
+            uint32_t cm = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
+            uint32_t dm = cm ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float e = ex2_ftz(qa_v.y * lg2_ftz(v1[j] * qa_v.w));
+                ql[j] = e * qb_v.x;
+                qh[j] = e * qb_v.y;
+            }
+            uint32_t cv = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
+            uint32_t dv = cv ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
+            // sign of the first moment (certain: every interval excludes zero)
+            cm |= ((__float_as_uint(m1[0]) >> 31) << 7) | ((__float_as_uint(m1[1]) >> 31) << 15) |
+                  ((__float_as_uint(m1[2]) >> 31) << 23) | ((__float_as_uint(m1[3]) >> 31) << 31);
+            if (qb_m.w == 0.0f) dm = 0xffffffffu;   // new scalars outside the modelled range: recompute all
+            if (qb_v.w == 0.0f) dv = 0xffffffffu;
+            uint8_t* code_m = reinterpret_cast<uint8_t*>(w.ptr_m[slot]);
+            uint8_t* code_v = reinterpret_cast<uint8_t*>(w.ptr_v[slot]);
+            if (dm | dv) queue_exact<scalar_t>(w, slot, lane, dm, dv, cm, cv, h, c, n_pend_total);
+            reinterpret_cast<uint32_t*>(code_m)[lane] = cm;
+            reinterpret_cast<uint32_t*>(code_v)[lane] = cv;
+            __syncwarp();
+            if (w.n_pend >= 32u) { PHASE_CLOCK(4); flush_pending<scalar_t>(w, lane, h, c); PHASE_CLOCK(5); }
+        }
+        PHASE_CLOCK(4);
+    }
+    flush_pending<scalar_t>(w, lane, h, c);
+#ifdef COAT_ADAMW_PROFILE
+    if (dbg && lane == 0)
+        for (int i = 0; i < 6; ++i) atomicAdd(dbg + 8 + i, (unsigned long long)phase_cycles[i]);
+#endif
+    if (dbg) {
+        n_pend_total = __reduce_add_sync(COAT_FULL_MASK, (unsigned)n_pend_total);
+        if (lane == 0) {
+            atomicAdd(dbg + 0, n_fast);
+            atomicAdd(dbg + 1, n_exact);
+            atomicAdd(dbg + 2, n_cand_total);
+            atomicAdd(dbg + 3, n_pend_total);
+        }
+    }
+}
+
 template <typename scalar_t, bool EXPAND, bool MULTI>
 __global__ void __launch_bounds__(kThreads)
 fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
                  const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
-                 AdamwHyper h) {
+                 AdamwHyper h, unsigned long long* dbg) {
     __shared__ float smem_min[kWarpsPerCta][kGroup];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     // hoisted per-launch scalars, evaluated on the device with the same routines as
     // the reference (fp8_adamw_expand_cuda_kernel.cu:52-58)
-    const float om_beta1 = 1 - h.beta1;
-    const float om_beta2 = 1 - h.beta2;
-    const float correction1 = 1.0f - powf(h.beta1, h.step);
-    const float correction2_sqrt = sqrtf(1.0f - powf(h.beta2, h.step));
+    StepConsts c;
+    c.om_beta1 = 1 - h.beta1;
+    c.om_beta2 = 1 - h.beta2;
+    c.correction1 = 1.0f - powf(h.beta1, h.step);
+    c.correction2_sqrt = sqrtf(1.0f - powf(h.beta2, h.step));
+    c.p_a = c.correction1 / c.correction2_sqrt;
+    c.p_b = h.eps * c.correction1;
 
     const int64_t warps_total = (int64_t)gridDim.x * kWarpsPerCta;
     int64_t gi = (int64_t)blockIdx.x * kWarpsPerCta + warp;
     if (!MULTI) {
         const bool vec_ok = desc_vec_ok(single, Elem4<scalar_t>::kVecAlign);
-        for (; gi < total_groups; gi += warps_total)
-            process_group_exact<scalar_t, EXPAND>(single, gi, lane, h, om_beta1, om_beta2, correction1,
-                                                  correction2_sqrt, vec_ok, smem_min[warp]);
+        for (; gi < total_groups; gi += warps_total) {
+            process_group_exact<scalar_t, EXPAND>(single, gi, lane, h, c.om_beta1, c.om_beta2, c.correction1,
+                                                  c.correction2_sqrt, vec_ok, smem_min[warp]);
+            if (dbg && lane == 0) atomicAdd(dbg + 1, 1ull);
+        }
     } else {
         int ti = 0;
         for (; gi < total_groups; gi += warps_total) {
@@ -384,11 +981,15 @@ fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
             }
             TensorDesc t = table[ti];
             const bool vec_ok = desc_vec_ok(t, Elem4<scalar_t>::kVecAlign);
-            process_group_exact<scalar_t, EXPAND>(t, gi - group_prefix[ti], lane, h, om_beta1, om_beta2,
-                                                  correction1, correction2_sqrt, vec_ok, smem_min[warp]);
+            const int64_t local = gi - group_prefix[ti];
+            process_group_exact<scalar_t, EXPAND>(t, local, lane, h, c.om_beta1, c.om_beta2, c.correction1,
+                                                  c.correction2_sqrt, vec_ok, smem_min[warp]);
+            if (dbg && lane == 0) atomicAdd(dbg + 1, 1ull);
         }
     }
 }
+
+unsigned long long* g_debug_counters = nullptr;
 
 int grid_for(int64_t total_groups) {
     int sms = coat_sm_count();
@@ -397,28 +998,49 @@ int grid_for(int64_t total_groups) {
     return (int)(ctas_needed < cap ? (ctas_needed > 0 ? ctas_needed : 1) : cap);
 }
 
+constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(float));
+constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmem + 1024));
+static_assert(kTiledCtasPerSm * (kTiledSmem + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
+
+template <typename scalar_t, bool EXPAND, bool MULTI>
+int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_t* prefix, int n_tensors,
+                 int64_t total_groups, const AdamwHyper& h, int flags, cudaStream_t st) {
+    // The tiled guarded kernel serves fp32 (master) weights, the case the optimizer class supports; other
+    // weight types and the COAT_ADAMW_EXACT_POW flag take the one-group-per-warp exact kernel.
+    if constexpr (EXPAND && std::is_same<scalar_t, float>::value) {
+        if (!(flags & COAT_ADAMW_EXACT_POW)) {
+            auto kern = fp8_adamw_expand_tiled_kernel<scalar_t, MULTI>;
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTiledSmem) != cudaSuccess)
+                return COAT_E_LAUNCH;
+            const int64_t tiles = (total_groups + kTile - 1) / kTile;
+            const int64_t ctas_needed = (tiles + kTiledWarps - 1) / kTiledWarps;
+            const int64_t cap = (int64_t)coat_sm_count() * kTiledCtasPerSm;
+            const int grid = (int)(ctas_needed < cap ? ctas_needed : cap);
+            kern<<<grid, kTiledThreads, kTiledSmem, st>>>(single, table, prefix, n_tensors, total_groups, h,
+                                                          g_debug_counters);
+            return coat_launch_status();
+        }
+    }
+    fp8_adamw_kernel<scalar_t, EXPAND, MULTI><<<grid_for(total_groups), kThreads, 0, st>>>(
+        single, table, prefix, n_tensors, total_groups, h, g_debug_counters);
+    return coat_launch_status();
+}
+
 template <bool EXPAND, bool MULTI>
 int launch(int p_dtype, const TensorDesc& single, const TensorDesc* table, const int64_t* prefix,
-           int n_tensors, int64_t total_groups, const AdamwHyper& h, cudaStream_t st) {
+           int n_tensors, int64_t total_groups, const AdamwHyper& h, int flags, cudaStream_t st) {
     if (total_groups <= 0) return COAT_OK;
-    int grid = grid_for(total_groups);
     switch (p_dtype) {
         case COAT_F32:
-            fp8_adamw_kernel<float, EXPAND, MULTI><<<grid, kThreads, 0, st>>>(single, table, prefix, n_tensors,
-                                                                             total_groups, h);
-            break;
+            return launch_typed<float, EXPAND, MULTI>(single, table, prefix, n_tensors, total_groups, h, flags, st);
         case COAT_BF16:
-            fp8_adamw_kernel<__nv_bfloat16, EXPAND, MULTI><<<grid, kThreads, 0, st>>>(single, table, prefix,
-                                                                                     n_tensors, total_groups, h);
-            break;
+            return launch_typed<__nv_bfloat16, EXPAND, MULTI>(single, table, prefix, n_tensors, total_groups, h,
+                                                             flags, st);
         case COAT_F16:
-            fp8_adamw_kernel<__half, EXPAND, MULTI><<<grid, kThreads, 0, st>>>(single, table, prefix, n_tensors,
-                                                                              total_groups, h);
-            break;
+            return launch_typed<__half, EXPAND, MULTI>(single, table, prefix, n_tensors, total_groups, h, flags, st);
         default:
             return COAT_E_BADARG;
     }
-    return coat_launch_status();
 }
 
 }  // namespace
@@ -428,7 +1050,6 @@ extern "C" int coat_fp8_adamw_expand_step(void* p, const void* g, uint8_t* m, fl
                                           float beta1, float beta2, float lr, float wd, float eps, int step,
                                           int qgroup, int expand_min, int64_t numel, int p_dtype,
                                           void* bf16_out, int flags, void* stream) {
-    (void)flags;
     if (qgroup != kGroup) return COAT_E_QGROUP;
     if (numel < 0) return COAT_E_BADARG;
     if (numel == 0) return COAT_OK;
@@ -436,14 +1057,13 @@ extern "C" int coat_fp8_adamw_expand_step(void* p, const void* g, uint8_t* m, fl
     TensorDesc t = {p, g, m, v, s_m, k_m, r_m, s_v, k_v, r_v, bf16_out, numel};
     AdamwHyper h = {beta1, beta2, lr, wd, eps, step, expand_min};
     return launch<true, false>(p_dtype, t, nullptr, nullptr, 1, (numel + kGroup - 1) / kGroup, h,
-                               (cudaStream_t)stream);
+                               flags, (cudaStream_t)stream);
 }
 
 extern "C" int coat_fp8_adamw_step(void* p, const void* g, uint8_t* m, float* s_m, uint8_t* v, float* s_v,
                                    float beta1, float beta2, float lr, float wd, float eps, int step,
                                    int qgroup, int64_t numel, int p_dtype, void* bf16_out, int flags,
                                    void* stream) {
-    (void)flags;
     if (qgroup != kGroup) return COAT_E_QGROUP;
     if (numel < 0) return COAT_E_BADARG;
     if (numel == 0) return COAT_OK;
@@ -451,14 +1071,13 @@ extern "C" int coat_fp8_adamw_step(void* p, const void* g, uint8_t* m, float* s_
     TensorDesc t = {p, g, m, v, s_m, nullptr, nullptr, s_v, nullptr, nullptr, bf16_out, numel};
     AdamwHyper h = {beta1, beta2, lr, wd, eps, step, 0};
     return launch<false, false>(p_dtype, t, nullptr, nullptr, 1, (numel + kGroup - 1) / kGroup, h,
-                                (cudaStream_t)stream);
+                                flags, (cudaStream_t)stream);
 }
 
 extern "C" int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int64_t* group_prefix,
                                          int n_tensors, int64_t total_groups, int expand, float beta1,
                                          float beta2, float lr, float wd, float eps, int step, int qgroup,
                                          int expand_min, int p_dtype, int flags, void* stream) {
-    (void)flags;
     if (qgroup != kGroup) return COAT_E_QGROUP;
     if (n_tensors < 0 || total_groups < 0) return COAT_E_BADARG;
     if (n_tensors == 0 || total_groups == 0) return COAT_OK;
@@ -466,8 +1085,25 @@ extern "C" int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int
     TensorDesc none = {};
     AdamwHyper h = {beta1, beta2, lr, wd, eps, step, expand_min};
     if (expand)
-        return launch<true, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h,
+        return launch<true, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h, flags,
                                   (cudaStream_t)stream);
-    return launch<false, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h,
+    return launch<false, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h, flags,
                                (cudaStream_t)stream);
+}
+
+// Debug aid: six device counters (groups on the fast path, groups on the exact path, iterations of
+// the max/min-candidate loop, iterations of the uncertain-rounding loop, uncertain elements, spare)
+// that later launches add to; pass NULL to switch counting off.  Not thread safe.
+extern "C" int coat_fp8_adamw_debug_counters(unsigned long long* device_counters) {
+    g_debug_counters = device_counters;
+    return COAT_OK;
+}
+
+// Reads (and clears) the device-side status word of the optimizer kernels on the current device:
+// COAT_OK, or COAT_E_TIMEOUT if a bounded wait on a staging copy ever ran out.  Synchronises the device.
+extern "C" int coat_fp8_adamw_device_status(void) {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_adamw_device_status, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    if (v != 0 && cudaMemcpyToSymbol(g_adamw_device_status, &zero, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    return v;
 }

@@ -31,6 +31,7 @@ def fp8_adamw_expand_step(params, grads, exp_avg, scale_exp_avg, expand_exp_avg,
     if grads.dtype != params.dtype or grads.numel() != n:
         raise RuntimeError("grads must match params in dtype and size")
     P = _lib.dev_ptr
+    P(params, "params")  # raises for a CPU tensor before any device is selected
     with torch.cuda.device(params.device):
         rc = _lib.lib().coat_fp8_adamw_expand_step(
             P(params, "params"), P(grads, "grads"), P(exp_avg, "exp_avg"), P(scale_exp_avg),
@@ -53,6 +54,7 @@ def fp8_adamw_step(params, grads, exp_avg, scale_exp_avg, exp_avg_sq, scale_exp_
     if grads.dtype != params.dtype or grads.numel() != n:
         raise RuntimeError("grads must match params in dtype and size")
     P = _lib.dev_ptr
+    P(params, "params")  # raises for a CPU tensor before any device is selected
     with torch.cuda.device(params.device):
         rc = _lib.lib().coat_fp8_adamw_step(
             P(params, "params"), P(grads, "grads"), P(exp_avg, "exp_avg"), P(scale_exp_avg),

@@ -110,6 +110,18 @@ int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int64_t* group
                               int step, int qgroup, int expand_min, int p_dtype,
                               int flags, void* stream);
 
+/*
+ * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
+ * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded
+ *   fast path, groups on the exact path, exactly recomputed max/min candidates, exactly recomputed
+ *   roundings, -, -, and (as float bit patterns in the low 32 bits) the largest observed fraction of the
+ *   modelled error bound actually used by the first / second moment.  NULL switches counting off.
+ * coat_fp8_adamw_device_status: synchronises, returns and clears the device status word
+ *   (COAT_E_TIMEOUT if a bounded wait for a staging copy ever ran out).
+ */
+int coat_fp8_adamw_debug_counters(unsigned long long* device_counters);
+int coat_fp8_adamw_device_status(void);
+
 #ifdef __cplusplus
 }
 #endif
