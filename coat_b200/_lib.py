@@ -14,6 +14,11 @@ LIB_PATH = os.environ.get("COAT_B200_LIB", os.path.join(_HERE, "libcoat_b200.so"
 F32, BF16, F16 = 0, 1, 2
 E4M3, E5M2 = 0, 1
 ADAMW_EXACT_POW = 1
+QUANT_IEEE_DIV = 1
+
+# Default flags of the quantizer entry points: 0 = the reference's (Triton's) division, QUANT_IEEE_DIV
+# = IEEE division.  Tests that compare with the CPU checker switch it.
+quant_flags = 0
 
 _lib = None
 
@@ -26,6 +31,12 @@ SIGNATURES = {
     "coat_fp8_adamw_expand_step": [_vp] * 10 + [_f] * 5 + [_i, _i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_step": [_vp] * 6 + [_f] * 5 + [_i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_multi_step": [_vp, _vp, _i, _i64, _i] + [_f] * 5 + [_i, _i, _i, _i, _i, _vp],
+    "coat_fp8_quantize": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_group_scales_amax": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_division": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],
+    "coat_fp8_quantize_transpose": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_transpose": [_vp, _vp, _i64, _i64, _vp],
+    "coat_fp8_dequantize": [_vp, _vp, _vp, _i64, _i64, _i, _i, _i, _vp],
     "coat_fp8_adamw_debug_counters": [_vp],
     "coat_fp8_adamw_device_status": [],
 }
@@ -86,6 +97,25 @@ def param_dtype(t):
     if t.dtype == torch.float16:
         return F16
     raise RuntimeError(f"coat_b200: unsupported parameter dtype {t.dtype}")
+
+
+def float_dtype(t_or_dtype):
+    dt = t_or_dtype.dtype if isinstance(t_or_dtype, torch.Tensor) else t_or_dtype
+    if dt == torch.float32:
+        return F32
+    if dt == torch.bfloat16:
+        return BF16
+    if dt == torch.float16:
+        return F16
+    raise RuntimeError(f"coat_b200: unsupported floating dtype {dt}")
+
+
+def fp8_enum_of(t):
+    if t.dtype == torch.float8_e4m3fn:
+        return E4M3
+    if t.dtype == torch.float8_e5m2:
+        return E5M2
+    raise RuntimeError(f"coat_b200: expected an fp8 tensor, got {t.dtype}")
 
 
 _FP8_NAMES = {"E4M3": (E4M3, torch.float8_e4m3fn), "E5M2": (E5M2, torch.float8_e5m2)}

@@ -1,0 +1,210 @@
+"""Host side of the quantizers: same names, positional arguments and return tuples as the reference's
+python wrappers; each allocates its outputs with torch and makes one or two calls into the C ABI.
+
+Reference wrappers mirrored here:
+  fp8_quantize                      _quantize.py:120-163
+  fp8_quantize_pertensor            _quantize_pertensor.py:106-147
+  fp8_quantize_pertensor_transpose  _quantize_pertensor_transpose.py:106-150
+  fp8_division                      _division.py:153-207
+  fp8_division_transpose            _division_transpose.py:147-210
+  fp8_quantize_transpose            _quantize_transpose.py:176-226
+  fp8_transpose                     _transpose.py:85-115
+  fp8_dequantize                    _dequantize.py:119-156
+(paths under coat/activation/real_quantization/).
+"""
+import torch
+
+from ... import _lib
+from .common import FP8_MAX_VALUE, SCALE_MIN_THRES, convert_str_to_fp8
+
+
+def _flat2d(x):
+    """3-D inputs are treated as (B*S, H), as the reference does."""
+    if x.dim() == 3:
+        return x.reshape(-1, x.shape[-1]), x.shape[0]
+    if x.dim() != 2:
+        raise RuntimeError(f"expected a 2-D or 3-D tensor, got {x.dim()}-D")
+    return x, None
+
+
+def _fp8_dtype(fp8type):
+    if isinstance(fp8type, str):
+        return convert_str_to_fp8[fp8type]
+    return fp8type
+
+
+def _prep(x):
+    x, bs = _flat2d(x)
+    if not x.is_cuda:
+        raise RuntimeError("coat_b200: the quantizers need CUDA tensors (no CPU path exists)")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x, bs
+
+
+def _call(name, *args):
+    _lib.check(getattr(_lib.lib(), name)(*args), name)
+
+
+def _flags(flags):
+    return _lib.quant_flags if flags is None else flags
+
+
+def fp8_quantize(x, QB, fp8type, scale_dtype=torch.bfloat16, *, flags=None):
+    x, bs = _prep(x)
+    M, N = x.shape
+    fp8type = _fp8_dtype(fp8type)
+    y = torch.empty((M, N), dtype=fp8type, device=x.device)
+    s_y = torch.empty((M, N // QB), dtype=scale_dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_quantize", x.data_ptr(), y.data_ptr(), s_y.data_ptr(), M, N, x.stride(0), QB,
+              _lib.fp8_enum_of(y), _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags),
+              _lib.stream_ptr(x.device))
+    if bs is not None:
+        y = y.reshape(bs, -1, y.shape[-1])
+        s_y = s_y.reshape(bs, -1, s_y.shape[-1])
+    return y, s_y
+
+
+def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_transposed, flags):
+    """Pass 1 (tensor amax, optional group scales) + pass 2 (division by the one scale)."""
+    M, N = x.shape
+    fmt = _lib.fp8_format(fp8type)[0]
+    dev = x.device
+    amax = torch.empty(1, dtype=torch.int32, device=dev)   # 4-byte scratch word, zeroed by pass 1
+    s_y = torch.empty((M, N // QB), dtype=scale_dtype, device=dev) if want_scales else None
+    s_max = torch.empty((), dtype=scale_dtype, device=dev)
+    y = torch.empty((M, N), dtype=fp8type, device=dev) if want_straight else None
+    y_t = torch.empty((N, M), dtype=fp8type, device=dev) if want_transposed else None
+    P = lambda t: None if t is None else t.data_ptr()
+    with torch.cuda.device(dev):
+        st = _lib.stream_ptr(dev)
+        _call("coat_fp8_group_scales_amax", x.data_ptr(), P(s_y), amax.data_ptr(), M, N, x.stride(0), QB, fmt,
+              _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
+        _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), None, s_max.data_ptr(), amax.data_ptr(), M, N,
+              x.stride(0), fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
+    return y, s_max, s_y, y_t
+
+
+def fp8_quantize_pertensor(x, QB, fp8type, stochastic=False, scale_dtype=torch.bfloat16, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    x, bs = _prep(x)
+    fp8type = _fp8_dtype(fp8type)
+    y, s_max, s_y, _ = _pertensor(x, QB, fp8type, scale_dtype, True, True, False, flags)
+    if bs is not None:
+        y = y.reshape(bs, -1, y.shape[-1])
+        s_y = s_y.reshape(bs, -1, s_y.shape[-1])
+    return y, s_max, s_y
+
+
+def fp8_quantize_pertensor_transpose(x, QB, fp8type, transpose_output_2d=False, stochastic=False,
+                                     scale_dtype=torch.bfloat16, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    x, bs = _prep(x)
+    fp8type = _fp8_dtype(fp8type)
+    qy, s_max, _, qy_t = _pertensor(x, QB, fp8type, scale_dtype, False, True, True, flags)
+    if bs is not None:
+        qy = qy.reshape(bs, -1, qy.shape[-1])
+        if not transpose_output_2d:
+            qy_t = qy_t.reshape(bs, -1, qy_t.shape[-1])
+    return qy, s_max, qy_t
+
+
+def _default_scale(x, fp8type, flags):
+    """(x.abs().max() + 1e-10) / fp8_max in x's dtype, the reference's default when no scale is passed
+    (_division.py:178-179); the maximum comes from the amax kernel, the two scalar operations are torch's."""
+    M, N = x.shape
+    amax = torch.empty(1, dtype=torch.int32, device=x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_group_scales_amax", x.data_ptr(), None, amax.data_ptr(), M, N, x.stride(0), 16,
+              _lib.fp8_format(fp8type)[0], _lib.float_dtype(x), _lib.BF16, _flags(flags), _lib.stream_ptr(x.device))
+    return (amax.view(torch.float32)[0].to(x.dtype) + SCALE_MIN_THRES) / FP8_MAX_VALUE[fp8type]
+
+
+def _division(x, fp8type, s_y, want_straight, want_transposed, flags):
+    M, N = x.shape
+    if s_y is None:
+        s_y = _default_scale(x, fp8type, flags)
+    if not torch.is_tensor(s_y):
+        s_y = torch.tensor(float(s_y), dtype=torch.float32, device=x.device)
+    if not s_y.is_cuda:
+        s_y = s_y.to(x.device)
+    y = torch.empty((M, N), dtype=fp8type, device=x.device) if want_straight else None
+    y_t = torch.empty((N, M), dtype=fp8type, device=x.device) if want_transposed else None
+    P = lambda t: None if t is None else t.data_ptr()
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), s_y.data_ptr(), None, None, M, N, x.stride(0),
+              _lib.fp8_format(fp8type)[0], _lib.float_dtype(x), _lib.float_dtype(s_y), _flags(flags),
+              _lib.stream_ptr(x.device))
+    return y, s_y, y_t
+
+
+def fp8_division(x, QB, fp8type, s_y=None, stochastic=False, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    x, bs = _prep(x)
+    fp8type = _fp8_dtype(fp8type)
+    y, s_y, _ = _division(x, fp8type, s_y, True, False, flags)
+    if bs is not None:
+        y = y.reshape(bs, -1, y.shape[-1])
+    return y, s_y
+
+
+def fp8_division_transpose(x, QB, fp8type, s_y=None, stochastic=False, only_transposed=False, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    x, bs = _prep(x)
+    fp8type = _fp8_dtype(fp8type)
+    y, s_y, y_t = _division(x, fp8type, s_y, not only_transposed, True, flags)
+    if only_transposed:
+        return y_t, s_y
+    if bs is not None:
+        y = y.reshape(bs, -1, y.shape[-1])
+    return y, s_y, y_t   # y_t stays 2-D
+
+
+def fp8_quantize_transpose(x, QB, fp8type, scale_dtype=torch.bfloat16, *, flags=None):
+    x, _ = _prep(x)
+    M, N = x.shape
+    fp8type = _fp8_dtype(fp8type)
+    y = torch.empty((M, N), dtype=fp8type, device=x.device)
+    y_t = torch.empty((N, M), dtype=fp8type, device=x.device)
+    s_y = torch.empty((M, N // QB), dtype=scale_dtype, device=x.device)
+    s_y_t = torch.empty((N, M // QB), dtype=scale_dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_quantize_transpose", x.data_ptr(), y.data_ptr(), s_y.data_ptr(), y_t.data_ptr(),
+              s_y_t.data_ptr(), M, N, x.stride(0), QB, _lib.fp8_enum_of(y), _lib.float_dtype(x),
+              _lib.float_dtype(scale_dtype), _flags(flags), _lib.stream_ptr(x.device))
+    return (y, s_y), (y_t, s_y_t)
+
+
+def fp8_transpose(x, transpose_output_2d=False):
+    x, bs = _flat2d(x)
+    if not x.is_cuda:
+        raise RuntimeError("coat_b200: fp8_transpose needs a CUDA tensor")
+    x = x.contiguous()
+    M, N = x.shape
+    y = torch.empty((N, M), dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_transpose", x.data_ptr(), y.data_ptr(), M, N, _lib.stream_ptr(x.device))
+    if bs is not None and not transpose_output_2d:
+        y = y.reshape(bs, -1, y.shape[-1])
+    return y
+
+
+def fp8_dequantize(x, s_x, QB):
+    x, bs = _flat2d(x)
+    if not x.is_cuda:
+        raise RuntimeError("coat_b200: fp8_dequantize needs CUDA tensors")
+    x = x.contiguous()
+    s_x = s_x.reshape(-1, s_x.shape[-1]).contiguous()
+    M, N = x.shape
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_dequantize", x.data_ptr(), s_x.data_ptr(), y.data_ptr(), M, N, QB, _lib.fp8_enum_of(x),
+              _lib.float_dtype(s_x), _lib.stream_ptr(x.device))
+    if bs is not None:
+        y = y.reshape(bs, -1, y.shape[-1])
+    return y

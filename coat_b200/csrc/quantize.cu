@@ -1,0 +1,540 @@
+// Mixed-granularity FP8 quantizers for sm_100a: per-1xQB-group quantize, the two passes of the
+// per-tensor quantize (group scales / global amax, then division by one scale), the fused
+// quantize+transpose and division+transpose, byte transpose and dequantize.
+//
+// Arithmetic follows the reference's Triton kernels statement by statement
+//   coat/activation/real_quantization/_quantize.py:74-92            scale = (max|x| + 1e-10) / fp8_max ; q = x / scale
+//   coat/activation/real_quantization/_quantize_pertensor.py:80-92  same scale, stored only (pass 1)
+//   coat/activation/real_quantization/_division.py:84-114           q = x / s with one scalar s
+//   coat/activation/real_quantization/_quantize_transpose.py:84-145 row groups and column groups of one tile
+// including the two details that decide the bits: both divisions are the PTX instruction div.full.f32
+// (what Triton emits for an fp32 `/` and for tl.fdiv), and the scale is stored rounded to the scale
+// dtype AFTER the un-rounded fp32 scale has divided the values.  The float->FP8 cast is round to
+// nearest even, saturating (cvt.rn.satfinite), as Triton's.  COAT_QUANT_IEEE_DIV switches both
+// divisions to IEEE division, which a CPU can reproduce bit for bit (used by the parity tests).
+//
+// Layout / mapping: the straight kernels give every thread 16 consecutive elements of a row (two or
+// four 16-byte loads, one 16-byte store of codes), so a warp touches 1 KB of contiguous input; groups
+// wider than 16 are reduced with shuffles among the QB/16 neighbouring lanes.  The transposing kernels
+// give every thread a 4x4 block, a warp a 16(M) x 32(N) patch (lane = 8*mb + nb), so that a 1x16 row
+// group is 4 neighbouring lanes (xor 1, 2) and a 16x1 column group is the 4 lanes 8 apart (xor 8, 16);
+// the 4x4 byte blocks are transposed in registers and cross a padded shared tile once, so that both the
+// straight and the transposed codes leave in 128-byte rows.
+
+#include "common.cuh"
+
+namespace {
+
+constexpr float kScaleMinThres = 1e-10f;   // SCALE_MIN_THRES, coat/activation/real_quantization/common.py:20
+
+template <bool IEEE>
+__device__ __forceinline__ float qdiv(float a, float b) {
+    return IEEE ? __fdiv_rn(a, b) : coat_div_full(a, b);
+}
+
+// ---- typed 16-element row segments -------------------------------------------------------------
+template <typename T> struct Seg16;
+template <> struct Seg16<__nv_bfloat16> {
+    static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&x)[16]) {
+        const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[2 * i] = __uint_as_float(w[i] << 16);
+            x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+    static __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&x)[4]) {
+        const uint2 a = *reinterpret_cast<const uint2*>(p);
+        x[0] = __uint_as_float(a.x << 16); x[1] = __uint_as_float(a.x & 0xffff0000u);
+        x[2] = __uint_as_float(a.y << 16); x[3] = __uint_as_float(a.y & 0xffff0000u);
+    }
+    static __device__ __forceinline__ float get(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+};
+template <> struct Seg16<__half> {
+    static __device__ __forceinline__ void load(const __half* p, float (&x)[16]) {
+        const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            x[2 * i] = f.x; x[2 * i + 1] = f.y;
+        }
+    }
+    static __device__ __forceinline__ void load4(const __half* p, float (&x)[4]) {
+        const uint2 a = *reinterpret_cast<const uint2*>(p);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
+        const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
+        x[0] = f.x; x[1] = f.y; x[2] = g.x; x[3] = g.y;
+    }
+    static __device__ __forceinline__ float get(const __half* p) { return __half2float(*p); }
+};
+template <> struct Seg16<float> {
+    static __device__ __forceinline__ void load(const float* p, float (&x)[16]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 a = reinterpret_cast<const float4*>(p)[i];
+            x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
+        }
+    }
+    static __device__ __forceinline__ void load4(const float* p, float (&x)[4]) {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    }
+    static __device__ __forceinline__ float get(const float* p) { return *p; }
+};
+
+// scale stores / loads in the caller's scale dtype (COAT_F32 / COAT_BF16 / COAT_F16)
+__device__ __forceinline__ void store_scale(void* base, int64_t idx, int dtype, float s) {
+    if (dtype == COAT_F32) reinterpret_cast<float*>(base)[idx] = s;
+    else if (dtype == COAT_BF16) reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(s);
+    else reinterpret_cast<__half*>(base)[idx] = __float2half_rn(s);
+}
+__device__ __forceinline__ float load_scale(const void* base, int64_t idx, int dtype) {
+    if (dtype == COAT_F32) return reinterpret_cast<const float*>(base)[idx];
+    if (dtype == COAT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+    return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+}
+__device__ __forceinline__ float round_to_dtype(float s, int dtype) {
+    if (dtype == COAT_F32) return s;
+    if (dtype == COAT_BF16) return __bfloat162float(__float2bfloat16_rn(s));
+    return __half2float(__float2half_rn(s));
+}
+
+template <int FMT>
+__device__ __forceinline__ uint4 pack16(const float (&q)[16]) {
+    uint4 r;
+    r.x = coat_float4_to_fp8x4<FMT>(q[0], q[1], q[2], q[3]);
+    r.y = coat_float4_to_fp8x4<FMT>(q[4], q[5], q[6], q[7]);
+    r.z = coat_float4_to_fp8x4<FMT>(q[8], q[9], q[10], q[11]);
+    r.w = coat_float4_to_fp8x4<FMT>(q[12], q[13], q[14], q[15]);
+    return r;
+}
+
+// max over the `lanes` (power of two <= 8) neighbouring lanes that share a group
+__device__ __forceinline__ float subgroup_max(float v, int lanes) {
+    for (int o = 1; o < lanes; o <<= 1) v = fmaxf(v, __shfl_xor_sync(COAT_FULL_MASK, v, o));
+    return v;
+}
+
+constexpr int kStraightThreads = 256;
+
+// =================================================================================================
+// 1. per-1xQB-group quantize  (_quantize.py:37-118)  and pass 1 of the per-tensor quantize
+//    (_quantize_pertensor.py:46-103): group scales only, plus the tensor's amax for the fused pass 2
+// =================================================================================================
+// MODE 0: write codes + scales.  MODE 1: write scales (if s != null) and atomically max the tensor amax.
+template <typename T, int FMT, bool IEEE, int MODE>
+__global__ void __launch_bounds__(kStraightThreads)
+group_quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* __restrict__ s, int scale_dtype,
+                      unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int64_t ldx, int64_t ldy, int QB) {
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    const int lanes = QB >> 4;
+    const float fp8_max = CoatFp8Max<FMT>::value;
+    float block_max = 0.f;
+    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < ((total + 31) & ~31ll);
+         seg += (int64_t)gridDim.x * blockDim.x) {
+        const bool live = seg < total;
+        const int64_t row = live ? seg / segs_per_row : 0, c16 = live ? seg - row * segs_per_row : 0;
+        float v[16];
+        float amax = 0.f;
+        if (live) {
+            Seg16<T>::load(x + row * ldx + c16 * 16, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
+        amax = subgroup_max(amax, lanes);
+        if (!live) continue;
+        const float scale = qdiv<IEEE>(amax + kScaleMinThres, fp8_max);
+        if (MODE == 0) {
+            float q[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
+            *reinterpret_cast<uint4*>(y + row * ldy + c16 * 16) = pack16<FMT>(q);
+        } else {
+            block_max = fmaxf(block_max, amax);
+        }
+        if (s && (c16 & (lanes - 1)) == 0) store_scale(s, row * (N / QB) + c16 / lanes, scale_dtype, scale);
+    }
+    if (MODE == 1) {
+        block_max = coat_warp_max(block_max);
+        __shared__ float wmax[kStraightThreads / 32];
+        if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = block_max;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float m = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+            m = coat_warp_max(m);
+            // non-negative floats order like their bit patterns
+            if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+        }
+    }
+}
+
+// The one scale of a per-tensor quantize.  From the tensor amax it is what the reference obtains as the
+// maximum of its group scales: every group scale is round_to_scale_dtype((amax_g + 1e-10) / fp8_max),
+// rounding is monotone, so the maximum is the rounded scale of the largest group
+// (_quantize_pertensor.py:139: s_y.max()).
+template <int FMT, bool IEEE>
+__device__ __forceinline__ float tensor_scale_from_amax(const unsigned int* amax_bits, int scale_dtype) {
+    const float amax = __uint_as_float(*amax_bits);
+    return round_to_dtype(qdiv<IEEE>(amax + kScaleMinThres, CoatFp8Max<FMT>::value), scale_dtype);
+}
+
+// =================================================================================================
+// 2. division by one scale (_division.py:45-126): q = x / s
+// =================================================================================================
+// The scale is either a device scalar in `scale_dtype` (scale_from_amax == 0) or derived from the amax word
+// of pass 1, in which case block 0 also writes it to `s_out` (in `scale_dtype`).
+template <typename T, int FMT, bool IEEE>
+__global__ void __launch_bounds__(kStraightThreads)
+division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __restrict__ s_in, void* __restrict__ s_out,
+                int scale_dtype, const unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int64_t ldx,
+                int64_t ldy) {
+    const float scale = amax_bits ? tensor_scale_from_amax<FMT, IEEE>(amax_bits, scale_dtype)
+                                  : load_scale(s_in, 0, scale_dtype);
+    if (amax_bits && s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scale);
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < total;
+         seg += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
+        float v[16], q[16];
+        Seg16<T>::load(x + row * ldx + c16 * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
+        *reinterpret_cast<uint4*>(y + row * ldy + c16 * 16) = pack16<FMT>(q);
+    }
+}
+
+// =================================================================================================
+// 3. dequantize (_dequantize.py:44-116): y = bf16(code * group scale)
+// =================================================================================================
+template <int FMT>
+__global__ void __launch_bounds__(kStraightThreads)
+dequantize_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s, int scale_dtype,
+                  __nv_bfloat16* __restrict__ y, int64_t M, int64_t N, int QB) {
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < total;
+         seg += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
+        const float scale = load_scale(s, row * (N / QB) + (c16 * 16) / QB, scale_dtype);
+        const uint4 w = *reinterpret_cast<const uint4*>(x + row * N + c16 * 16);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float f[4];
+            coat_fp8x4_to_float4<FMT>(ww[i], f);
+            out[2 * i] = (uint32_t)coat_float_to_bf16_bits(f[0] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[1] * scale) << 16);
+            out[2 * i + 1] = (uint32_t)coat_float_to_bf16_bits(f[2] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[3] * scale) << 16);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(y + row * N + c16 * 16);
+        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+}
+
+// =================================================================================================
+// 4. transposing kernels: division+transpose (_division_transpose.py:48-144) and
+//    quantize+transpose (_quantize_transpose.py:39-173)
+// =================================================================================================
+// CTA tile: 128 rows (M) x 64 columns (N), 256 threads.  Thread = 4x4 block; warp = 16(M) x 32(N) patch with
+// lane = 8*mb + nb (nb: 4-column block 0..7, mb: 4-row block 0..3).  Warp w of the CTA takes the patch
+// (M block w, N half h) for h = 0, 1.
+constexpr int kTM = 128, kTN = 64;
+constexpr int kTileThreads = 256;
+constexpr int kLdT = kTM / 4 + 1;   // words per row of the transposed shared tile (+1: conflict-free scatter)
+
+// 4x4 byte transpose in registers: in[j] holds codes (j, 0..3), out[i] holds codes (0..3, i)
+__device__ __forceinline__ void transpose4x4(const uint32_t (&in)[4], uint32_t (&out)[4]) {
+    const uint32_t a = __byte_perm(in[0], in[1], 0x5140);   // r0c0 r1c0 r0c1 r1c1
+    const uint32_t b = __byte_perm(in[2], in[3], 0x5140);   // r2c0 r3c0 r2c1 r3c1
+    const uint32_t c = __byte_perm(in[0], in[1], 0x7362);   // r0c2 r1c2 r0c3 r1c3
+    const uint32_t d = __byte_perm(in[2], in[3], 0x7362);
+    out[0] = __byte_perm(a, b, 0x5410);   // r0c0 r1c0 r2c0 r3c0
+    out[1] = __byte_perm(a, b, 0x7632);
+    out[2] = __byte_perm(c, d, 0x5410);
+    out[3] = __byte_perm(c, d, 0x7632);
+}
+
+// GROUPS: true = 1x16 group scales along both directions (QB is fixed to 16 by the tile mapping);
+//         false = one scalar scale.  STRAIGHT: also write the un-transposed codes.
+template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT>
+__global__ void __launch_bounds__(kTileThreads)
+transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t* __restrict__ y_t,
+                       void* __restrict__ s_y, void* __restrict__ s_y_t, const void* __restrict__ s_in,
+                       void* __restrict__ s_out, int scale_dtype, const unsigned int* __restrict__ amax_bits,
+                       int M, int N, int64_t ldx) {
+    __shared__ uint32_t tile_t[kTN][kLdT];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = lane & 7, mb = lane >> 3;
+    const int m_tile = blockIdx.y * kTM, n_tile = blockIdx.x * kTN;
+    const float fp8_max = CoatFp8Max<FMT>::value;
+    float scalar = 1.f;
+    if (!GROUPS) {
+        scalar = amax_bits ? tensor_scale_from_amax<FMT, IEEE>(amax_bits, scale_dtype) : load_scale(s_in, 0, scale_dtype);
+        if (amax_bits && s_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+            store_scale(s_out, 0, scale_dtype, scalar);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int m_loc = warp * 16 + mb * 4, n_loc = h * 32 + nb * 4;   // inside the CTA tile
+        const int m0 = m_tile + m_loc, n0 = n_tile + n_loc;
+        float v[4][4];
+        const bool col_ok = n0 < N;   // N is a multiple of 16, so a 4-column block is in or out as a whole
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (col_ok && m0 + j < M) Seg16<T>::load4(x + (int64_t)(m0 + j) * ldx + n0, v[j]);
+            else { v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f; }
+        }
+        uint32_t straight[4], transposed[4];
+        if (GROUPS) {
+            // row groups: 16 consecutive columns = this lane and its neighbours nb^1, nb^2
+            float rs[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float a = fmaxf(fmaxf(fabsf(v[j][0]), fabsf(v[j][1])), fmaxf(fabsf(v[j][2]), fabsf(v[j][3])));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 1));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 2));
+                rs[j] = qdiv<IEEE>(a + kScaleMinThres, fp8_max);
+                straight[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], rs[j]), qdiv<IEEE>(v[j][1], rs[j]),
+                                                        qdiv<IEEE>(v[j][2], rs[j]), qdiv<IEEE>(v[j][3], rs[j]));
+            }
+            if ((nb & 3) == 0 && col_ok) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (m0 + j < M) store_scale(s_y, (int64_t)(m0 + j) * (N >> 4) + (n0 >> 4), scale_dtype, rs[j]);
+            }
+            // column groups: 16 consecutive rows = the lanes mb^1, mb^2 (lane xor 8, 16)
+            float cs[4];
+            uint32_t qt[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float a = fmaxf(fmaxf(fabsf(v[0][i]), fabsf(v[1][i])), fmaxf(fabsf(v[2][i]), fabsf(v[3][i])));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 8));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 16));
+                cs[i] = qdiv<IEEE>(a + kScaleMinThres, fp8_max);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                qt[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], cs[0]), qdiv<IEEE>(v[j][1], cs[1]),
+                                                  qdiv<IEEE>(v[j][2], cs[2]), qdiv<IEEE>(v[j][3], cs[3]));
+            transpose4x4(qt, transposed);
+            if (mb == 0 && col_ok && m0 < M) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    store_scale(s_y_t, (int64_t)(n0 + i) * (M >> 4) + (m0 >> 4), scale_dtype, cs[i]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                straight[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], scalar), qdiv<IEEE>(v[j][1], scalar),
+                                                        qdiv<IEEE>(v[j][2], scalar), qdiv<IEEE>(v[j][3], scalar));
+            transpose4x4(straight, transposed);
+        }
+        if (STRAIGHT && col_ok) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (m0 + j < M) *reinterpret_cast<uint32_t*>(y + (int64_t)(m0 + j) * N + n0) = straight[j];
+        }
+        // scatter into the transposed tile: row = column of x, word = 4-row block of x
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tile_t[n_loc + i][m_loc >> 2] = transposed[i];
+    }
+    __syncthreads();
+    // transposed rows leave as 128 contiguous bytes: one warp instruction = one row of the tile
+    for (int r = warp; r < kTN; r += kTileThreads / 32) {
+        const int n = n_tile + r, m = m_tile + lane * 4;
+        if (n < N && m < M) *reinterpret_cast<uint32_t*>(y_t + (int64_t)n * M + m) = tile_t[r][lane];
+    }
+}
+
+// =================================================================================================
+// 5. byte transpose (_transpose.py:39-82)
+// =================================================================================================
+__global__ void __launch_bounds__(kTileThreads)
+transpose_bytes_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y_t, int M, int N) {
+    __shared__ uint32_t tile_t[kTN][kLdT];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = lane & 7, mb = lane >> 3;
+    const int m_tile = blockIdx.y * kTM, n_tile = blockIdx.x * kTN;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int m_loc = warp * 16 + mb * 4, n_loc = h * 32 + nb * 4;
+        const int m0 = m_tile + m_loc, n0 = n_tile + n_loc;
+        uint32_t in[4], out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            in[j] = (n0 < N && m0 + j < M) ? *reinterpret_cast<const uint32_t*>(x + (int64_t)(m0 + j) * N + n0) : 0u;
+        transpose4x4(in, out);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tile_t[n_loc + i][m_loc >> 2] = out[i];
+    }
+    __syncthreads();
+    for (int r = warp; r < kTN; r += kTileThreads / 32) {
+        const int n = n_tile + r, m = m_tile + lane * 4;
+        if (n < N && m < M) *reinterpret_cast<uint32_t*>(y_t + (int64_t)n * M + m) = tile_t[r][lane];
+    }
+}
+
+// =================================================================================================
+// host side
+// =================================================================================================
+int straight_grid(int64_t segs) {
+    const int64_t blocks = (segs + kStraightThreads - 1) / kStraightThreads;
+    const int64_t cap = (int64_t)coat_sm_count() * 16;   // persistent beyond 16 CTAs of 256 threads per SM
+    return (int)(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+bool qb_ok(int QB) { return QB == 16 || QB == 32 || QB == 64 || QB == 128; }
+bool scale_dtype_ok(int d) { return d == COAT_F32 || d == COAT_BF16 || d == COAT_F16; }
+
+// Calls f.template run<T, FMT, IEEE>() for the runtime (in_dtype, fmt, flags) triple.
+template <typename F>
+int dispatch(int in_dtype, int fmt, int flags, F&& f) {
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+#define COAT_CASE(T)                                                                         \
+    if (fmt == COAT_E4M3) return ieee ? f.template run<T, COAT_E4M3, true>() : f.template run<T, COAT_E4M3, false>(); \
+    if (fmt == COAT_E5M2) return ieee ? f.template run<T, COAT_E5M2, true>() : f.template run<T, COAT_E5M2, false>(); \
+    return COAT_E_BADARG;
+    switch (in_dtype) {
+        case COAT_BF16: { COAT_CASE(__nv_bfloat16) }
+        case COAT_F16: { COAT_CASE(__half) }
+        case COAT_F32: { COAT_CASE(float) }
+        default: return COAT_E_BADARG;
+    }
+#undef COAT_CASE
+}
+
+int elem_size(int dtype) { return dtype == COAT_F32 ? 4 : 2; }
+
+struct GroupQuantArgs {
+    const void* x; uint8_t* y; void* s; int scale_dtype; unsigned int* amax; int64_t M, N, ldx; int QB; int mode;
+    cudaStream_t st;
+    template <typename T, int FMT, bool IEEE> int run() const {
+        const int grid = straight_grid(M * (N / 16));
+        if (mode == 0)
+            group_quantize_kernel<T, FMT, IEEE, 0><<<grid, kStraightThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), y, s, scale_dtype, nullptr, M, N, ldx, N, QB);
+        else
+            group_quantize_kernel<T, FMT, IEEE, 1><<<grid, kStraightThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), nullptr, s, scale_dtype, amax, M, N, ldx, N, QB);
+        return coat_launch_status();
+    }
+};
+
+struct DivisionArgs {
+    const void* x; uint8_t* y; uint8_t* y_t; const void* s_in; void* s_out; int scale_dtype; const unsigned int* amax;
+    int64_t M, N, ldx; cudaStream_t st;
+    template <typename T, int FMT, bool IEEE> int run() const {
+        if (!y_t) {
+            division_kernel<T, FMT, IEEE><<<straight_grid(M * (N / 16)), kStraightThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), y, s_in, s_out, scale_dtype, amax, M, N, ldx, N);
+            return coat_launch_status();
+        }
+        const dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+        if (y)
+            transpose_quant_kernel<T, FMT, IEEE, false, true><<<grid, kTileThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), y, y_t, nullptr, nullptr, s_in, s_out, scale_dtype, amax, (int)M, (int)N, ldx);
+        else
+            transpose_quant_kernel<T, FMT, IEEE, false, false><<<grid, kTileThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), nullptr, y_t, nullptr, nullptr, s_in, s_out, scale_dtype, amax, (int)M, (int)N, ldx);
+        return coat_launch_status();
+    }
+};
+
+struct QuantTransposeArgs {
+    const void* x; uint8_t* y; uint8_t* y_t; void* s_y; void* s_y_t; int scale_dtype; int64_t M, N, ldx; cudaStream_t st;
+    template <typename T, int FMT, bool IEEE> int run() const {
+        const dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+        transpose_quant_kernel<T, FMT, IEEE, true, true><<<grid, kTileThreads, 0, st>>>(
+            reinterpret_cast<const T*>(x), y, y_t, s_y, s_y_t, nullptr, nullptr, scale_dtype, nullptr, (int)M, (int)N, ldx);
+        return coat_launch_status();
+    }
+};
+
+int check_2d(const void* x, int64_t M, int64_t N, int64_t ldx, int in_dtype, int QB) {
+    if (M < 0 || N < 0 || ldx < N) return COAT_E_BADARG;
+    if (!qb_ok(QB) || N % QB != 0) return COAT_E_SHAPE;
+    // 16-element row segments are moved with 16-byte vector accesses
+    if (!coat_aligned(x, 16) || (ldx * elem_size(in_dtype)) % 16 != 0) return COAT_E_ALIGN;
+    return COAT_OK;
+}
+
+}  // namespace
+
+extern "C" int coat_fp8_quantize(const void* x, uint8_t* y, void* s_y, int64_t M, int64_t N, int64_t ldx, int QB,
+                                 int fmt, int in_dtype, int scale_dtype, int flags, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !y || !s_y || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, QB)) return rc;
+    if (!coat_aligned(y, 16)) return COAT_E_ALIGN;
+    GroupQuantArgs a{x, y, s_y, scale_dtype, nullptr, M, N, ldx, QB, 0, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, a);
+}
+
+extern "C" int coat_fp8_group_scales_amax(const void* x, void* s_y, unsigned int* amax_bits, int64_t M, int64_t N,
+                                          int64_t ldx, int QB, int fmt, int in_dtype, int scale_dtype, int flags,
+                                          void* stream) {
+    if (!amax_bits) return COAT_E_BADARG;
+    if (cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), (cudaStream_t)stream) != cudaSuccess) return COAT_E_LAUNCH;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, QB)) return rc;
+    GroupQuantArgs a{x, nullptr, s_y, scale_dtype, amax_bits, M, N, ldx, QB, 1, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, a);
+}
+
+extern "C" int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const void* s_in, void* s_out,
+                                 const unsigned int* amax_bits, int64_t M, int64_t N, int64_t ldx, int fmt,
+                                 int in_dtype, int scale_dtype, int flags, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || (!y && !y_t) || (!s_in && !amax_bits) || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, 16)) return rc;
+    if ((y && !coat_aligned(y, 16)) || (y_t && (!coat_aligned(y_t, 4) || M % 4 != 0))) return COAT_E_ALIGN;
+    DivisionArgs a{x, y, y_t, s_in, s_out, scale_dtype, amax_bits, M, N, ldx, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, a);
+}
+
+extern "C" int coat_fp8_quantize_transpose(const void* x, uint8_t* y, void* s_y, uint8_t* y_t, void* s_y_t, int64_t M,
+                                           int64_t N, int64_t ldx, int QB, int fmt, int in_dtype, int scale_dtype,
+                                           int flags, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !y || !s_y || !y_t || !s_y_t || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (QB != 16) return COAT_E_SHAPE;   // the tile mapping fixes 1x16 groups (the only size the models use)
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, QB)) return rc;
+    if (M % QB != 0) return COAT_E_SHAPE;
+    if (!coat_aligned(y, 4) || !coat_aligned(y_t, 4)) return COAT_E_ALIGN;
+    QuantTransposeArgs a{x, y, y_t, s_y, s_y_t, scale_dtype, M, N, ldx, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, a);
+}
+
+extern "C" int coat_fp8_transpose(const uint8_t* x, uint8_t* y_t, int64_t M, int64_t N, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !y_t || M < 0 || N < 0) return COAT_E_BADARG;
+    if (M % 4 != 0 || N % 4 != 0) return COAT_E_SHAPE;
+    if (!coat_aligned(x, 4) || !coat_aligned(y_t, 4)) return COAT_E_ALIGN;
+    const dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+    transpose_bytes_kernel<<<grid, kTileThreads, 0, (cudaStream_t)stream>>>(x, y_t, (int)M, (int)N);
+    return coat_launch_status();
+}
+
+extern "C" int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf16, int64_t M, int64_t N, int QB,
+                                   int fmt, int scale_dtype, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !s_x || !y_bf16 || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (!qb_ok(QB) || N % QB != 0) return COAT_E_SHAPE;
+    if (!coat_aligned(x, 16) || !coat_aligned(y_bf16, 16)) return COAT_E_ALIGN;
+    const int grid = straight_grid(M * (N / 16));
+    if (fmt == COAT_E4M3)
+        dequantize_kernel<COAT_E4M3><<<grid, kStraightThreads, 0, (cudaStream_t)stream>>>(
+            x, s_x, scale_dtype, reinterpret_cast<__nv_bfloat16*>(y_bf16), M, N, QB);
+    else if (fmt == COAT_E5M2)
+        dequantize_kernel<COAT_E5M2><<<grid, kStraightThreads, 0, (cudaStream_t)stream>>>(
+            x, s_x, scale_dtype, reinterpret_cast<__nv_bfloat16*>(y_bf16), M, N, QB);
+    else
+        return COAT_E_BADARG;
+    return coat_launch_status();
+}

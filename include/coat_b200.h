@@ -42,6 +42,12 @@ extern "C" {
  * the reference kernel does (slow, the checker for the guarded fast path).   */
 #define COAT_ADAMW_EXACT_POW 1
 
+/* ---- flags for the quantizers --------------------------------------------- */
+/* Use IEEE division for scale = (amax + 1e-10) / fp8_max and q = x / scale instead of the
+ * PTX div.full.f32 the reference's Triton kernels compile to (a CPU can reproduce IEEE
+ * division bit for bit; div.full.f32 differs from it in the last place now and then).   */
+#define COAT_QUANT_IEEE_DIV 1
+
 const char* coat_b200_version(void);
 const char* coat_strerror(int code);
 /* 0 if the current device is sm_100, else COAT_E_DEVICE. */
@@ -109,6 +115,53 @@ int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int64_t* group
                               float beta1, float beta2, float lr, float wd, float eps,
                               int step, int qgroup, int expand_min, int p_dtype,
                               int flags, void* stream);
+
+/* =========================== quantizers ====================================
+ * x is an M x N row-major matrix of in_dtype (COAT_BF16 / COAT_F16 / COAT_F32) with row stride ldx
+ * (elements); codes are dense M x N (or N x M) bytes of format fmt (COAT_E4M3 / COAT_E5M2); scales are
+ * of scale_dtype (COAT_BF16, the reference's default, COAT_F32 or COAT_F16).  N must be a multiple of QB,
+ * x 16-byte aligned with a 16-byte multiple row pitch.  3-D inputs are flattened by the caller, as the
+ * reference's python wrappers do.
+ */
+
+/* Per-1xQB-group quantize: s = (max|x| + 1e-10) / fp8_max per group, q = x / s; QB in {16,32,64,128}.
+ * Replaces fp8_quantize (coat/activation/real_quantization/_quantize.py:120-163, kernel :37-118). */
+int coat_fp8_quantize(const void* x, uint8_t* y, void* s_y, int64_t M, int64_t N, int64_t ldx, int QB,
+                      int fmt, int in_dtype, int scale_dtype, int flags, void* stream);
+
+/* Pass 1 of the per-tensor quantize: the tensor's amax (as the bit pattern of a non-negative float, in the
+ * 4-byte scratch word *amax_bits, which this call zeroes first on the stream) and, if s_y != NULL, the
+ * per-1xQB-group scales.  Replaces the kernel of fp8_quantize_pertensor /
+ * fp8_quantize_pertensor_transpose (_quantize_pertensor.py:46-103, _quantize_pertensor_transpose.py:46-103)
+ * together with the torch reduction s_y.max() that follows it (:139). */
+int coat_fp8_group_scales_amax(const void* x, void* s_y, unsigned int* amax_bits, int64_t M, int64_t N,
+                               int64_t ldx, int QB, int fmt, int in_dtype, int scale_dtype, int flags,
+                               void* stream);
+
+/* Division by ONE scale, q = x / s, with optional transposed copy: y (M x N) and / or y_t (N x M) may be
+ * NULL (y == NULL is the reference's only_transposed=True).  The scale is the device scalar *s_in of
+ * scale_dtype, or, if amax_bits != NULL, round_to_scale_dtype((amax + 1e-10) / fp8_max) taken from pass 1,
+ * which is then also written to *s_out.  Replaces fp8_division (_division.py:153-207, kernel :45-126) and
+ * fp8_division_transpose (_division_transpose.py:147-210, kernel :48-144); stochastic rounding is not
+ * provided (no caller in the reference's models enables it). */
+int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const void* s_in, void* s_out,
+                      const unsigned int* amax_bits, int64_t M, int64_t N, int64_t ldx, int fmt,
+                      int in_dtype, int scale_dtype, int flags, void* stream);
+
+/* One pass: 1x16 groups along the rows -> (y, s_y[M, N/16]) and 1x16 groups of the transposed matrix
+ * (16 consecutive rows of one column) -> (y_t[N, M], s_y_t[N, M/16]).  QB must be 16, M a multiple of 16.
+ * Replaces fp8_quantize_transpose (_quantize_transpose.py:176-226, kernel :39-173). */
+int coat_fp8_quantize_transpose(const void* x, uint8_t* y, void* s_y, uint8_t* y_t, void* s_y_t, int64_t M,
+                                int64_t N, int64_t ldx, int QB, int fmt, int in_dtype, int scale_dtype,
+                                int flags, void* stream);
+
+/* Byte transpose of an M x N code matrix (M, N multiples of 4).
+ * Replaces fp8_transpose (_transpose.py:85-115, kernel :39-82). */
+int coat_fp8_transpose(const uint8_t* x, uint8_t* y_t, int64_t M, int64_t N, void* stream);
+
+/* y = bf16(code * group scale).  Replaces fp8_dequantize (_dequantize.py:119-156, kernel :44-116). */
+int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf16, int64_t M, int64_t N, int QB,
+                        int fmt, int scale_dtype, void* stream);
 
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).

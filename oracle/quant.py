@@ -1,0 +1,80 @@
+"""CPU restatement of the reference's quantizer kernels in torch fp32 (TEST INFRASTRUCTURE ONLY).
+
+Each function follows the arithmetic of one Triton kernel of coat/activation/real_quantization/:
+    _quantize.py:74-92              scale = (max|x| + 1e-10) / fp8_max ; q = x / scale ; store scale rounded
+    _quantize_pertensor.py:80-92    the same scale, stored only; then s_y.max() (:139) and _division.py:86-93
+    _division.py:84-114             q = x / s with a scalar s
+    _quantize_transpose.py:84-145   row groups and groups of the transposed tile
+    _dequantize.py:87-97            code * scale -> bf16
+with IEEE fp32 division in the place of the GPU's div.full.f32 (a CPU cannot reproduce the latter bit for
+bit; the CUDA kernels offer IEEE division behind COAT_QUANT_IEEE_DIV for exactly this comparison), and the
+saturating round-to-nearest-even cast written as clamp + torch's RNE cast.
+"""
+import torch
+
+FP8_MAX = {torch.float8_e4m3fn: 448.0, torch.float8_e5m2: 57344.0}
+FP8_DTYPE = {"E4M3": torch.float8_e4m3fn, "E5M2": torch.float8_e5m2}
+SCALE_MIN_THRES = 1e-10
+
+
+def _dt(fp8type):
+    return FP8_DTYPE[fp8type] if isinstance(fp8type, str) else fp8type
+
+
+def cast_fp8(x, fp8type):
+    """float -> fp8, round to nearest even, saturate to the largest finite value."""
+    fp8type = _dt(fp8type)
+    m = FP8_MAX[fp8type]
+    return x.float().clamp(-m, m).to(fp8type)
+
+
+def group_scales(x, QB, fp8type):
+    """fp32 (un-rounded) scale of every 1xQB group of a 2-D tensor."""
+    M, N = x.shape
+    amax = x.float().reshape(M, N // QB, QB).abs().amax(dim=-1)
+    return (amax + torch.tensor(SCALE_MIN_THRES, dtype=torch.float32)) / torch.tensor(FP8_MAX[_dt(fp8type)],
+                                                                                    dtype=torch.float32)
+
+
+def fp8_quantize(x, QB, fp8type, scale_dtype=torch.bfloat16):
+    M, N = x.shape
+    s = group_scales(x, QB, fp8type)
+    q = cast_fp8((x.float().reshape(M, N // QB, QB) / s.unsqueeze(-1)).reshape(M, N), fp8type)
+    return q, s.to(scale_dtype)
+
+
+def fp8_division(x, fp8type, s):
+    return cast_fp8(x.float() / s.float(), fp8type)
+
+
+def fp8_quantize_pertensor(x, QB, fp8type, scale_dtype=torch.bfloat16):
+    """-> (q, s_max, s_y): group scales rounded to scale_dtype, their maximum, q = x / s_max."""
+    s_y = group_scales(x, QB, fp8type).to(scale_dtype)
+    s_max = s_y.max()
+    return fp8_division(x, fp8type, s_max), s_max, s_y
+
+
+def fp8_quantize_pertensor_transpose(x, QB, fp8type, scale_dtype=torch.bfloat16):
+    q, s_max, _ = fp8_quantize_pertensor(x, QB, fp8type, scale_dtype)
+    return q, s_max, q.view(torch.uint8).t().contiguous().view(q.dtype)
+
+
+def fp8_quantize_transpose(x, QB, fp8type, scale_dtype=torch.bfloat16):
+    y, s_y = fp8_quantize(x, QB, fp8type, scale_dtype)
+    y_t, s_y_t = fp8_quantize(x.t().contiguous(), QB, fp8type, scale_dtype)
+    return (y, s_y), (y_t, s_y_t)
+
+
+def fp8_dequantize(q, s, QB):
+    M, N = q.shape
+    return (q.float().reshape(M, N // QB, QB) * s.float().unsqueeze(-1)).reshape(M, N).to(torch.bfloat16)
+
+
+def near_rounding_boundary(x_over_s, fp8type, ulps=4):
+    """Mask of quotients that lie within `ulps` fp32 ulps of an FP8 rounding boundary (where IEEE
+    division and div.full.f32, which may differ by 2 ulp, can legitimately give different codes)."""
+    fp8type = _dt(fp8type)
+    q = x_over_s.float().abs().clamp(max=FP8_MAX[fp8type])
+    lo = cast_fp8(q * (1 - ulps * 2.0 ** -23), fp8type).view(torch.uint8)
+    hi = cast_fp8(q * (1 + ulps * 2.0 ** -23), fp8type).view(torch.uint8)
+    return lo != hi
