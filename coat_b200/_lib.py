@@ -35,6 +35,7 @@ SIGNATURES = {
     "coat_fp8_group_scales_amax": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_division": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_quantize_transpose": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_quantize_pertensor_static": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_transpose": [_vp, _vp, _i64, _i64, _vp],
     "coat_fp8_dequantize": [_vp, _vp, _vp, _i64, _i64, _i, _i, _i, _vp],
     "coat_fp8_adamw_debug_counters": [_vp],

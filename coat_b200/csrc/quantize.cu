@@ -538,3 +538,133 @@ extern "C" int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf
         return COAT_E_BADARG;
     return coat_launch_status();
 }
+
+namespace {
+
+// =================================================================================================
+// Per-tensor quantize that allocates nothing
+// =================================================================================================
+// Who this is for: a host that may not allocate device memory at the point where it quantizes, and
+// cannot reserve a scratch word ahead of time either.  Examples are a plugin that has been handed a
+// fixed memory budget by the framework around it, a host written without a caching allocator where the
+// only way to get four bytes is cudaMalloc, and code that runs in a latency-critical section between
+// other GPU work, where cudaMalloc / cudaFree would synchronise the whole device.  The ordinary entry
+// points above need the caller to pass a 4-byte scratch word for the tensor's amax; this one keeps its
+// scratch in the library image instead.
+//
+// The scratch is the file-scope array below: one partial maximum per CTA of the first pass, then the
+// reduced maximum in the slot after the last partial.  It is part of the loaded library, so every GPU
+// that loads the library holds these ~17 KB until the process exits.  Its size fixes the largest input:
+// kStaticMaxCtas CTAs of kStaticChunk elements each.
+//
+// Sharing: every call on a device uses the same array, and it keeps whatever the previous call left
+// there.  Nothing in it has to start at zero (each call overwrites every slot it later reads: its own
+// partials, then the reduced word), but two calls whose kernels overlap on the GPU - different streams,
+// or different host threads - race on it and can corrupt each other's scale.  Calls on one stream are
+// safe back to back.
+constexpr int kStaticMaxCtas = 4096;
+constexpr int kStaticSegsPerThread = 4;
+constexpr int64_t kStaticChunk = (int64_t)kStraightThreads * 16 * kStaticSegsPerThread;   // 16384 elements per CTA
+constexpr int64_t kStaticMaxElements = kStaticChunk * kStaticMaxCtas;                     // 67 108 864
+
+static __device__ __align__(256) float g_pertensor_scratch[kStaticMaxCtas + 64];
+
+// first pass: CTA b reduces |x| over its chunk of 16-element row segments into scratch[b]
+template <typename T>
+__global__ void __launch_bounds__(kStraightThreads)
+static_partial_amax_kernel(const T* __restrict__ x, float* __restrict__ partials, int64_t M, int64_t N, int64_t ldx) {
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    const int64_t first = (int64_t)blockIdx.x * kStraightThreads * kStaticSegsPerThread;
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < kStaticSegsPerThread; ++k) {
+        const int64_t seg = first + (int64_t)k * kStraightThreads + threadIdx.x;
+        if (seg < total) {
+            const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
+            float v[16];
+            Seg16<T>::load(x + row * ldx + c16 * 16, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
+    }
+    amax = coat_warp_max(amax);
+    __shared__ float wmax[kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+        m = coat_warp_max(m);
+        if (threadIdx.x == 0) partials[blockIdx.x] = m;
+    }
+}
+
+// second step: one CTA folds the partials into the word the division kernels read (bit pattern of a
+// non-negative float), stored right after the last partial slot
+__global__ void __launch_bounds__(kStraightThreads)
+static_reduce_amax_kernel(float* __restrict__ scratch, int n_partials) {
+    float m = 0.f;
+    for (int i = threadIdx.x; i < n_partials; i += kStraightThreads) m = fmaxf(m, scratch[i]);
+    m = coat_warp_max(m);
+    __shared__ float wmax[kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float r = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+        r = coat_warp_max(r);
+        if (threadIdx.x == 0) reinterpret_cast<unsigned int*>(scratch)[kStaticMaxCtas] = __float_as_uint(r);
+    }
+}
+
+// In host code the name g_pertensor_scratch is only a stand-in for the device array, not an address a
+// kernel can use; the address comes from cudaGetSymbolAddress, once per device, with that device current.
+int static_scratch_address(float** out) {
+    static float* cached[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return COAT_E_DEVICE;
+    if (!cached[dev]) {
+        float* p = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_pertensor_scratch) != cudaSuccess || !p)
+            return COAT_E_LAUNCH;
+        cached[dev] = p;
+    }
+    *out = cached[dev];
+    return COAT_OK;
+}
+
+struct StaticAmaxArgs {
+    const void* x; float* scratch; int64_t M, N, ldx; int n_ctas; cudaStream_t st;
+    template <typename T, int FMT, bool IEEE> int run() const {
+        static_partial_amax_kernel<T><<<n_ctas, kStraightThreads, 0, st>>>(reinterpret_cast<const T*>(x), scratch, M, N, ldx);
+        static_reduce_amax_kernel<<<1, kStraightThreads, 0, st>>>(scratch, n_ctas);
+        return coat_launch_status();
+    }
+};
+
+}  // namespace
+
+// Per-tensor quantize (optionally with the transposed copy) without any allocation and without a
+// caller-provided scratch word; see the block comment above for who needs it, the size limit and the
+// sharing rules.  Same results as coat_fp8_group_scales_amax(s_y = NULL) followed by coat_fp8_division
+// with that amax word.  y or y_t may be NULL (not both); *s_out receives the scale.  Returns
+// COAT_E_TOOBIG if M*N exceeds 67 108 864 elements.  The first call on a device looks up the address
+// of the scratch array (a runtime query, no allocation); make that first call before starting any
+// stream capture on that device.
+extern "C" int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, void* s_out, int64_t M,
+                                                  int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
+                                                  int flags, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || (!y && !y_t) || !s_out || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, 16)) return rc;
+    if (M * N > kStaticMaxElements) return COAT_E_TOOBIG;
+    if ((y && !coat_aligned(y, 16)) || (y_t && (!coat_aligned(y_t, 4) || M % 4 != 0))) return COAT_E_ALIGN;
+    float* scratch = nullptr;
+    if (int rc = static_scratch_address(&scratch)) return rc;
+    const int64_t segs = M * (N / 16);
+    const int n_ctas = (int)((segs + kStraightThreads * kStaticSegsPerThread - 1) / (kStraightThreads * kStaticSegsPerThread));
+    StaticAmaxArgs a{x, scratch, M, N, ldx, n_ctas, (cudaStream_t)stream};
+    if (int rc = dispatch(in_dtype, fmt, flags, a)) return rc;
+    DivisionArgs d{x, y, y_t, nullptr, s_out, scale_dtype,
+                   reinterpret_cast<const unsigned int*>(scratch) + kStaticMaxCtas, M, N, ldx, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, d);
+}

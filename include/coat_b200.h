@@ -163,6 +163,20 @@ int coat_fp8_transpose(const uint8_t* x, uint8_t* y_t, int64_t M, int64_t N, voi
 int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf16, int64_t M, int64_t N, int QB,
                         int fmt, int scale_dtype, void* stream);
 
+/* Per-tensor quantize, optionally with the transposed copy, for callers that can neither allocate device
+ * memory nor set aside the 4-byte amax word the two-call form above needs: a plugin living inside a
+ * fixed memory budget, a host without a caching allocator, code in a section where cudaMalloc's
+ * device-wide synchronisation is not acceptable.  It has no counterpart in the reference (whose wrappers
+ * allocate freely through torch).  The scratch is a ~17 KB array inside the library image, which every
+ * GPU that loads the library keeps until the process ends; it limits the input to 67 108 864 elements
+ * (COAT_E_TOOBIG beyond that).  All calls on a device share that array: back-to-back calls on one
+ * stream are fine, calls that overlap on the GPU race.  The first call on a device queries the array's
+ * address and should be made before any stream capture starts.  Results are identical to
+ * coat_fp8_group_scales_amax + coat_fp8_division.  y or y_t may be NULL (not both). */
+int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, void* s_out, int64_t M,
+                                       int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
+                                       int flags, void* stream);
+
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
  * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded
