@@ -216,6 +216,75 @@ def e2e_public_api(torch, device, steps, warmup):
     return n / (ms / 1e3), 4 * n, 4 * n, n
 
 
+def quantizer_extras(torch, device, peak):
+    """GB/s of the quantizers on BASELINE.json's activation configuration (8192 tokens x 4096 bf16,
+    0.1 % of the entries x100): algorithmic bytes / CUDA-event time of the C-ABI calls on preallocated
+    outputs, 20 calls replayed from one CUDA graph so that host launch overhead (comparable to these
+    15-30 us kernels) stays out of the device time.  The input (64 MB) is smaller than L2, so four
+    distinct inputs rotate (256 MB of reads between two uses of the same buffer)."""
+    from coat_b200 import _lib
+    L = _lib.lib()
+    M, N = 8192, 4096
+    gen = torch.Generator(device=device).manual_seed(1)
+    xs = []
+    for _ in range(4):
+        x = torch.randn(M, N, generator=gen, device=device)
+        x = torch.where(torch.rand(M, N, generator=gen, device=device) < 1e-3, x * 100, x).to(torch.bfloat16)
+        xs.append(x)
+    y = torch.empty(M, N, dtype=torch.uint8, device=device)
+    y_t = torch.empty(N, M, dtype=torch.uint8, device=device)
+    s_y = torch.empty(M, N // 16, dtype=torch.bfloat16, device=device)
+    s_y_t = torch.empty(N, M // 16, dtype=torch.bfloat16, device=device)
+    s_max = torch.empty((), dtype=torch.bfloat16, device=device)
+    amax = torch.empty(1, dtype=torch.int32, device=device)
+    E4M3, BF16 = _lib.E4M3, _lib.BF16
+
+    def st():
+        return _lib.stream_ptr(device)
+
+    def group(x):
+        return L.coat_fp8_quantize(x.data_ptr(), y.data_ptr(), s_y.data_ptr(), M, N, N, 16, E4M3, BF16, BF16, 0, st())
+
+    def pertensor(x, transposed):
+        rc = L.coat_fp8_group_scales_amax(x.data_ptr(), None if transposed else s_y.data_ptr(), amax.data_ptr(), M, N,
+                                          N, 16, E4M3, BF16, BF16, 0, st())
+        return rc or L.coat_fp8_division(x.data_ptr(), y.data_ptr(), y_t.data_ptr() if transposed else None, None,
+                                         s_max.data_ptr(), amax.data_ptr(), M, N, N, E4M3, BF16, BF16, 0, st())
+
+    def qt(x):
+        return L.coat_fp8_quantize_transpose(x.data_ptr(), y.data_ptr(), s_y.data_ptr(), y_t.data_ptr(),
+                                             s_y_t.data_ptr(), M, N, N, 16, E4M3, BF16, BF16, 0, st())
+
+    cases = {
+        "quantize_1x16": (group, 3.125, 1),
+        "quantize_pertensor": (lambda x: pertensor(x, False), 3.125, 2),
+        "quantize_pertensor_transpose": (lambda x: pertensor(x, True), 4.0, 2),
+        "quantize_transpose_1x16": (qt, 4.25, 1),
+    }
+    out = {}
+    iters = 20
+    for name, (fn, bytes_per_elem, launches) in cases.items():
+        for i in range(4):
+            _lib.check(fn(xs[i]), name)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(iters):
+                fn(xs[i & 3])
+        graph.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / iters
+        gbs = M * N * bytes_per_elem / (ms / 1e3) / 1e9
+        out[name] = {"us": ms * 1e3, "GB/s": gbs, "frac_of_measured_hbm": gbs / peak,
+                     "algorithmic_bytes_per_elem": bytes_per_elem, "kernels_per_call": launches}
+    return out
+
+
 def run_gpu_arm(args):
     import torch
     import torch.distributed as dist
@@ -327,6 +396,10 @@ def run_gpu_arm(args):
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
+        if not args.kernel_only and args.workload == "llama2-7b":
+            del opt, grads, tables
+            torch.cuda.empty_cache()
+            line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
         if cpu_v is not None:
             line["cpu_baseline"] = {
                 "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
