@@ -38,6 +38,14 @@ SIGNATURES = {
     "coat_fp8_quantize_pertensor_static": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_transpose": [_vp, _vp, _i64, _i64, _vp],
     "coat_fp8_dequantize": [_vp, _vp, _vp, _i64, _i64, _i, _i, _i, _vp],
+    "coat_fp8_silu_forward": [_vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
+    "coat_fp8_act_backward": [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_gelu_forward": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
+    "coat_fp8_mul_forward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
+    "coat_fp8_mul_backward": [_vp] * 9 + [_i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_add": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_rmsnorm_forward": [_vp] * 7 + [_i64, _i64, _i, _f, _i, _i, _i, _i, _vp],
+    "coat_fp8_rmsnorm_backward": [_vp] * 7 + [_i, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_adamw_debug_counters": [_vp],
     "coat_fp8_adamw_device_status": [],
 }

@@ -7,3 +7,12 @@ from ._quantize import fp8_quantize  # noqa: F401
 from ._quantize_pertensor import fp8_quantize_pertensor  # noqa: F401
 from ._quantize_pertensor_transpose import fp8_quantize_pertensor_transpose  # noqa: F401
 from ._transpose import fp8_transpose  # noqa: F401
+from .add_bwd import fp8_add_Ifp_Ifp_Ofp_Opt  # noqa: F401
+from .add_fwd import fp8_add_Ifp_Ifp_Ofp_Og16  # noqa: F401
+from .func_rmsnorm import fp8_rmsnorm_backward, fp8_rmsnorm_forward  # noqa: F401
+from .gelu_bwd import fp8_gelu_backward  # noqa: F401
+from .gelu_fwd import fp8_gelu_forward  # noqa: F401
+from .mul_bwd import fp8_mul_backward  # noqa: F401
+from .mul_fwd import fp8_mul_forward  # noqa: F401
+from .silu_bwd import fp8_silu_backward  # noqa: F401
+from .silu_fwd import fp8_silu_forward  # noqa: F401

@@ -1,0 +1,214 @@
+"""Host side of the fused quantize-on-save operators: the reference's names, positional arguments
+and return tuples; torch allocates the outputs, the C ABI does the work.
+
+Reference wrappers mirrored (paths under coat/activation/real_quantization/):
+  fp8_silu_forward   silu_fwd.py:152-198      fp8_silu_backward  silu_bwd.py:170-238
+  fp8_gelu_forward   gelu_fwd.py:152-203      fp8_gelu_backward  gelu_bwd.py:173-230
+  fp8_mul_forward    mul_fwd.py:191-254       fp8_mul_backward   mul_bwd.py:221-315
+  fp8_add_Ifp_Ifp_Ofp_Og16  add_fwd.py:162-213    fp8_add_Ifp_Ifp_Ofp_Opt  add_bwd.py:147-200
+  fp8_rmsnorm_forward / fp8_rmsnorm_backward  func_rmsnorm.py:223-335
+Where the reference runs kernel -> `s_y.max()` -> fp8_division[_transpose], the producing kernel here also
+leaves the tensor's amax in a 4-byte word and the division derives the same scale from it.
+"""
+import torch
+
+from ... import _lib
+from ._ops import _call, _flags, _fp8_dtype
+
+
+def _flat(*ts):
+    """Flatten 3-D tensors to 2-D the way the reference does; returns the batch size or None."""
+    bs = ts[0].shape[0] if ts[0].dim() == 3 else None
+    out = []
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("coat_b200: the fused operators need CUDA tensors (no CPU path exists)")
+        out.append(t.reshape(-1, t.shape[-1]).contiguous())
+    return out, bs
+
+
+def _unflat(t, bs):
+    return t if bs is None or t is None else t.reshape(bs, -1, t.shape[-1])
+
+
+def _amax_word(device):
+    return torch.empty(1, dtype=torch.int32, device=device)
+
+
+def _divide(y_bf16, fp8type, amax, want_transposed, flags, scale_dtype=torch.bfloat16):
+    """Per-tensor quantize of a bf16 intermediate with the scale derived from the amax word."""
+    M, N = y_bf16.shape
+    dev = y_bf16.device
+    q = torch.empty((M, N), dtype=fp8type, device=dev)
+    q_t = torch.empty((N, M), dtype=fp8type, device=dev) if want_transposed else None
+    s_max = torch.empty((), dtype=scale_dtype, device=dev)
+    _call("coat_fp8_division", y_bf16.data_ptr(), q.data_ptr(), None if q_t is None else q_t.data_ptr(), None,
+          s_max.data_ptr(), amax.data_ptr(), M, N, N, _lib.fp8_format(fp8type)[0], _lib.BF16,
+          _lib.float_dtype(scale_dtype), _flags(flags), _lib.stream_ptr(dev))
+    return q, s_max, q_t
+
+
+def fp8_silu_forward(x, s_x, QB, *, flags=None):
+    (x2, s2), bs = _flat(x, s_x)
+    M, N = x2.shape
+    y = torch.empty_like(x2)
+    s_y = torch.empty_like(s2)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_silu_forward", x2.data_ptr(), s2.data_ptr(), y.data_ptr(), s_y.data_ptr(), M, N, QB,
+              _lib.fp8_enum_of(x2), _lib.float_dtype(s2), _flags(flags), _lib.stream_ptr(x.device))
+    return _unflat(y, bs), _unflat(s_y, bs)
+
+
+def _act_backward(gelu, x, s_x, g, QB, fp8type, flags):
+    (x2, s2, g2), bs = _flat(x, s_x, g)
+    M, N = x2.shape
+    fp8type = _fp8_dtype(fp8type)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    s_y = torch.empty(s2.shape, dtype=torch.bfloat16, device=x.device)
+    amax = _amax_word(x.device)
+    _call("coat_fp8_act_backward", int(gelu), x2.data_ptr(), s2.data_ptr(), g2.data_ptr(), y.data_ptr(),
+          s_y.data_ptr(), amax.data_ptr(), M, N, QB, _lib.fp8_enum_of(x2), _lib.float_dtype(s2),
+          _lib.float_dtype(g2), _lib.fp8_format(fp8type)[0], _flags(flags), _lib.stream_ptr(x.device))
+    return y, s_y, amax, bs, fp8type
+
+
+def fp8_silu_backward(x, s_x, g, QB, fp8type, stochastic=False, output_quantized_transpose=False, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    with torch.cuda.device(x.device):
+        y, s_y, amax, bs, fp8type = _act_backward(False, x, s_x, g, QB, fp8type, flags)
+        if not output_quantized_transpose:
+            return _unflat(y, bs), _unflat(s_y, bs)
+        qy, s_max, qy_t = _divide(y, fp8type, amax, True, flags)
+    return _unflat(qy, bs), s_max, qy_t
+
+
+def fp8_gelu_forward(x, s_x, QB, transpose_output_2d=False, *, flags=None):
+    (x2, s2), bs = _flat(x, s_x)
+    M, N = x2.shape
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    s_y = torch.empty_like(s2)
+    amax = _amax_word(x.device)
+    with torch.cuda.device(x.device):
+        _call("coat_fp8_gelu_forward", x2.data_ptr(), s2.data_ptr(), y.data_ptr(), s_y.data_ptr(), amax.data_ptr(),
+              M, N, QB, _lib.fp8_enum_of(x2), _lib.float_dtype(s2), _flags(flags), _lib.stream_ptr(x.device))
+        qy, s_max, qy_t = _divide(y, x2.dtype, amax, True, flags, scale_dtype=s2.dtype)
+    if bs is not None and not transpose_output_2d:
+        qy_t = qy_t.reshape(bs, -1, N)
+    return _unflat(qy, bs), s_max, qy_t
+
+
+def fp8_gelu_backward(x, s_x, g, QB, fp8type, *, flags=None):
+    with torch.cuda.device(x.device):
+        y, s_y, amax, bs, fp8type = _act_backward(True, x, s_x, g, QB, fp8type, flags)
+        qy, s_max, _ = _divide(y, fp8type, amax, False, flags)
+    return _unflat(qy, bs), s_max
+
+
+def fp8_mul_forward(x1, s_x1, x2, s_x2, QB, transpose_output_2d=False, *, flags=None):
+    (a, sa, b, sb), bs = _flat(x1, s_x1, x2, s_x2)
+    assert a.shape == b.shape and sa.shape == sb.shape
+    M, N = a.shape
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    s_y = torch.empty_like(sa)
+    amax = _amax_word(a.device)
+    with torch.cuda.device(a.device):
+        _call("coat_fp8_mul_forward", a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(), y.data_ptr(),
+              s_y.data_ptr(), amax.data_ptr(), M, N, QB, _lib.fp8_enum_of(a), _lib.float_dtype(sa), _flags(flags),
+              _lib.stream_ptr(a.device))
+        qy, s_max, qy_t = _divide(y, b.dtype, amax, True, flags, scale_dtype=sa.dtype)
+    if bs is not None and not transpose_output_2d:
+        qy_t = qy_t.reshape(bs, -1, qy.shape[-1])
+    return _unflat(qy, bs), s_max, qy_t
+
+
+def fp8_mul_backward(x1, s_x1, x2, s_x2, g, QB, fp8type, stochastic=False, output_quantized_transpose=False, *,
+                     flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    (a, sa, b, sb, g2), bs = _flat(x1, s_x1, x2, s_x2, g)
+    assert a.shape == b.shape and sa.shape == sb.shape
+    M, N = a.shape
+    fp8type = _fp8_dtype(fp8type)
+    dev = a.device
+    y1 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    y2 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    s_y2 = torch.empty(sa.shape, dtype=torch.bfloat16, device=dev)
+    amax = _amax_word(dev)
+    with torch.cuda.device(dev):
+        _call("coat_fp8_mul_backward", a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(), g2.data_ptr(),
+              y1.data_ptr(), y2.data_ptr(), s_y2.data_ptr(), amax.data_ptr(), M, N, QB, _lib.fp8_enum_of(a),
+              _lib.float_dtype(sa), _lib.float_dtype(g2), _lib.fp8_format(fp8type)[0], _flags(flags),
+              _lib.stream_ptr(dev))
+        if not output_quantized_transpose:
+            return _unflat(y1, bs), (_unflat(y2, bs), _unflat(s_y2, bs))
+        qy2, s_max, qy2_t = _divide(y2, fp8type, amax, True, flags)
+    return _unflat(y1, bs), (_unflat(qy2, bs), s_max, qy2_t)
+
+
+def _add(x1, x2, QB, fp8type, want_codes, want_amax, flags):
+    (a, b), bs = _flat(x1, x2)
+    assert a.shape == b.shape
+    M, N = a.shape
+    dev = a.device
+    y1 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    y2 = torch.empty((M, N), dtype=fp8type, device=dev) if want_codes else None
+    s_y2 = torch.empty((M, N // QB), dtype=torch.bfloat16, device=dev)
+    amax = _amax_word(dev) if want_amax else None
+    _call("coat_fp8_add", a.data_ptr(), b.data_ptr(), y1.data_ptr(), None if y2 is None else y2.data_ptr(),
+          s_y2.data_ptr(), None if amax is None else amax.data_ptr(), M, N, QB, _lib.float_dtype(a),
+          _lib.float_dtype(b), _lib.fp8_format(fp8type)[0], _flags(flags), _lib.stream_ptr(dev))
+    return y1, y2, s_y2, amax, bs
+
+
+def fp8_add_Ifp_Ifp_Ofp_Og16(x1, x2, fp8type, QB, *, flags=None):
+    fp8type = _fp8_dtype(fp8type)
+    with torch.cuda.device(x1.device):
+        y1, y2, s_y2, _, bs = _add(x1, x2, QB, fp8type, True, False, flags)
+    return _unflat(y1, bs), (_unflat(y2, bs), _unflat(s_y2, bs))
+
+
+def fp8_add_Ifp_Ifp_Ofp_Opt(x1, x2, QB, fp8type, stochastic=False, *, flags=None):
+    if stochastic:
+        raise NotImplementedError("stochastic rounding is not provided")
+    fp8type = _fp8_dtype(fp8type)
+    with torch.cuda.device(x1.device):
+        y1, _, s_y2, amax, bs = _add(x1, x2, QB, fp8type, False, True, flags)
+        qy2, s_max, _ = _divide(y1, fp8type, amax, False, flags)
+    return _unflat(y1, bs), (_unflat(qy2, bs), s_max, _unflat(s_y2, bs))
+
+
+def fp8_rmsnorm_forward(x, s_x, w, QB, eps, transpose_output_2d=False, *, flags=None):
+    (x2, s2), bs = _flat(x, s_x)
+    M, N = x2.shape
+    dev = x.device
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    s_y = torch.empty((M,), dtype=torch.bfloat16, device=dev)
+    rstd = torch.empty((M,), dtype=torch.float32, device=dev)
+    amax = _amax_word(dev)
+    w = w.contiguous()
+    with torch.cuda.device(dev):
+        _call("coat_fp8_rmsnorm_forward", x2.data_ptr(), s2.data_ptr(), w.data_ptr(), y.data_ptr(), s_y.data_ptr(),
+              rstd.data_ptr(), amax.data_ptr(), M, N, QB, float(eps), _lib.fp8_enum_of(x2), _lib.float_dtype(s2),
+              _lib.float_dtype(w), _flags(flags), _lib.stream_ptr(dev))
+        qy, s_max, qy_t = _divide(y, x2.dtype, amax, True, flags)
+    if bs is not None and not transpose_output_2d:
+        qy_t = qy_t.reshape(bs, -1, N)
+    num_warps = 8   # kept in the returned context for signature compatibility; unused here
+    return _unflat(qy, bs), s_max, qy_t, (w, rstd, num_warps)
+
+
+def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps):
+    (x2, s2, g2), bs = _flat(x, s_x, g)
+    M, N = g2.shape
+    dev = x.device
+    dx = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    dw = torch.empty((N,), dtype=w.dtype, device=dev)
+    n_partials = min(M, 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+    partial = torch.empty((n_partials, N), dtype=torch.float32, device=dev)
+    w = w.contiguous()
+    with torch.cuda.device(dev):
+        _call("coat_fp8_rmsnorm_backward", x2.data_ptr(), s2.data_ptr(), g2.data_ptr(), w.data_ptr(), v.data_ptr(),
+              dx.data_ptr(), partial.data_ptr(), n_partials, dw.data_ptr(), M, N, QB, _lib.fp8_enum_of(x2),
+              _lib.float_dtype(s2), _lib.float_dtype(g2), _lib.float_dtype(w), _lib.stream_ptr(dev))
+    return _unflat(dx, bs), dw

@@ -1,0 +1,504 @@
+// Fused "quantize-on-save" element-wise operators for sm_100a: SiLU / GELU forward and backward, the
+// gated product forward and backward, and the residual add, each dequantising its 1xQB-quantised FP8
+// inputs on the fly, computing in fp32, and emitting a bf16 result and / or a 1xQB-quantised FP8 result,
+// the per-group scales, and the tensor's amax for a following per-tensor division.
+//
+// Arithmetic follows the reference's Triton kernels (paths under coat/activation/real_quantization/):
+//   silu_fwd.py:100-118   x = code*s ; sig = 1/(1+exp(-x)) ; y = sig*x ; group quantize
+//   silu_bwd.py:112-137   (sig + x*sig*(1-sig)) * g -> bf16, group scales
+//   gelu_fwd.py:100-118   0.5*(1+erf(x/sqrt 2))*x -> bf16, group scales
+//   gelu_bwd.py:112-140   (cdf + x*exp(-x^2/2)/sqrt(2 pi)) * g -> bf16, group scales
+//   mul_fwd.py:101-127    (c1*s1)*(c2*s2) -> bf16, group scales
+//   mul_bwd.py:117-152    g*x2 -> bf16 ; g*x1 -> bf16, group scales
+//   add_fwd.py:92-121     a+b -> bf16 and 1xQB FP8 + scales ;  add_bwd.py:92-113  a+b -> bf16, group scales
+// Where the reference then calls `s_y.max()` and fp8_division[_transpose] on the bf16 result, the kernels
+// here also leave the tensor's amax (of the fp32 values, as the group scales are) in a scratch word, so
+// that coat_fp8_division can derive the same scale without a reduction pass.
+//
+// One thread owns 16 consecutive elements of a row (16-byte loads of codes, 32-byte loads of bf16);
+// groups wider than 16 are reduced over the QB/16 neighbouring lanes.
+
+#include <math.h>
+
+#include "quant_common.cuh"
+
+namespace {
+
+enum FusedOp { OP_SILU_FWD = 0, OP_SILU_BWD, OP_GELU_FWD, OP_GELU_BWD, OP_MUL_FWD, OP_MUL_BWD, OP_ADD };
+
+struct FusedArgs {
+    const uint8_t* x1; const void* s1;      // first quantised input and its 1xQB scales
+    const uint8_t* x2; const void* s2;      // second quantised input (gated product)
+    const void* g;                          // bf16 upstream gradient, or first addend (add)
+    const void* h;                          // second addend (add)
+    __nv_bfloat16* y_bf16;                  // bf16 result (may be null)
+    __nv_bfloat16* y1_bf16;                 // mul backward: g * x2
+    uint8_t* y_q;                           // 1xQB FP8 result (may be null)
+    void* s_y;                              // group scales of the result (may be null)
+    unsigned int* amax_bits;                // tensor amax (may be null)
+    int64_t M, N;
+    int QB;
+    int in_scale_dtype, out_scale_dtype;
+    int g_dtype, h_dtype;                   // dtypes of the floating inputs
+    float fp8_max;                          // largest finite value of the FP8 format the scales are for
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_dequant16(const uint8_t* codes, const void* scales, int scale_dtype, int64_t row,
+                                               int64_t c16, int64_t N, int QB, float (&x)[16]) {
+    const uint4 w = *reinterpret_cast<const uint4*>(codes + row * N + c16 * 16);
+    const float s = load_scale(scales, row * (N / QB) + (c16 * 16) / QB, scale_dtype);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[4];
+        coat_fp8x4_to_float4<FMT>(ww[i], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[4 * i + j] = f[j] * s;
+    }
+}
+
+__device__ __forceinline__ void load_float16(const void* base, int dtype, int64_t off, float (&x)[16]) {
+    if (dtype == COAT_BF16) Seg16<__nv_bfloat16>::load(reinterpret_cast<const __nv_bfloat16*>(base) + off, x);
+    else if (dtype == COAT_F16) Seg16<__half>::load(reinterpret_cast<const __half*>(base) + off, x);
+    else Seg16<float>::load(reinterpret_cast<const float*>(base) + off, x);
+}
+
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        o[i] = (uint32_t)coat_float_to_bf16_bits(v[2 * i]) | ((uint32_t)coat_float_to_bf16_bits(v[2 * i + 1]) << 16);
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// sigmoid exactly as `1 / (1.0 + libdevice.exp(-x))` compiles: libdevice expf, then the non-IEEE division
+template <bool IEEE>
+__device__ __forceinline__ float sigmoid_ref(float x) { return qdiv<IEEE>(1.0f, 1.0f + expf(-x)); }
+
+__device__ __forceinline__ float sqrt_approx(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float ex2_approx(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+
+template <int OP, int FMT_IN, int FMT_OUT, bool IEEE>
+__global__ void __launch_bounds__(kStraightThreads)
+fused_elementwise_kernel(FusedArgs a) {
+    const int64_t segs_per_row = a.N >> 4;
+    const int64_t total = a.M * segs_per_row;
+    const int lanes = a.QB >> 4;
+    const float fp8_max = a.fp8_max;
+    float block_max = 0.f;
+    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < ((total + 31) & ~31ll);
+         seg += (int64_t)gridDim.x * blockDim.x) {
+        const bool live = seg < total;
+        const int64_t row = live ? seg / segs_per_row : 0, c16 = live ? seg - row * segs_per_row : 0;
+        const int64_t off = row * a.N + c16 * 16;
+        float v[16];
+        float amax = 0.f;
+        if (live) {
+            float x[16], t[16];
+            if (OP == OP_ADD) {
+                load_float16(a.g, a.g_dtype, off, x);
+                load_float16(a.h, a.h_dtype, off, t);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = x[i] + t[i];
+            } else {
+                load_dequant16<FMT_IN>(a.x1, a.s1, a.in_scale_dtype, row, c16, a.N, a.QB, x);
+                if (OP == OP_SILU_FWD) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = sigmoid_ref<IEEE>(x[i]) * x[i];
+                } else if (OP == OP_SILU_BWD) {
+                    load_float16(a.g, a.g_dtype, off, t);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float sg = sigmoid_ref<IEEE>(x[i]);
+                        // sigmoid + input * sigmoid * (1 - sigmoid), the outer multiply-add contracted
+                        v[i] = __fmaf_rn(x[i] * sg, 1.0f - sg, sg) * t[i];
+                    }
+                } else if (OP == OP_GELU_FWD) {
+                    const float rt2 = sqrt_approx(2.0f);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = qdiv<IEEE>(1.0f + erff(qdiv<IEEE>(x[i], rt2)), 2.0f) * x[i];
+                } else if (OP == OP_GELU_BWD) {
+                    load_float16(a.g, a.g_dtype, off, t);
+                    const float rt2 = sqrt_approx(2.0f), rt2pi = sqrt_approx(2.0f * 3.1415927410125732f);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float cdf = qdiv<IEEE>(1.0f + erff(qdiv<IEEE>(x[i], rt2)), 2.0f);
+                        // tl.exp(u) is ex2.approx(u * log2 e)
+                        const float e = ex2_approx(qdiv<IEEE>(-powf(x[i], 2.0f), 2.0f) * 1.4426950408889634f);
+                        v[i] = (cdf + qdiv<IEEE>(x[i] * e, rt2pi)) * t[i];
+                    }
+                } else {   // OP_MUL_FWD, OP_MUL_BWD
+                    load_dequant16<FMT_IN>(a.x2, a.s2, a.in_scale_dtype, row, c16, a.N, a.QB, t);
+                    if (OP == OP_MUL_FWD) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] = x[i] * t[i];
+                    } else {
+                        float gr[16], y1[16];
+                        load_float16(a.g, a.g_dtype, off, gr);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) { y1[i] = gr[i] * t[i]; v[i] = gr[i] * x[i]; }
+                        store_bf16x16(a.y1_bf16 + off, y1);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
+        amax = subgroup_max(amax, lanes);
+        if (!live) continue;
+        const float scale = qdiv<IEEE>(amax + kScaleMinThres, fp8_max);
+        if (a.y_bf16) store_bf16x16(a.y_bf16 + off, v);
+        if (a.y_q) {
+            float q[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
+            *reinterpret_cast<uint4*>(a.y_q + off) = pack16<FMT_OUT>(q);
+        }
+        if (a.s_y && (c16 & (lanes - 1)) == 0)
+            store_scale(a.s_y, row * (a.N / a.QB) + c16 / lanes, a.out_scale_dtype, scale);
+        block_max = fmaxf(block_max, amax);
+    }
+    if (a.amax_bits) {
+        block_max = coat_warp_max(block_max);
+        __shared__ float wmax[kStraightThreads / 32];
+        if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = block_max;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float m = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+            m = coat_warp_max(m);
+            if (threadIdx.x == 0) atomicMax(a.amax_bits, __float_as_uint(m));
+        }
+    }
+}
+
+// =================================================================================================
+// RMSNorm on a 1xQB-quantised input (func_rmsnorm.py:54-111 forward, :121-220 backward)
+// =================================================================================================
+// One CTA of 256 threads per row; thread t owns the 16-element segments t, t+256, ... (S of them, in
+// registers), so a row of up to 16384 elements is read once.  Row sums are reduced in a fixed order
+// (sequential inside a thread, xor-shuffles inside a warp, then the 8 warp results in order), so the
+// result does not depend on scheduling.  The reference's sum order is whatever layout Triton picks, so
+// rstd agrees with it to rounding only, not bit for bit.
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* smem /*[8]*/) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(COAT_FULL_MASK, v, o);
+    __syncthreads();   // protects smem reuse between consecutive reductions
+    if ((threadIdx.x & 31) == 0) smem[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) r += smem[w];
+    return r;
+}
+__device__ __forceinline__ float block_max(float v, float* smem /*[8]*/) {
+    v = coat_warp_max(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) smem[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) r = fmaxf(r, smem[w]);
+    return r;
+}
+
+template <int FMT, int S, bool IEEE>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, int in_scale_dtype,
+                   const void* __restrict__ w, int w_dtype, __nv_bfloat16* __restrict__ y,
+                   __nv_bfloat16* __restrict__ s_y, float* __restrict__ rstd_out, unsigned int* __restrict__ amax_bits,
+                   int64_t M, int64_t N, int QB, float eps, int fp8_fmt_out) {
+    __shared__ float red[kNormThreads / 32];
+    const int64_t row = blockIdx.x;
+    const int64_t segs = N >> 4;
+    float v[S][16];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+            load_dequant16<FMT>(x, s_x, in_scale_dtype, row, c16, N, QB, v[k]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss += v[k][i] * v[k][i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[k][i] = 0.f;
+        }
+    }
+    const float var = qdiv<IEEE>(block_sum(ss, red), (float)N);
+    const float rstd = qdiv<IEEE>(1.0f, sqrt_approx(var + eps));
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+            float wv[16];
+            load_float16(w, w_dtype, c16 * 16, wv);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[k][i] = (v[k][i] * rstd) * wv[i];
+                amax = fmaxf(amax, fabsf(v[k][i]));
+            }
+            store_bf16x16(y + row * N + c16 * 16, v[k]);
+        }
+    }
+    amax = block_max(amax, red);
+    if (threadIdx.x == 0) {
+        const float fmax = fp8_fmt_out == COAT_E4M3 ? 448.0f : 57344.0f;
+        s_y[row] = __float2bfloat16_rn(qdiv<IEEE>(amax + kScaleMinThres, fmax));
+        rstd_out[row] = rstd;
+        if (amax_bits) atomicMax(amax_bits, __float_as_uint(amax));
+    }
+}
+
+// Backward: dx per row, and per-CTA partial sums of dW over the rows the CTA walks (rows cta, cta+P, ...),
+// accumulated in fp32 registers and written to partial[cta][N]; a second kernel sums the partials in
+// order.  No locks, no atomics: the result is deterministic (the reference serialises its partial sums
+// behind a spin lock in arrival order, func_rmsnorm.py:186-196).
+template <int FMT, int S>
+__global__ void __launch_bounds__(kNormThreads)
+rmsnorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, int in_scale_dtype,
+                   const void* __restrict__ dy, int dy_dtype, const void* __restrict__ w, int w_dtype,
+                   const float* __restrict__ rstd_in, __nv_bfloat16* __restrict__ dx, float* __restrict__ partial_dw,
+                   int64_t M, int64_t N, int QB) {
+    __shared__ float red[kNormThreads / 32];
+    const int64_t segs = N >> 4;
+    float acc[S][16];
+    float wv[S][16];
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { acc[k][i] = 0.f; wv[k][i] = 0.f; }
+        if (c16 < segs) load_float16(w, w_dtype, c16 * 16, wv[k]);
+    }
+    for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+        const float rstd = rstd_in[row];
+        float xhat[S][16], wdy[S][16];
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+            if (c16 < segs) {
+                float g[16];
+                load_dequant16<FMT>(x, s_x, in_scale_dtype, row, c16, N, QB, xhat[k]);
+                load_float16(dy, dy_dtype, row * N + c16 * 16, g);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    xhat[k][i] *= rstd;
+                    wdy[k][i] = wv[k][i] * g[i];
+                    dot += xhat[k][i] * wdy[k][i];
+                    acc[k][i] += g[i] * xhat[k][i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { xhat[k][i] = 0.f; wdy[k][i] = 0.f; }
+            }
+        }
+        const float c1 = block_sum(dot, red) / (float)N;
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+            if (c16 < segs) {
+                float o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = (wdy[k][i] - xhat[k][i] * c1) * rstd;
+                store_bf16x16(dx + row * N + c16 * 16, o);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+            float4* dst = reinterpret_cast<float4*>(partial_dw + (int64_t)blockIdx.x * N + c16 * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                dst[i] = make_float4(acc[k][4 * i], acc[k][4 * i + 1], acc[k][4 * i + 2], acc[k][4 * i + 3]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+rmsnorm_dw_reduce_kernel(const float* __restrict__ partial_dw, int n_partials, void* __restrict__ dw, int w_dtype,
+                         int64_t N) {
+    const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= N) return;
+    float s = 0.f;
+    for (int p = 0; p < n_partials; ++p) s += partial_dw[(int64_t)p * N + col];
+    if (w_dtype == COAT_F32) reinterpret_cast<float*>(dw)[col] = s;
+    else if (w_dtype == COAT_BF16) reinterpret_cast<__nv_bfloat16*>(dw)[col] = __float2bfloat16_rn(s);
+    else reinterpret_cast<__half*>(dw)[col] = __float2half_rn(s);
+}
+
+// =================================================================================================
+// host side
+// =================================================================================================
+bool fmt_ok(int f) { return f == COAT_E4M3 || f == COAT_E5M2; }
+bool fdt_ok(int d) { return d == COAT_F32 || d == COAT_BF16 || d == COAT_F16; }
+float fmt_max(int f) { return f == COAT_E4M3 ? 448.0f : 57344.0f; }
+
+int check_shape(int64_t M, int64_t N, int QB) {
+    if (M < 0 || N < 0) return COAT_E_BADARG;
+    if (!(QB == 16 || QB == 32 || QB == 64 || QB == 128) || N % QB != 0) return COAT_E_SHAPE;
+    return COAT_OK;
+}
+
+template <int OP>
+int launch_fused(const FusedArgs& a, int fmt_in, int fmt_out, int flags, cudaStream_t st) {
+    if (a.amax_bits && cudaMemsetAsync(a.amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
+    if (a.M == 0 || a.N == 0) return COAT_OK;
+    const int grid = straight_grid(a.M * (a.N / 16));
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+#define COAT_LAUNCH(FI, FO)                                                                                 \
+    do {                                                                                                    \
+        if (ieee) fused_elementwise_kernel<OP, FI, FO, true><<<grid, kStraightThreads, 0, st>>>(a);         \
+        else fused_elementwise_kernel<OP, FI, FO, false><<<grid, kStraightThreads, 0, st>>>(a);             \
+        return coat_launch_status();                                                                        \
+    } while (0)
+    // only the kernels that write FP8 codes depend on the output format at compile time
+    const bool writes_codes = OP == OP_SILU_FWD || OP == OP_ADD;
+    if (fmt_in == COAT_E4M3) {
+        if (writes_codes && fmt_out == COAT_E5M2) COAT_LAUNCH(COAT_E4M3, COAT_E5M2);
+        COAT_LAUNCH(COAT_E4M3, COAT_E4M3);
+    } else {
+        if (writes_codes && fmt_out == COAT_E4M3) COAT_LAUNCH(COAT_E5M2, COAT_E4M3);
+        COAT_LAUNCH(COAT_E5M2, COAT_E5M2);
+    }
+#undef COAT_LAUNCH
+}
+
+FusedArgs base_args(int64_t M, int64_t N, int QB, int in_scale_dtype, int out_scale_dtype, int fmt_for_scales) {
+    FusedArgs a = {};
+    a.M = M; a.N = N; a.QB = QB;
+    a.in_scale_dtype = in_scale_dtype; a.out_scale_dtype = out_scale_dtype;
+    a.g_dtype = COAT_BF16; a.h_dtype = COAT_BF16;
+    a.fp8_max = fmt_max(fmt_for_scales);
+    return a;
+}
+
+}  // namespace
+
+extern "C" int coat_fp8_silu_forward(const uint8_t* x, const void* s_x, uint8_t* y, void* s_y, int64_t M, int64_t N,
+                                     int QB, int fmt, int scale_dtype, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x || !s_x || !y || !s_y)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(scale_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, scale_dtype, scale_dtype, fmt);
+    a.x1 = x; a.s1 = s_x; a.y_q = y; a.s_y = s_y;
+    return launch_fused<OP_SILU_FWD>(a, fmt, fmt, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_act_backward(int gelu, const uint8_t* x, const void* s_x, const void* g, void* y_bf16,
+                                     void* s_y, unsigned int* amax_bits, int64_t M, int64_t N, int QB, int fmt_in,
+                                     int in_scale_dtype, int g_dtype, int fmt_out, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x || !s_x || !g || !y_bf16)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt_in) || !fmt_ok(fmt_out) || !fdt_ok(in_scale_dtype) || !fdt_ok(g_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, in_scale_dtype, COAT_BF16, fmt_out);
+    a.x1 = x; a.s1 = s_x; a.g = g; a.g_dtype = g_dtype;
+    a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y_bf16); a.s_y = s_y; a.amax_bits = amax_bits;
+    return gelu ? launch_fused<OP_GELU_BWD>(a, fmt_in, fmt_out, flags, (cudaStream_t)stream)
+                : launch_fused<OP_SILU_BWD>(a, fmt_in, fmt_out, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_gelu_forward(const uint8_t* x, const void* s_x, void* y_bf16, void* s_y,
+                                     unsigned int* amax_bits, int64_t M, int64_t N, int QB, int fmt, int scale_dtype,
+                                     int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x || !s_x || !y_bf16)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(scale_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, scale_dtype, scale_dtype, fmt);
+    a.x1 = x; a.s1 = s_x; a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y_bf16); a.s_y = s_y; a.amax_bits = amax_bits;
+    return launch_fused<OP_GELU_FWD>(a, fmt, fmt, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_mul_forward(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                                    void* y_bf16, void* s_y, unsigned int* amax_bits, int64_t M, int64_t N, int QB,
+                                    int fmt, int scale_dtype, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x1 || !s_x1 || !x2 || !s_x2 || !y_bf16)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(scale_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, scale_dtype, scale_dtype, fmt);
+    a.x1 = x1; a.s1 = s_x1; a.x2 = x2; a.s2 = s_x2;
+    a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y_bf16); a.s_y = s_y; a.amax_bits = amax_bits;
+    return launch_fused<OP_MUL_FWD>(a, fmt, fmt, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                                     const void* g, void* y1_bf16, void* y2_bf16, void* s_y2, unsigned int* amax_bits,
+                                     int64_t M, int64_t N, int QB, int fmt_in, int in_scale_dtype, int g_dtype,
+                                     int fmt_out, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x1 || !s_x1 || !x2 || !s_x2 || !g || !y1_bf16 || !y2_bf16)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt_in) || !fmt_ok(fmt_out) || !fdt_ok(in_scale_dtype) || !fdt_ok(g_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, in_scale_dtype, COAT_BF16, fmt_out);
+    a.x1 = x1; a.s1 = s_x1; a.x2 = x2; a.s2 = s_x2; a.g = g; a.g_dtype = g_dtype;
+    a.y1_bf16 = reinterpret_cast<__nv_bfloat16*>(y1_bf16); a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y2_bf16);
+    a.s_y = s_y2; a.amax_bits = amax_bits;
+    return launch_fused<OP_MUL_BWD>(a, fmt_in, fmt_out, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_add(const void* x1, const void* x2, void* y_bf16, uint8_t* y_q, void* s_y,
+                            unsigned int* amax_bits, int64_t M, int64_t N, int QB, int x1_dtype, int x2_dtype,
+                            int fmt_out, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M && N && (!x1 || !x2 || !y_bf16 || !s_y)) return COAT_E_BADARG;
+    if (!fmt_ok(fmt_out) || !fdt_ok(x1_dtype) || !fdt_ok(x2_dtype)) return COAT_E_BADARG;
+    FusedArgs a = base_args(M, N, QB, COAT_BF16, COAT_BF16, fmt_out);
+    a.g = x1; a.h = x2; a.g_dtype = x1_dtype; a.h_dtype = x2_dtype;
+    a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y_bf16); a.y_q = y_q; a.s_y = s_y; a.amax_bits = amax_bits;
+    return launch_fused<OP_ADD>(a, fmt_out, fmt_out, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_rmsnorm_forward(const uint8_t* x, const void* s_x, const void* w, void* y_bf16,
+                                        void* s_y_rows_bf16, float* rstd, unsigned int* amax_bits, int64_t M,
+                                        int64_t N, int QB, float eps, int fmt, int in_scale_dtype, int w_dtype,
+                                        int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (amax_bits && cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !s_x || !w || !y_bf16 || !s_y_rows_bf16 || !rstd) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(in_scale_dtype) || !fdt_ok(w_dtype)) return COAT_E_BADARG;
+    if (N > 16384) return COAT_E_TOOBIG;
+    const int S = N <= 4096 ? 1 : (N <= 8192 ? 2 : 4);
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(y_bf16);
+    __nv_bfloat16* sy = reinterpret_cast<__nv_bfloat16*>(s_y_rows_bf16);
+#define COAT_RMS(F, SS)                                                                                          \
+    do {                                                                                                         \
+        if (ieee) rmsnorm_fwd_kernel<F, SS, true><<<(unsigned)M, kNormThreads, 0, st>>>(                          \
+            x, s_x, in_scale_dtype, w, w_dtype, y, sy, rstd, amax_bits, M, N, QB, eps, fmt);                     \
+        else rmsnorm_fwd_kernel<F, SS, false><<<(unsigned)M, kNormThreads, 0, st>>>(                              \
+            x, s_x, in_scale_dtype, w, w_dtype, y, sy, rstd, amax_bits, M, N, QB, eps, fmt);                     \
+    } while (0)
+    if (fmt == COAT_E4M3) { if (S == 1) COAT_RMS(COAT_E4M3, 1); else if (S == 2) COAT_RMS(COAT_E4M3, 2); else COAT_RMS(COAT_E4M3, 4); }
+    else { if (S == 1) COAT_RMS(COAT_E5M2, 1); else if (S == 2) COAT_RMS(COAT_E5M2, 2); else COAT_RMS(COAT_E5M2, 4); }
+#undef COAT_RMS
+    return coat_launch_status();
+}
+
+extern "C" int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
+                                         const float* rstd, void* dx_bf16, float* partial_dw, int n_partials,
+                                         void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
+                                         int dy_dtype, int w_dtype, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !s_x || !dy || !w || !rstd || !dx_bf16 || !partial_dw || !dw || n_partials < 1) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(in_scale_dtype) || !fdt_ok(dy_dtype) || !fdt_ok(w_dtype)) return COAT_E_BADARG;
+    if (N > 16384) return COAT_E_TOOBIG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = N <= 4096 ? 1 : (N <= 8192 ? 2 : 4);
+    const unsigned grid = (unsigned)(n_partials < M ? n_partials : M);
+    __nv_bfloat16* dx = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
+#define COAT_RMSB(F, SS) rmsnorm_bwd_kernel<F, SS><<<grid, kNormThreads, 0, st>>>(x, s_x, in_scale_dtype, dy, dy_dtype, w, w_dtype, rstd, dx, partial_dw, M, N, QB)
+    if (fmt == COAT_E4M3) { if (S == 1) COAT_RMSB(COAT_E4M3, 1); else if (S == 2) COAT_RMSB(COAT_E4M3, 2); else COAT_RMSB(COAT_E4M3, 4); }
+    else { if (S == 1) COAT_RMSB(COAT_E5M2, 1); else if (S == 2) COAT_RMSB(COAT_E5M2, 2); else COAT_RMSB(COAT_E5M2, 4); }
+#undef COAT_RMSB
+    rmsnorm_dw_reduce_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(partial_dw, (int)grid, dw, w_dtype, N);
+    return coat_launch_status();
+}

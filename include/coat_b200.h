@@ -177,6 +177,67 @@ int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, 
                                        int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
                                        int flags, void* stream);
 
+/* =========================== fused quantize-on-save operators =================================
+ * Inputs x, x1, x2 are M x N code matrices quantised in 1xQB groups with scales s_* of shape [M, N/QB];
+ * g is a floating (bf16 by default) M x N matrix.  Where an amax_bits pointer is given, the call zeroes
+ * that 4-byte word on the stream and leaves the bit pattern of max|result| (of the fp32 values) in it,
+ * which coat_fp8_division turns into the per-tensor scale the reference gets from `s_y.max()`.
+ */
+
+/* y = 1xQB FP8 of silu(x).  Replaces fp8_silu_forward (coat/activation/real_quantization/silu_fwd.py:152-198,
+ * kernel :47-149). */
+int coat_fp8_silu_forward(const uint8_t* x, const void* s_x, uint8_t* y, void* s_y, int64_t M, int64_t N,
+                          int QB, int fmt, int scale_dtype, int flags, void* stream);
+
+/* y = bf16( act'(x) * g ), group scales (bf16) for FP8 format fmt_out, tensor amax.  gelu = 0: SiLU
+ * (fp8_silu_backward, silu_bwd.py:170-238, kernel :47-167); gelu = 1: erf-GELU (fp8_gelu_backward,
+ * gelu_bwd.py:173-230, kernel :47-170). */
+int coat_fp8_act_backward(int gelu, const uint8_t* x, const void* s_x, const void* g, void* y_bf16,
+                          void* s_y, unsigned int* amax_bits, int64_t M, int64_t N, int QB, int fmt_in,
+                          int in_scale_dtype, int g_dtype, int fmt_out, int flags, void* stream);
+
+/* y = bf16(gelu(x)), group scales, tensor amax.  Replaces the kernel of fp8_gelu_forward
+ * (gelu_fwd.py:152-203, kernel :47-149). */
+int coat_fp8_gelu_forward(const uint8_t* x, const void* s_x, void* y_bf16, void* s_y,
+                          unsigned int* amax_bits, int64_t M, int64_t N, int QB, int fmt, int scale_dtype,
+                          int flags, void* stream);
+
+/* y = bf16((x1*s1) * (x2*s2)), group scales, tensor amax.  Replaces the kernel of fp8_mul_forward
+ * (mul_fwd.py:191-254, kernel :51-188). */
+int coat_fp8_mul_forward(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                         void* y_bf16, void* s_y, unsigned int* amax_bits, int64_t M, int64_t N, int QB,
+                         int fmt, int scale_dtype, int flags, void* stream);
+
+/* y1 = bf16(g * x2), y2 = bf16(g * x1) with group scales (bf16) and tensor amax of y2.  Replaces the kernel
+ * of fp8_mul_backward (mul_bwd.py:221-315, kernel :49-218). */
+int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                          const void* g, void* y1_bf16, void* y2_bf16, void* s_y2, unsigned int* amax_bits,
+                          int64_t M, int64_t N, int QB, int fmt_in, int in_scale_dtype, int g_dtype,
+                          int fmt_out, int flags, void* stream);
+
+/* y = bf16(x1 + x2); if y_q != NULL also its 1xQB FP8 copy; group scales (bf16); optional tensor amax.
+ * Replaces fp8_add_Ifp_Ifp_Ofp_Og16 (add_fwd.py:162-213, kernel :46-159) and the kernel of
+ * fp8_add_Ifp_Ifp_Ofp_Opt (add_bwd.py:147-200, kernel :48-144). */
+int coat_fp8_add(const void* x1, const void* x2, void* y_bf16, uint8_t* y_q, void* s_y,
+                 unsigned int* amax_bits, int64_t M, int64_t N, int QB, int x1_dtype, int x2_dtype,
+                 int fmt_out, int flags, void* stream);
+
+/* RMSNorm of a 1xQB-quantised input: y = bf16(x * rstd * w), one bf16 scale per row, rstd (fp32) per row,
+ * tensor amax.  N <= 16384.  Replaces the kernel of fp8_rmsnorm_forward (func_rmsnorm.py:223-278,
+ * kernel :54-111). */
+int coat_fp8_rmsnorm_forward(const uint8_t* x, const void* s_x, const void* w, void* y_bf16,
+                             void* s_y_rows_bf16, float* rstd, unsigned int* amax_bits, int64_t M,
+                             int64_t N, int QB, float eps, int fmt, int in_scale_dtype, int w_dtype,
+                             int flags, void* stream);
+
+/* RMSNorm backward: dx (bf16) and dw (w_dtype).  partial_dw is caller-provided scratch of n_partials x N
+ * fp32 (n_partials CTAs each sum their rows in registers, a second kernel adds the partials in order:
+ * deterministic, no locks).  Replaces fp8_rmsnorm_backward (func_rmsnorm.py:281-335, kernels :121-220). */
+int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
+                              const float* rstd, void* dx_bf16, float* partial_dw, int n_partials,
+                              void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
+                              int dy_dtype, int w_dtype, void* stream);
+
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
  * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded
