@@ -16,3 +16,4 @@ from .mul_bwd import fp8_mul_backward  # noqa: F401
 from .mul_fwd import fp8_mul_forward  # noqa: F401
 from .silu_bwd import fp8_silu_backward  # noqa: F401
 from .silu_fwd import fp8_silu_forward  # noqa: F401
+from .linear import fp8_linear_backward, fp8_linear_forward  # noqa: F401

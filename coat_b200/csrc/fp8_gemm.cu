@@ -1,0 +1,337 @@
+// FP8 GEMM for sm_100a on the 5th-generation tensor cores: C = (A * B^T) * (s_a * s_b) [+ bias], with A [M,K]
+// and B [N,K] both K-major FP8 (E4M3 or E5M2, chosen per operand), fp32 accumulation in tensor memory, and a
+// bf16 result or a fused 1xQB FP8 quantisation of the result with bf16 group scales.
+//
+// It replaces the reference's Triton kernel _fp8matmul_kernel (coat/activation/real_quantization/linear.py:61-169)
+// behind fp8matmul / fp8_linear_forward / fp8_linear_backward (:172-302).  The reference always hands that kernel
+// a `.t()` view of a contiguous matrix as B (linear.py:257, :285-286), which is why both operands are K-major
+// here for forward (X, W), dgrad (G, W^T) and wgrad (G^T, X^T) alike.
+//
+// Structure (one CTA per 128 x 256 output tile, 192 threads):
+//   warp 0, one lane   TMA producer: cp.async.bulk.tensor (no multicast) of a 128x128 B A-tile and a 256x128 B B-tile
+//                      per pipeline stage into 128-byte-swizzled shared memory, completion on the stage's mbarrier
+//   warp 1             allocates 256 columns of tensor memory; one lane issues tcgen05.mma.kind::f8f6f4
+//                      (M=128, N=256, K=32 per instruction, 4 per stage) and commits each stage back to the producer
+//   warps 2-5          epilogue: tcgen05.ld of the accumulator (lane quarter = warp index mod 4, 32 columns at a
+//                      time, so one thread holds 32 consecutive columns of one row), scaling, bias, bf16 or 1xQB FP8
+//                      conversion and 64-byte row-segment stores
+// Every wait on an mbarrier is bounded; a wait that runs out sets a device status word, and the CTA still goes
+// through its tear-down (tensor memory is released) before it returns.
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 128;       // CTA tile; kBK bytes of K per stage (= one 128B swizzle row)
+constexpr int kStages = 4;
+constexpr int kUmmaK = 32;                            // K per tcgen05.mma for 8-bit operands
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 256;
+constexpr uint32_t kStageBytesA = kBM * kBK, kStageBytesB = kBN * kBK;
+constexpr uint32_t kStageBytes = kStageBytesA + kStageBytesB;
+constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*alignment slack*/ + 256 /*barriers*/;
+constexpr int kWaitLimit = 1 << 22;
+
+__device__ int g_gemm_device_status = 0;
+
+__device__ __forceinline__ uint32_t s2u(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s2u(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s2u(bar)), "r"(bytes) : "memory");
+}
+// bounded wait for the phase with the given parity; false = gave up
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < kWaitLimit; ++i) {
+        uint32_t done;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done) : "r"(s2u(bar)), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 ::"r"(s2u(dst)), "l"(map), "r"(s2u(bar)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 64-bit shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows 128 B apart, 8-row groups
+// 1024 B apart (stride byte offset), descriptor version 1 (Blackwell)
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr & 0x3ffff) >> 4);          // start address, bits [0,14)
+    d |= (uint64_t)1 << 16;                               // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;                     // stride byte offset, bits [32,46)
+    d |= (uint64_t)1 << 46;                               // version
+    d |= (uint64_t)2 << 61;                               // layout type: SWIZZLE_128B
+    return d;
+}
+// 32-bit instruction descriptor for kind::f8f6f4: fp32 accumulator, per-operand FP8 format, both operands K-major
+__host__ __device__ constexpr uint32_t make_idesc(int fmt_a, int fmt_b, int m, int n) {
+    return (1u << 4) | ((uint32_t)fmt_a << 7) | ((uint32_t)fmt_b << 10) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }"
+                 ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s2u(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmEpilogue {
+    void* c;                 // bf16 [M,N] or FP8 codes [M,N]
+    void* scale_c;           // bf16 [M, N/QB] when quantising
+    const void* scale_a;     // device scalars
+    const void* scale_b;
+    const void* bias;        // [N] or null
+    int scale_dtype, bias_dtype;
+    int quantize;            // 0: bf16 result, 1: 1xQB FP8 + scales
+    int QB;
+    int fmt_c;
+    int ieee_div;
+    int M, N, K;
+};
+
+__device__ __forceinline__ float ld_scalar(const void* p, int dtype, int64_t i = 0) {
+    if (dtype == COAT_F32) return reinterpret_cast<const float*>(p)[i];
+    if (dtype == COAT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+template <int FMT_C>
+__device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, int col0, float (&v)[32]) {
+    // v: 32 consecutive columns col0.. of one row, already scaled (and biased)
+    if (row >= e.M || col0 >= e.N) return;
+    const bool full = col0 + 32 <= e.N;
+    if (!e.quantize) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.c) + (int64_t)row * e.N + col0;
+        if (full && ((e.N & 7) == 0)) {
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                o[i] = (uint32_t)coat_float_to_bf16_bits(v[2 * i]) | ((uint32_t)coat_float_to_bf16_bits(v[2 * i + 1]) << 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                reinterpret_cast<uint4*>(dst)[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        } else {
+            for (int i = 0; i < 32 && col0 + i < e.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+        }
+    } else {
+        // fused 1xQB quantisation (linear.py:139-164): QB is 16 or 32, N a multiple of QB, so groups never
+        // straddle the 32 columns a thread holds
+        const float fmax = CoatFp8Max<FMT_C>::value;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(e.c) + (int64_t)row * e.N + col0;
+        __nv_bfloat16* sdst = reinterpret_cast<__nv_bfloat16*>(e.scale_c) + (int64_t)row * (e.N / e.QB) + col0 / e.QB;
+        const int groups = 32 / e.QB;
+        for (int gi = 0; gi < groups; ++gi) {
+            if (col0 + gi * e.QB >= e.N) break;
+            float amax = 0.f;
+            for (int i = 0; i < e.QB; ++i) amax = fmaxf(amax, fabsf(v[gi * e.QB + i]));
+            const float num = amax + 1e-10f;
+            const float scale = e.ieee_div ? __fdiv_rn(num, fmax) : coat_div_full(num, fmax);
+            sdst[gi] = __float2bfloat16_rn(scale);
+            for (int i = 0; i < e.QB; i += 4) {
+                float q[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float x = v[gi * e.QB + i + j];
+                    q[j] = e.ieee_div ? __fdiv_rn(x, scale) : coat_div_full(x, scale);
+                }
+                *reinterpret_cast<uint32_t*>(dst + gi * e.QB + i) = coat_float4_to_fp8x4<FMT_C>(q[0], q[1], q[2], q[3]);
+            }
+        }
+    }
+}
+
+template <int FMT_C>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint32_t idesc,
+                GemmEpilogue e) {
+    extern __shared__ uint8_t smem_raw[];
+    // 128-byte-swizzled TMA destinations and UMMA operands need 1024-byte alignment
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + (size_t)kStages * kStageBytesA;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);
+    uint64_t* full_bar = bars;                 // [kStages] TMA -> MMA
+    uint64_t* empty_bar = bars + kStages;      // [kStages] MMA -> TMA
+    uint64_t* acc_bar = bars + 2 * kStages;    // accumulator complete -> epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_m = blockIdx.y, tile_n = blockIdx.x;
+    const int k_blocks = (e.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        mbar_init(acc_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {   // whole warp: allocate the accumulator columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s2u(tmem_slot)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            for (int kb = 0; kb < k_blocks && ok; ++kb) {
+                const int s = kb % kStages;
+                if (kb >= kStages) ok = mbar_wait(&empty_bar[s], ((kb / kStages) - 1) & 1);
+                if (!ok) break;
+                mbar_expect_tx(&full_bar[s], kStageBytes);
+                tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * kBM, &full_bar[s]);
+                tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, tile_n * kBN, &full_bar[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            for (int kb = 0; kb < k_blocks && ok; ++kb) {
+                const int s = kb % kStages;
+                ok = mbar_wait(&full_bar[s], (kb / kStages) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t da = make_smem_desc(s2u(smem_a + (size_t)s * kStageBytesA));
+                const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kStageBytesB));
+#pragma unroll
+                for (int k = 0; k < kBK / kUmmaK; ++k) {
+                    // advancing K inside the 128-byte swizzle row: +32 bytes = +2 in the (>>4) address field
+                    umma_f8(tmem_base, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc,
+                            (kb | k) != 0);
+                }
+                umma_commit(&empty_bar[s]);      // frees the stage once these MMAs have read it
+            }
+            umma_commit(acc_bar);                 // accumulator final once everything issued has completed
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        ok = __all_sync(COAT_FULL_MASK, mbar_wait(acc_bar, 0));   // warp-uniform: tcgen05.ld is warp-collective
+        tc_fence_after();
+        if (ok) {
+            const int quarter = warp & 3;                         // TMEM lanes this warp may read
+            const int row = tile_m * kBM + quarter * 32 + lane;
+            const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), r);
+                float v[32];
+                const int col0 = tile_n * kBN + c * 32;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    v[i] = __uint_as_float(r[i]) * sab;
+                    if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
+                }
+                epilogue_store<FMT_C>(e, row, col0, v);
+            }
+        }
+    }
+    if (!ok) g_gemm_device_status = COAT_E_TIMEOUT;
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// K-major byte matrix [rows, K] with row pitch K; box = 128 bytes of K x box_rows rows, 128-byte swizzle
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return COAT_E_DEVICE;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? COAT_OK : COAT_E_BADARG;
+}
+
+}  // namespace
+
+extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* scale_c, const void* scale_a,
+                             const void* scale_b, const void* bias, int64_t M, int64_t N, int64_t K, int fmt_a,
+                             int fmt_b, int scale_dtype, int bias_dtype, int output_quantize, int QB, int flags,
+                             void* stream) {
+    if (M < 0 || N < 0 || K < 0) return COAT_E_BADARG;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!a || !b || !c || !scale_a || !scale_b || (output_quantize && !scale_c)) return COAT_E_BADARG;
+    if ((fmt_a != COAT_E4M3 && fmt_a != COAT_E5M2) || (fmt_b != COAT_E4M3 && fmt_b != COAT_E5M2)) return COAT_E_BADARG;
+    if (K == 0 || K % 16 != 0) return COAT_E_SHAPE;            // TMA row pitch must be a multiple of 16 bytes
+    if (!coat_aligned(a, 16) || !coat_aligned(b, 16) || !coat_aligned(c, 16)) return COAT_E_ALIGN;
+    if (output_quantize && ((QB != 16 && QB != 32) || N % QB != 0)) return COAT_E_SHAPE;
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return COAT_E_TOOBIG;
+    CUtensorMap map_a, map_b;
+    if (int rc = make_map(&map_a, a, M, K, kBM)) return rc;
+    if (int rc = make_map(&map_b, b, N, K, kBN)) return rc;
+    GemmEpilogue e = {};
+    e.c = c; e.scale_c = scale_c; e.scale_a = scale_a; e.scale_b = scale_b; e.bias = bias;
+    e.scale_dtype = scale_dtype; e.bias_dtype = bias_dtype; e.quantize = output_quantize; e.QB = QB;
+    e.fmt_c = fmt_a; e.ieee_div = (flags & COAT_QUANT_IEEE_DIV) ? 1 : 0;
+    e.M = (int)M; e.N = (int)N; e.K = (int)K;
+    const uint32_t idesc = make_idesc(fmt_a, fmt_b, kBM, kBN);
+    const dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+    cudaStream_t st = (cudaStream_t)stream;
+    if (fmt_a == COAT_E4M3) {
+        if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
+            return COAT_E_LAUNCH;
+        fp8_gemm_kernel<COAT_E4M3><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e);
+    } else {
+        if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E5M2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
+            return COAT_E_LAUNCH;
+        fp8_gemm_kernel<COAT_E5M2><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e);
+    }
+    return coat_launch_status();
+}
+
+// Synchronises, returns and clears the GEMM's device status word (COAT_E_TIMEOUT if a bounded wait ran out).
+extern "C" int coat_fp8_gemm_device_status(void) {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_device_status, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    if (v != 0 && cudaMemcpyToSymbol(g_gemm_device_status, &zero, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    return v;
+}

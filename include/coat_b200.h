@@ -238,6 +238,23 @@ int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy,
                               void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
                               int dy_dtype, int w_dtype, void* stream);
 
+/* =========================== FP8 GEMM ==========================================================
+ * C[M,N] = (A[M,K] * B[N,K]^T) * (float(*scale_a) * float(*scale_b)) (+ bias[N]), A and B FP8 codes, both with
+ * K contiguous (row pitch K bytes, K a multiple of 16, 16-byte aligned bases), formats fmt_a / fmt_b chosen per
+ * operand (forward E4M3 x E4M3, dgrad / wgrad E5M2 x E4M3).  fp32 accumulation on the tcgen05 tensor cores.
+ * output_quantize == 0: C is bf16 [M,N].  output_quantize == 1: C is FP8 (format fmt_a) quantised in 1xQB
+ * groups (QB 16 or 32, N a multiple of QB) with bf16 scales scale_c[M, N/QB].  scale_a / scale_b are device
+ * scalars of scale_dtype, bias (may be NULL) is of bias_dtype.
+ * Replaces fp8matmul (coat/activation/real_quantization/linear.py:172-250, kernel _fp8matmul_kernel :61-169),
+ * which fp8_linear_forward (:253-258) and fp8_linear_backward (:272-302) call with B passed as a `.t()` view.
+ * coat_fp8_gemm_device_status synchronises, returns and clears the kernel's status word (COAT_E_TIMEOUT if a
+ * bounded wait on a pipeline barrier ever ran out). */
+int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* scale_c, const void* scale_a,
+                  const void* scale_b, const void* bias, int64_t M, int64_t N, int64_t K, int fmt_a,
+                  int fmt_b, int scale_dtype, int bias_dtype, int output_quantize, int QB, int flags,
+                  void* stream);
+int coat_fp8_gemm_device_status(void);
+
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
  * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded

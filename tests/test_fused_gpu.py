@@ -41,7 +41,7 @@ def frac_equal(a, b):
 def bf16_ulps(a, b):
     """|a-b| in units of the bf16 spacing at |b| (inputs bf16)."""
     a, b = a.detach().cpu().float(), b.detach().cpu().float()
-    ulp = torch.maximum(b.abs(), torch.tensor(1e-30)) * 2.0 ** -8
+    ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(b.abs(), torch.tensor(1e-30)))) - 7)
     return ((a - b).abs() / ulp)
 
 
