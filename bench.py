@@ -285,6 +285,69 @@ def quantizer_extras(torch, device, peak):
     return out
 
 
+def gemm_extras(torch, device, iters=10):
+    """TFLOP/s of the FP8 GEMM on BASELINE.json's Llama-2-7B MLP shape (8192 tokens, 4096 -> 11008): forward
+    (E4M3 x E4M3), dgrad and wgrad (E5M2 x E4M3), 2*M*N*K flops each = 0.7388 TFLOP, CUDA-event time of the
+    C-ABI call on preallocated outputs.  Operands (45-90 MB each, > 200 MB per GEMM with the output) exceed
+    L2 together.  Fractions are against 2x the measured bf16 GEMM peak of this pool (no FP8 peak was measured
+    by the driver) and against the nominal 4500 dense FP8 TFLOP/s."""
+    from coat_b200 import _lib
+    L = _lib.lib()
+    T, H, I = 8192, 4096, 11008
+    gen = torch.Generator(device=device).manual_seed(2)
+
+    def codes(r, c, dtype, scale):
+        return (torch.randn(r, c, generator=gen, device=device) * scale).to(dtype)
+
+    x, x_t = codes(T, H, torch.float8_e4m3fn, 50), codes(H, T, torch.float8_e4m3fn, 50)
+    w, w_t = codes(I, H, torch.float8_e4m3fn, 50), codes(H, I, torch.float8_e4m3fn, 50)
+    g, g_t = codes(T, I, torch.float8_e5m2, 500), codes(I, T, torch.float8_e5m2, 500)
+    s = torch.tensor(0.01, dtype=torch.bfloat16, device=device)
+    bf16_peak = 1651.6
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            bf16_peak = float(json.load(f).get("bf16_tflops", bf16_peak))
+    out = {}
+    for name, a, bm in (("forward_e4m3xe4m3", x, w), ("dgrad_e5m2xe4m3", g, w_t), ("wgrad_e5m2xe4m3", g_t, x_t)):
+        M, K = a.shape
+        N = bm.shape[0]
+        c = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+
+        def call():
+            return L.coat_fp8_gemm(a.data_ptr(), bm.data_ptr(), c.data_ptr(), None, s.data_ptr(), s.data_ptr(), None,
+                                   M, N, K, _lib.fp8_enum_of(a), _lib.fp8_enum_of(bm), _lib.BF16, _lib.BF16, 0, 16, 0,
+                                   _lib.stream_ptr(device))
+        for _ in range(3):
+            _lib.check(call(), name)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            call()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / iters
+        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        out[name] = {"M": M, "N": N, "K": K, "us": ms * 1e3, "TFLOP/s": tf, "frac_of_2x_measured_bf16": tf / (2 * bf16_peak),
+                     "frac_of_nominal_fp8": tf / 4500.0}
+    out["device_status"] = L.coat_fp8_gemm_device_status()
+    return out
+
+
+def run_kernel_workload(args):
+    """`--workload quantizers|gemm`: only those kernels, for profiling captures and quick checks."""
+    import torch
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    peak, kind = measured_peaks()
+    if args.workload == "quantizers":
+        extras = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
+    else:
+        extras = {"fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device, iters=max(1, args.steps))}
+    print(json.dumps({"metric": "extras only", "config": {"workload": args.workload}, "extras": extras}), flush=True)
+
+
 def run_gpu_arm(args):
     import torch
     import torch.distributed as dist
@@ -399,7 +462,8 @@ def run_gpu_arm(args):
         if not args.kernel_only and args.workload == "llama2-7b":
             del opt, grads, tables
             torch.cuda.empty_cache()
-            line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
+            line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
+                              "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device)}
         if cpu_v is not None:
             line["cpu_baseline"] = {
                 "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
@@ -416,12 +480,14 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1"],
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload in ("quantizers", "gemm"):
+        run_kernel_workload(args)
     else:
         run_gpu_arm(args)
 

@@ -7,10 +7,11 @@
 // a `.t()` view of a contiguous matrix as B (linear.py:257, :285-286), which is why both operands are K-major
 // here for forward (X, W), dgrad (G, W^T) and wgrad (G^T, X^T) alike.
 //
-// Structure (one CTA per 128 x 256 output tile, 192 threads):
+// Structure (persistent CTAs of 192 threads, one per SM, each walking 128 x 256 output tiles):
 //   warp 0, one lane   TMA producer: cp.async.bulk.tensor (no multicast) of a 128x128 B A-tile and a 256x128 B B-tile
 //                      per pipeline stage into 128-byte-swizzled shared memory, completion on the stage's mbarrier
-//   warp 1             allocates 256 columns of tensor memory; one lane issues tcgen05.mma.kind::f8f6f4
+//   warp 1             allocates all 512 columns of tensor memory (two accumulators, so the epilogue of one tile
+//                      overlaps the main loop of the next); one lane issues tcgen05.mma.kind::f8f6f4
 //                      (M=128, N=256, K=32 per instruction, 4 per stage) and commits each stage back to the producer
 //   warps 2-5          epilogue: tcgen05.ld of the accumulator (lane quarter = warp index mod 4, 32 columns at a
 //                      time, so one thread holds 32 consecutive columns of one row), scaling, bias, bf16 or 1xQB FP8
@@ -28,11 +29,11 @@ constexpr int kBM = 128, kBN = 256, kBK = 128;       // CTA tile; kBK bytes of K
 constexpr int kStages = 4;
 constexpr int kUmmaK = 32;                            // K per tcgen05.mma for 8-bit operands
 constexpr int kGemmThreads = 192;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 512;                        // two 128 x 256 fp32 accumulators
 constexpr uint32_t kStageBytesA = kBM * kBK, kStageBytesB = kBN * kBK;
 constexpr uint32_t kStageBytes = kStageBytesA + kStageBytesB;
 constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*alignment slack*/ + 256 /*barriers*/;
-constexpr int kWaitLimit = 1 << 22;
+constexpr int kWaitLimit = 1 << 20;
 
 __device__ int g_gemm_device_status = 0;
 
@@ -45,8 +46,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s2u(bar)), "r"(bytes) : "memory");
 }
 // bounded wait for the phase with the given parity; false = gave up
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag) {
     for (int i = 0; i < kWaitLimit; ++i) {
+        if ((i & 63) == 63 && *abort_flag) return false;   // another role of this CTA has given up
         uint32_t done;
         asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                      : "=r"(done) : "r"(s2u(bar)), "r"(parity) : "memory");
@@ -162,31 +164,38 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, i
     }
 }
 
+// Persistent kernel: gridDim.x CTAs (one per SM) walk the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...
+// (tile t -> m-tile t % tiles_m, n-tile t / tiles_m, so that the CTAs running at the same time share B tiles
+// and cover all of A).  Tensor memory holds two 128 x 256 fp32 accumulators: while the epilogue warps drain
+// one, the MMA warp already fills the other with the next tile.
 template <int FMT_C>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint32_t idesc,
-                GemmEpilogue e) {
+                GemmEpilogue e, int tiles_m, int tiles_n) {
     extern __shared__ uint8_t smem_raw[];
     // 128-byte-swizzled TMA destinations and UMMA operands need 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + (size_t)kStages * kStageBytesA;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);
-    uint64_t* full_bar = bars;                 // [kStages] TMA -> MMA
-    uint64_t* empty_bar = bars + kStages;      // [kStages] MMA -> TMA
-    uint64_t* acc_bar = bars + 2 * kStages;    // accumulator complete -> epilogue
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+    uint64_t* full_bar = bars;                      // [kStages] TMA -> MMA
+    uint64_t* empty_bar = bars + kStages;           // [kStages] MMA -> TMA
+    uint64_t* acc_full = bars + 2 * kStages;        // [2] accumulator complete -> epilogue
+    uint64_t* acc_empty = bars + 2 * kStages + 2;   // [2] accumulator drained -> MMA (4 epilogue warps arrive)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 4);
+    volatile uint32_t* abort_flag = tmem_slot + 1;  // set by whoever gives up waiting; makes every other wait bail out
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_m = blockIdx.y, tile_n = blockIdx.x;
     const int k_blocks = (e.K + kBK - 1) / kBK;
+    const int n_tiles = tiles_m * tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-        mbar_init(acc_bar, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+        *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {   // whole warp: allocate the accumulator columns
+    if (warp == 1) {   // whole warp: allocate both accumulators (all 512 columns)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s2u(tmem_slot)), "r"(kTmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -199,47 +208,63 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            for (int kb = 0; kb < k_blocks && ok; ++kb) {
-                const int s = kb % kStages;
-                if (kb >= kStages) ok = mbar_wait(&empty_bar[s], ((kb / kStages) - 1) & 1);
-                if (!ok) break;
-                mbar_expect_tx(&full_bar[s], kStageBytes);
-                tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * kBM, &full_bar[s]);
-                tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, tile_n * kBN, &full_bar[s]);
+            int it = 0;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages) ok = mbar_wait(&empty_bar[s], ((it / kStages) - 1) & 1, abort_flag);
+                    if (!ok) break;
+                    mbar_expect_tx(&full_bar[s], kStageBytes);
+                    tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * kBM, &full_bar[s]);
+                    tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, tile_n * kBN, &full_bar[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            for (int kb = 0; kb < k_blocks && ok; ++kb) {
-                const int s = kb % kStages;
-                ok = mbar_wait(&full_bar[s], (kb / kStages) & 1);
+            int it = 0, local = 0;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
+                const int buf = local & 1, use = local >> 1;
+                if (use >= 1) ok = mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_flag);   // epilogue has drained it
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t da = make_smem_desc(s2u(smem_a + (size_t)s * kStageBytesA));
-                const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kStageBytesB));
+                const uint32_t tmem_d = tmem_base + (uint32_t)(buf * kBN);
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    ok = mbar_wait(&full_bar[s], (it / kStages) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t da = make_smem_desc(s2u(smem_a + (size_t)s * kStageBytesA));
+                    const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kStageBytesB));
 #pragma unroll
-                for (int k = 0; k < kBK / kUmmaK; ++k) {
-                    // advancing K inside the 128-byte swizzle row: +32 bytes = +2 in the (>>4) address field
-                    umma_f8(tmem_base, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc,
-                            (kb | k) != 0);
+                    for (int k = 0; k < kBK / kUmmaK; ++k) {
+                        // advancing K inside the 128-byte swizzle row: +32 bytes = +2 in the (>>4) address field
+                        umma_f8(tmem_d, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc,
+                                (kb | k) != 0);
+                    }
+                    umma_commit(&empty_bar[s]);      // frees the stage once these MMAs have read it
                 }
-                umma_commit(&empty_bar[s]);      // frees the stage once these MMAs have read it
+                if (ok) umma_commit(&acc_full[buf]);  // this tile's accumulator is final once all of the above completed
             }
-            umma_commit(acc_bar);                 // accumulator final once everything issued has completed
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
-        ok = __all_sync(COAT_FULL_MASK, mbar_wait(acc_bar, 0));   // warp-uniform: tcgen05.ld is warp-collective
-        tc_fence_after();
-        if (ok) {
-            const int quarter = warp & 3;                         // TMEM lanes this warp may read
+        const int quarter = warp & 3;                         // TMEM lanes this warp may read
+        const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
+        int local = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
+            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            const int buf = local & 1, use = local >> 1;
+            ok = __all_sync(COAT_FULL_MASK, mbar_wait(&acc_full[buf], use & 1, abort_flag));   // warp-uniform
+            if (!ok) break;
+            tc_fence_after();
             const int row = tile_m * kBM + quarter * 32 + lane;
-            const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), r);
+                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kBN + c * 32), r);
                 float v[32];
                 const int col0 = tile_n * kBN + c * 32;
 #pragma unroll
@@ -249,9 +274,13 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                 }
                 epilogue_store<FMT_C>(e, row, col0, v);
             }
+            // all of this warp's reads of the accumulator are complete (tcgen05.wait::ld inside tmem_ld32)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s2u(&acc_empty[buf])) : "memory");
         }
     }
-    if (!ok) g_gemm_device_status = COAT_E_TIMEOUT;
+    if (!ok) { *abort_flag = 1; g_gemm_device_status = COAT_E_TIMEOUT; }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -314,16 +343,19 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     e.fmt_c = fmt_a; e.ieee_div = (flags & COAT_QUANT_IEEE_DIV) ? 1 : 0;
     e.M = (int)M; e.N = (int)N; e.K = (int)K;
     const uint32_t idesc = make_idesc(fmt_a, fmt_b, kBM, kBN);
-    const dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+    const int tiles_m = (int)((M + kBM - 1) / kBM), tiles_n = (int)((N + kBN - 1) / kBN);
+    const int64_t n_tiles = (int64_t)tiles_m * tiles_n;
+    const int sms = coat_sm_count();
+    const unsigned grid = (unsigned)(n_tiles < sms ? n_tiles : sms);
     cudaStream_t st = (cudaStream_t)stream;
     if (fmt_a == COAT_E4M3) {
         if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
             return COAT_E_LAUNCH;
-        fp8_gemm_kernel<COAT_E4M3><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e);
+        fp8_gemm_kernel<COAT_E4M3><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e, tiles_m, tiles_n);
     } else {
         if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E5M2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
             return COAT_E_LAUNCH;
-        fp8_gemm_kernel<COAT_E5M2><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e);
+        fp8_gemm_kernel<COAT_E5M2><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e, tiles_m, tiles_n);
     }
     return coat_launch_status();
 }
