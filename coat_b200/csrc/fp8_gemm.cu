@@ -119,6 +119,37 @@ __device__ __forceinline__ float ld_scalar(const void* p, int dtype, int64_t i =
     return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+template <int FMT_C, int QBV>
+__device__ __forceinline__ void quantize_groups(const GemmEpilogue& e, int row, int col0, const float (&v)[32]) {
+    const float fmax = CoatFp8Max<FMT_C>::value;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(e.c) + (int64_t)row * e.N + col0;
+    __nv_bfloat16* sdst = reinterpret_cast<__nv_bfloat16*>(e.scale_c) + (int64_t)row * (e.N / QBV) + col0 / QBV;
+#pragma unroll
+    for (int gi = 0; gi < 32 / QBV; ++gi) {
+        if (col0 + gi * QBV >= e.N) break;
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < QBV; ++i) amax = fmaxf(amax, fabsf(v[gi * QBV + i]));
+        const float num = amax + 1e-10f;
+        const float scale = e.ieee_div ? __fdiv_rn(num, fmax) : coat_div_full(num, fmax);
+        sdst[gi] = __float2bfloat16_rn(scale);
+        // div.full.f32(x, s) == x * rcp.approx.f32(s) bit for bit while |s| is in [2^-120, 2^120]
+        float r;
+        asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(scale));
+        const bool fast = !e.ieee_div && scale >= 7.5231638e-37f && scale <= 1.3292280e36f;
+#pragma unroll
+        for (int i = 0; i < QBV; i += 4) {
+            float q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float x = v[gi * QBV + i + j];
+                q[j] = fast ? x * r : (e.ieee_div ? __fdiv_rn(x, scale) : coat_div_full(x, scale));
+            }
+            *reinterpret_cast<uint32_t*>(dst + gi * QBV + i) = coat_float4_to_fp8x4<FMT_C>(q[0], q[1], q[2], q[3]);
+        }
+    }
+}
+
 template <int FMT_C>
 __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, int col0, float (&v)[32]) {
     // v: 32 consecutive columns col0.. of one row, already scaled (and biased)
@@ -140,34 +171,11 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, i
     } else {
         // fused 1xQB quantisation (linear.py:139-164): QB is 16 or 32, N a multiple of QB, so groups never
         // straddle the 32 columns a thread holds
-        const float fmax = CoatFp8Max<FMT_C>::value;
-        uint8_t* dst = reinterpret_cast<uint8_t*>(e.c) + (int64_t)row * e.N + col0;
-        __nv_bfloat16* sdst = reinterpret_cast<__nv_bfloat16*>(e.scale_c) + (int64_t)row * (e.N / e.QB) + col0 / e.QB;
-        const int groups = 32 / e.QB;
-        for (int gi = 0; gi < groups; ++gi) {
-            if (col0 + gi * e.QB >= e.N) break;
-            float amax = 0.f;
-            for (int i = 0; i < e.QB; ++i) amax = fmaxf(amax, fabsf(v[gi * e.QB + i]));
-            const float num = amax + 1e-10f;
-            const float scale = e.ieee_div ? __fdiv_rn(num, fmax) : coat_div_full(num, fmax);
-            sdst[gi] = __float2bfloat16_rn(scale);
-            for (int i = 0; i < e.QB; i += 4) {
-                float q[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float x = v[gi * e.QB + i + j];
-                    q[j] = e.ieee_div ? __fdiv_rn(x, scale) : coat_div_full(x, scale);
-                }
-                *reinterpret_cast<uint32_t*>(dst + gi * e.QB + i) = coat_float4_to_fp8x4<FMT_C>(q[0], q[1], q[2], q[3]);
-            }
-        }
+        if (e.QB == 16) quantize_groups<FMT_C, 16>(e, row, col0, v);
+        else quantize_groups<FMT_C, 32>(e, row, col0, v);
     }
 }
 
-// Persistent kernel: gridDim.x CTAs (one per SM) walk the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...
-// (tile t -> m-tile t % tiles_m, n-tile t / tiles_m, so that the CTAs running at the same time share B tiles
-// and cover all of A).  Tensor memory holds two 128 x 256 fp32 accumulators: while the epilogue warps drain
-// one, the MMA warp already fills the other with the next tile.
 template <int FMT_C>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint32_t idesc,

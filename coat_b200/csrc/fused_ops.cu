@@ -44,10 +44,11 @@ struct FusedArgs {
 };
 
 template <int FMT>
-__device__ __forceinline__ void load_dequant16(const uint8_t* codes, const void* scales, int scale_dtype, int64_t row,
-                                               int64_t c16, int64_t N, int QB, float (&x)[16]) {
-    const uint4 w = *reinterpret_cast<const uint4*>(codes + row * N + c16 * 16);
-    const float s = load_scale(scales, row * (N / QB) + (c16 * 16) / QB, scale_dtype);
+// contiguous rows, N a multiple of QB: segment `seg` of the matrix belongs to group seg >> lane_shift
+__device__ __forceinline__ void load_dequant16(const uint8_t* codes, const void* scales, int scale_dtype, int64_t seg,
+                                               int lane_shift, float (&x)[16]) {
+    const uint4 w = *reinterpret_cast<const uint4*>(codes + seg * 16);
+    const float s = load_scale(scales, seg >> lane_shift, scale_dtype);
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -83,16 +84,16 @@ __device__ __forceinline__ float ex2_approx(float x) { float r; asm("ex2.approx.
 template <int OP, int FMT_IN, int FMT_OUT, bool IEEE>
 __global__ void __launch_bounds__(kStraightThreads)
 fused_elementwise_kernel(FusedArgs a) {
-    const int64_t segs_per_row = a.N >> 4;
-    const int64_t total = a.M * segs_per_row;
+    // one 16-element segment per thread, one trip; every operand has contiguous rows, so no index division
+    const int64_t total = a.M * (a.N >> 4);
     const int lanes = a.QB >> 4;
+    const int lane_shift = 31 - __clz(lanes);
     const float fp8_max = a.fp8_max;
     float block_max = 0.f;
-    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < ((total + 31) & ~31ll);
-         seg += (int64_t)gridDim.x * blockDim.x) {
+    {
+        const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
         const bool live = seg < total;
-        const int64_t row = live ? seg / segs_per_row : 0, c16 = live ? seg - row * segs_per_row : 0;
-        const int64_t off = row * a.N + c16 * 16;
+        const int64_t off = seg * 16;
         float v[16];
         float amax = 0.f;
         if (live) {
@@ -103,7 +104,7 @@ fused_elementwise_kernel(FusedArgs a) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) v[i] = x[i] + t[i];
             } else {
-                load_dequant16<FMT_IN>(a.x1, a.s1, a.in_scale_dtype, row, c16, a.N, a.QB, x);
+                load_dequant16<FMT_IN>(a.x1, a.s1, a.in_scale_dtype, seg, lane_shift, x);
                 if (OP == OP_SILU_FWD) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = sigmoid_ref<IEEE>(x[i]) * x[i];
@@ -130,7 +131,7 @@ fused_elementwise_kernel(FusedArgs a) {
                         v[i] = (cdf + qdiv<IEEE>(x[i] * e, rt2pi)) * t[i];
                     }
                 } else {   // OP_MUL_FWD, OP_MUL_BWD
-                    load_dequant16<FMT_IN>(a.x2, a.s2, a.in_scale_dtype, row, c16, a.N, a.QB, t);
+                    load_dequant16<FMT_IN>(a.x2, a.s2, a.in_scale_dtype, seg, lane_shift, t);
                     if (OP == OP_MUL_FWD) {
 #pragma unroll
                         for (int i = 0; i < 16; ++i) v[i] = x[i] * t[i];
@@ -146,19 +147,18 @@ fused_elementwise_kernel(FusedArgs a) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
         }
-        amax = subgroup_max(amax, lanes);
-        if (!live) continue;
-        const float scale = qdiv<IEEE>(amax + kScaleMinThres, fp8_max);
-        if (a.y_bf16) store_bf16x16(a.y_bf16 + off, v);
-        if (a.y_q) {
-            float q[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
-            *reinterpret_cast<uint4*>(a.y_q + off) = pack16<FMT_OUT>(q);
+        amax = subgroup_max(amax, lanes);   // whole warps: the grid is rounded up to blocks of 256 threads
+        if (live) {
+            const float scale = qdiv<IEEE>(amax + kScaleMinThres, fp8_max);
+            if (a.y_bf16) store_bf16x16(a.y_bf16 + off, v);
+            if (a.y_q) {
+                float q[16];
+                ScaleDivider<IEEE>(scale).apply(v, q);
+                *reinterpret_cast<uint4*>(a.y_q + off) = pack16<FMT_OUT>(q);
+            }
+            if (a.s_y && (seg & (lanes - 1)) == 0) store_scale(a.s_y, seg >> lane_shift, a.out_scale_dtype, scale);
+            block_max = amax;
         }
-        if (a.s_y && (c16 & (lanes - 1)) == 0)
-            store_scale(a.s_y, row * (a.N / a.QB) + c16 / lanes, a.out_scale_dtype, scale);
-        block_max = fmaxf(block_max, amax);
     }
     if (a.amax_bits) {
         block_max = coat_warp_max(block_max);
@@ -220,7 +220,7 @@ rmsnorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
     for (int k = 0; k < S; ++k) {
         const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
         if (c16 < segs) {
-            load_dequant16<FMT>(x, s_x, in_scale_dtype, row, c16, N, QB, v[k]);
+            load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), v[k]);
 #pragma unroll
             for (int i = 0; i < 16; ++i) ss += v[k][i] * v[k][i];
         } else {
@@ -284,7 +284,7 @@ rmsnorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
             const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
             if (c16 < segs) {
                 float g[16];
-                load_dequant16<FMT>(x, s_x, in_scale_dtype, row, c16, N, QB, xhat[k]);
+                load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), xhat[k]);
                 load_float16(dy, dy_dtype, row * N + c16 * 16, g);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
@@ -351,7 +351,7 @@ template <int OP>
 int launch_fused(const FusedArgs& a, int fmt_in, int fmt_out, int flags, cudaStream_t st) {
     if (a.amax_bits && cudaMemsetAsync(a.amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
     if (a.M == 0 || a.N == 0) return COAT_OK;
-    const int grid = straight_grid(a.M * (a.N / 16));
+    const unsigned grid = straight_grid(a.M * (a.N / 16));
     const bool ieee = flags & COAT_QUANT_IEEE_DIV;
 #define COAT_LAUNCH(FI, FO)                                                                                 \
     do {                                                                                                    \

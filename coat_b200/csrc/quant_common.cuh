@@ -13,6 +13,40 @@ __device__ __forceinline__ float qdiv(float a, float b) {
     return IEEE ? __fdiv_rn(a, b) : coat_div_full(a, b);
 }
 
+// Division of many values by one scale.  For a divisor whose magnitude lies in [2^-120, 2^120],
+// div.full.f32(a, b) is bit for bit a * rcp.approx.f32(b) for every finite a (checked on sm_100 over
+// 8e9 random operand pairs, divisors from 1e-36 to 1e37; outside that range div.full rescales its
+// operands), so the reciprocal is taken once per scale and each element costs one multiplication.
+template <bool IEEE>
+struct ScaleDivider {
+    float s, r;
+    bool fast;
+    __device__ __forceinline__ explicit ScaleDivider(float scale) : s(scale), r(0.f), fast(false) {
+        if (!IEEE) {
+            const float a = fabsf(scale);
+            fast = a >= 7.5231638e-37f && a <= 1.3292280e36f;
+            asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(scale));
+        }
+    }
+    __device__ __forceinline__ float operator()(float x) const {
+        if (IEEE) return __fdiv_rn(x, s);
+        return fast ? x * r : coat_div_full(x, s);
+    }
+    template <int N>
+    __device__ __forceinline__ void apply(const float (&v)[N], float (&q)[N]) const {
+        if (IEEE) {
+#pragma unroll
+            for (int i = 0; i < N; ++i) q[i] = __fdiv_rn(v[i], s);
+        } else if (fast) {
+#pragma unroll
+            for (int i = 0; i < N; ++i) q[i] = v[i] * r;
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; ++i) q[i] = coat_div_full(v[i], s);
+        }
+    }
+};
+
 // ---- typed 16-element row segments -------------------------------------------------------------
 template <typename T> struct Seg16;
 template <> struct Seg16<__nv_bfloat16> {
@@ -100,11 +134,19 @@ __device__ __forceinline__ float subgroup_max(float v, int lanes) {
 
 constexpr int kStraightThreads = 256;
 
-inline int straight_grid(int64_t segs) {
+// one thread per 16-element segment, one trip
+inline unsigned straight_grid(int64_t segs) {
     const int64_t blocks = (segs + kStraightThreads - 1) / kStraightThreads;
-    const int64_t cap = (int64_t)coat_sm_count() * 16;   // persistent beyond 16 CTAs of 256 threads per SM
-    return (int)(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+    return (unsigned)(blocks < 1 ? 1 : blocks);
 }
 
+// Element offset of 16-element segment `seg` in a matrix of `segs_per_row` segments per row and row stride
+// `ld` elements.  Contiguous rows need no division (a 64-bit division costs about as much as the rest of a
+// segment's work).
+__device__ __forceinline__ int64_t seg_offset(int64_t seg, int64_t segs_per_row, int64_t ld) {
+    if (ld == segs_per_row * 16) return seg * 16;
+    const int64_t row = seg / segs_per_row;
+    return row * ld + (seg - row * segs_per_row) * 16;
+}
 
 }  // namespace

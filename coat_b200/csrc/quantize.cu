@@ -31,6 +31,9 @@ namespace {
 //    (_quantize_pertensor.py:46-103): group scales only, plus the tensor's amax for the fused pass 2
 // =================================================================================================
 // MODE 0: write codes + scales.  MODE 1: write scales (if s != null) and atomically max the tensor amax.
+// One 16-element segment per thread and one trip per thread: at 32 bytes loaded per thread the resident
+// warps of a full grid already keep HBM busy, and a one-trip grid measured faster than a persistent
+// grid-stride loop.  Contiguous rows (ld == N, the usual case) are addressed without any division.
 template <typename T, int FMT, bool IEEE, int MODE>
 __global__ void __launch_bounds__(kStraightThreads)
 group_quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* __restrict__ s, int scale_dtype,
@@ -38,34 +41,28 @@ group_quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* __
     const int64_t segs_per_row = N >> 4;
     const int64_t total = M * segs_per_row;
     const int lanes = QB >> 4;
-    const float fp8_max = CoatFp8Max<FMT>::value;
-    float block_max = 0.f;
-    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < ((total + 31) & ~31ll);
-         seg += (int64_t)gridDim.x * blockDim.x) {
-        const bool live = seg < total;
-        const int64_t row = live ? seg / segs_per_row : 0, c16 = live ? seg - row * segs_per_row : 0;
-        float v[16];
-        float amax = 0.f;
-        if (live) {
-            Seg16<T>::load(x + row * ldx + c16 * 16, v);
+    const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
+    const bool live = seg < total;
+    float v[16];
+    float amax = 0.f;
+    if (live) {
+        Seg16<T>::load(x + seg_offset(seg, segs_per_row, ldx), v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        }
-        amax = subgroup_max(amax, lanes);
-        if (!live) continue;
-        const float scale = qdiv<IEEE>(amax + kScaleMinThres, fp8_max);
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = subgroup_max(amax, lanes);   // whole warps: the grid is rounded up to blocks of 256 threads
+    if (live) {
+        const float scale = qdiv<IEEE>(amax + kScaleMinThres, CoatFp8Max<FMT>::value);
         if (MODE == 0) {
             float q[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
-            *reinterpret_cast<uint4*>(y + row * ldy + c16 * 16) = pack16<FMT>(q);
-        } else {
-            block_max = fmaxf(block_max, amax);
+            ScaleDivider<IEEE>(scale).apply(v, q);
+            *reinterpret_cast<uint4*>(y + seg_offset(seg, segs_per_row, ldy)) = pack16<FMT>(q);
         }
-        if (s && (c16 & (lanes - 1)) == 0) store_scale(s, row * (N / QB) + c16 / lanes, scale_dtype, scale);
+        // N is a multiple of QB, so group g of row r is group r * (N / QB) + g = seg / lanes of the matrix
+        if (s && (seg & (lanes - 1)) == 0) store_scale(s, seg >> (31 - __clz(lanes)), scale_dtype, scale);
     }
     if (MODE == 1) {
-        block_max = coat_warp_max(block_max);
+        float block_max = coat_warp_max(amax);
         __shared__ float wmax[kStraightThreads / 32];
         if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = block_max;
         __syncthreads();
@@ -103,15 +100,13 @@ division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __
     if (amax_bits && s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scale);
     const int64_t segs_per_row = N >> 4;
     const int64_t total = M * segs_per_row;
-    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < total;
-         seg += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
-        float v[16], q[16];
-        Seg16<T>::load(x + row * ldx + c16 * 16, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) q[i] = qdiv<IEEE>(v[i], scale);
-        *reinterpret_cast<uint4*>(y + row * ldy + c16 * 16) = pack16<FMT>(q);
-    }
+    const ScaleDivider<IEEE> divide(scale);
+    const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
+    if (seg >= total) return;
+    float v[16], q[16];
+    Seg16<T>::load(x + seg_offset(seg, segs_per_row, ldx), v);
+    divide.apply(v, q);
+    *reinterpret_cast<uint4*>(y + seg_offset(seg, segs_per_row, ldy)) = pack16<FMT>(q);
 }
 
 // =================================================================================================
@@ -121,26 +116,24 @@ template <int FMT>
 __global__ void __launch_bounds__(kStraightThreads)
 dequantize_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s, int scale_dtype,
                   __nv_bfloat16* __restrict__ y, int64_t M, int64_t N, int QB) {
-    const int64_t segs_per_row = N >> 4;
-    const int64_t total = M * segs_per_row;
-    for (int64_t seg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; seg < total;
-         seg += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
-        const float scale = load_scale(s, row * (N / QB) + (c16 * 16) / QB, scale_dtype);
-        const uint4 w = *reinterpret_cast<const uint4*>(x + row * N + c16 * 16);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-        uint32_t out[8];
+    const int64_t total = M * (N >> 4);
+    const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
+    if (seg >= total) return;
+    // rows are contiguous and N is a multiple of QB: segment `seg` belongs to group seg / (QB / 16)
+    const float scale = load_scale(s, seg >> (31 - __clz(QB >> 4)), scale_dtype);
+    const uint4 w = *reinterpret_cast<const uint4*>(x + seg * 16);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float f[4];
-            coat_fp8x4_to_float4<FMT>(ww[i], f);
-            out[2 * i] = (uint32_t)coat_float_to_bf16_bits(f[0] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[1] * scale) << 16);
-            out[2 * i + 1] = (uint32_t)coat_float_to_bf16_bits(f[2] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[3] * scale) << 16);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(y + row * N + c16 * 16);
-        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    for (int i = 0; i < 4; ++i) {
+        float f[4];
+        coat_fp8x4_to_float4<FMT>(ww[i], f);
+        out[2 * i] = (uint32_t)coat_float_to_bf16_bits(f[0] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[1] * scale) << 16);
+        out[2 * i + 1] = (uint32_t)coat_float_to_bf16_bits(f[2] * scale) | ((uint32_t)coat_float_to_bf16_bits(f[3] * scale) << 16);
     }
+    uint4* dst = reinterpret_cast<uint4*>(y + seg * 16);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
 }
 
 // =================================================================================================
@@ -206,8 +199,8 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 1));
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 2));
                 rs[j] = qdiv<IEEE>(a + kScaleMinThres, fp8_max);
-                straight[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], rs[j]), qdiv<IEEE>(v[j][1], rs[j]),
-                                                        qdiv<IEEE>(v[j][2], rs[j]), qdiv<IEEE>(v[j][3], rs[j]));
+                const ScaleDivider<IEEE> dr(rs[j]);
+                straight[j] = coat_float4_to_fp8x4<FMT>(dr(v[j][0]), dr(v[j][1]), dr(v[j][2]), dr(v[j][3]));
             }
             if ((nb & 3) == 0 && col_ok) {
 #pragma unroll
@@ -224,10 +217,10 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 16));
                 cs[i] = qdiv<IEEE>(a + kScaleMinThres, fp8_max);
             }
+            const ScaleDivider<IEEE> d0(cs[0]), d1(cs[1]), d2(cs[2]), d3(cs[3]);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                qt[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], cs[0]), qdiv<IEEE>(v[j][1], cs[1]),
-                                                  qdiv<IEEE>(v[j][2], cs[2]), qdiv<IEEE>(v[j][3], cs[3]));
+                qt[j] = coat_float4_to_fp8x4<FMT>(d0(v[j][0]), d1(v[j][1]), d2(v[j][2]), d3(v[j][3]));
             transpose4x4(qt, transposed);
             if (mb == 0 && col_ok && m0 < M) {
 #pragma unroll
@@ -235,10 +228,10 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
                     store_scale(s_y_t, (int64_t)(n0 + i) * (M >> 4) + (m0 >> 4), scale_dtype, cs[i]);
             }
         } else {
+            const ScaleDivider<IEEE> ds(scalar);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                straight[j] = coat_float4_to_fp8x4<FMT>(qdiv<IEEE>(v[j][0], scalar), qdiv<IEEE>(v[j][1], scalar),
-                                                        qdiv<IEEE>(v[j][2], scalar), qdiv<IEEE>(v[j][3], scalar));
+                straight[j] = coat_float4_to_fp8x4<FMT>(ds(v[j][0]), ds(v[j][1]), ds(v[j][2]), ds(v[j][3]));
             transpose4x4(straight, transposed);
         }
         if (STRAIGHT && col_ok) {
@@ -315,7 +308,7 @@ struct GroupQuantArgs {
     const void* x; uint8_t* y; void* s; int scale_dtype; unsigned int* amax; int64_t M, N, ldx; int QB; int mode;
     cudaStream_t st;
     template <typename T, int FMT, bool IEEE> int run() const {
-        const int grid = straight_grid(M * (N / 16));
+        const unsigned grid = straight_grid(M * (N / 16));
         if (mode == 0)
             group_quantize_kernel<T, FMT, IEEE, 0><<<grid, kStraightThreads, 0, st>>>(
                 reinterpret_cast<const T*>(x), y, s, scale_dtype, nullptr, M, N, ldx, N, QB);
@@ -428,7 +421,7 @@ extern "C" int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf
     if (!x || !s_x || !y_bf16 || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
     if (!qb_ok(QB) || N % QB != 0) return COAT_E_SHAPE;
     if (!coat_aligned(x, 16) || !coat_aligned(y_bf16, 16)) return COAT_E_ALIGN;
-    const int grid = straight_grid(M * (N / 16));
+    const unsigned grid = straight_grid(M * (N / 16));
     if (fmt == COAT_E4M3)
         dequantize_kernel<COAT_E4M3><<<grid, kStraightThreads, 0, (cudaStream_t)stream>>>(
             x, s_x, scale_dtype, reinterpret_cast<__nv_bfloat16*>(y_bf16), M, N, QB);
@@ -482,9 +475,8 @@ static_partial_amax_kernel(const T* __restrict__ x, float* __restrict__ partials
     for (int k = 0; k < kStaticSegsPerThread; ++k) {
         const int64_t seg = first + (int64_t)k * kStraightThreads + threadIdx.x;
         if (seg < total) {
-            const int64_t row = seg / segs_per_row, c16 = seg - row * segs_per_row;
             float v[16];
-            Seg16<T>::load(x + row * ldx + c16 * 16, v);
+            Seg16<T>::load(x + seg_offset(seg, segs_per_row, ldx), v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
         }
