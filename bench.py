@@ -361,12 +361,21 @@ def run_gpu_arm(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=device)
+        # the bucketed all-gather runs under the step kernels: give NCCL's stream priority over them
+        opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+        dist.init_process_group("nccl", device_id=device, pg_options=opts)
 
     shapes = llama2_7b_shapes() if args.workload == "llama2-7b" else [(4096, 4096)]
     numels = [numel(s) for s in shapes]
     total = sum(numels)
-    opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, **HYPER)
+    exchange, exchange_note = (args.exchange if world > 1 else None), ""
+    try:
+        opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange, **HYPER)
+    except RuntimeError as e:   # raised on every rank alike when the peer mapping is not available
+        if exchange != "p2p":
+            raise
+        exchange, exchange_note = "nccl", f" (p2p set-up failed: {str(e)[:200]})"
+        opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange="nccl", **HYPER)
     fill_synthetic(opt, shapes, torch)
     my_params = sum(pc.numel for pc in opt.my_pieces)
 
@@ -378,15 +387,12 @@ def run_gpu_arm(args):
     # two independent gradient sets, alternated, so that the moments do not converge onto one
     # fixed gradient (a single repeated gradient makes the requantisation unrealistically easy)
     grads = [opt.grad, torch.empty_like(opt.grad).normal_(0.0, 1e-3)]
-    tables = []
-    for gbuf in grads:   # one device-side tensor table per gradient set, built outside the timed region
-        opt.grad = gbuf
-        opt._build_table()
-        tables.append(opt._table)
+    for gbuf in grads:   # device-side tensor tables of both gradient sets are built outside the timed region
+        opt.set_grad_buffer(gbuf)
     step_no = [0]
 
     def one_step(local_only=False):
-        opt.grad, opt._table = grads[step_no[0] & 1], tables[step_no[0] & 1]
+        opt.set_grad_buffer(grads[step_no[0] & 1])
         step_no[0] += 1
         opt.local_step() if local_only else opt.step()
 
@@ -419,6 +425,8 @@ def run_gpu_arm(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kernel_ms = t.tolist()
+    n_launches = args.steps * opt.n_buckets
+    opt.close()   # collective: unmaps the peers' buffers
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
@@ -447,7 +455,11 @@ def run_gpu_arm(args):
                                     "(291 tensors, 6738415616 params)" if args.workload == "llama2-7b" else
                                     "FP8AdamW-expand step over one 4096x4096 tensor (profiling case)") +
                                    ", fp32 master weights, E4M3 moments group 128, "
-                                   "bf16 weight copy" + (" + NCCL all-gather" if world > 1 else ""),
+                                   "bf16 weight copy" + ({"p2p": " stored by the same kernel into every peer's buffer over NVLink "
+                                                                   "(fused step + all-gather), one-element all-reduce as "
+                                                                   "the closing barrier",
+                                                            "nccl": " + bucketed NCCL all-gather on a side stream",
+                                                            None: ""}[exchange]) + exchange_note,
                        "parallelism": f"zero-shard x{world} on 128-element group boundaries",
                        "l2": "inputs larger than L2 (>= 10 GB per GPU per step)" if args.workload == "llama2-7b" else
                              "inputs larger than L2 (308 MB per step)",
@@ -456,11 +468,11 @@ def run_gpu_arm(args):
             "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "workload": f"CoatAdamW.step on one decoder layer ({e2e_n} params), grads from pinned host "
                                 "memory, updated fp32 weights read back"},
-            "gpu_launches": args.steps,
+            "gpu_launches": n_launches,
             "clocks": clocks,
         }
         if not args.kernel_only and args.workload == "llama2-7b":
-            del opt, grads, tables
+            del opt, grads
             torch.cuda.empty_cache()
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device)}
@@ -482,6 +494,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
+                         "the step kernel itself, or bucketed NCCL all-gathers overlapped with the step")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":

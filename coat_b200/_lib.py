@@ -14,6 +14,8 @@ LIB_PATH = os.environ.get("COAT_B200_LIB", os.path.join(_HERE, "libcoat_b200.so"
 F32, BF16, F16 = 0, 1, 2
 E4M3, E5M2 = 0, 1
 ADAMW_EXACT_POW = 1
+MAX_PEERS = 7            # COAT_MAX_PEERS
+PEER_HANDLE_BYTES = 64   # COAT_PEER_HANDLE_BYTES
 QUANT_IEEE_DIV = 1
 
 # Default flags of the quantizer entry points: 0 = the reference's (Triton's) division, QUANT_IEEE_DIV
@@ -31,6 +33,11 @@ SIGNATURES = {
     "coat_fp8_adamw_expand_step": [_vp] * 10 + [_f] * 5 + [_i, _i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_step": [_vp] * 6 + [_f] * 5 + [_i, _i, _i64, _i, _vp, _i, _vp],
     "coat_fp8_adamw_multi_step": [_vp, _vp, _i, _i64, _i] + [_f] * 5 + [_i, _i, _i, _i, _i, _vp],
+    "coat_fp8_adamw_multi_step_bcast": [_vp, _vp, _i, _i64, _i] + [_f] * 5 + [_i, _i, _i, _i, _i, _vp, _i, _vp],
+    "coat_peer_buffer_create": [_i64, _vp, _vp],
+    "coat_peer_buffer_open": [_vp, _vp],
+    "coat_peer_buffer_close": [_vp],
+    "coat_peer_buffer_free": [_vp],
     "coat_fp8_quantize": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_group_scales_amax": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_division": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],

@@ -33,7 +33,32 @@ struct AdamwHyper {
     float beta1, beta2, lr, wd, eps;
     int step;
     int expand_min;
+    // Broadcast of the bf16 weight copy: besides bf16_out itself, every bf16 store is repeated at
+    // bf16_out + peer_delta[i] bytes (the same slot of another GPU's buffer, mapped into this process).
+    int n_peers;
+    long long peer_delta[COAT_MAX_PEERS];
 };
+
+// bf16 copy of 4 updated weights: the local store, then the same 8 bytes to every peer (plain stores over
+// NVLink; nothing here waits on a peer)
+template <bool BCAST>
+__device__ __forceinline__ void store_bf16x4_bcast(__nv_bfloat16* dst, const float (&q)[4], const AdamwHyper& h) {
+    uint2 t;
+    t.x = (uint32_t)coat_float_to_bf16_bits(q[0]) | ((uint32_t)coat_float_to_bf16_bits(q[1]) << 16);
+    t.y = (uint32_t)coat_float_to_bf16_bits(q[2]) | ((uint32_t)coat_float_to_bf16_bits(q[3]) << 16);
+    *reinterpret_cast<uint2*>(dst) = t;
+    if constexpr (BCAST)
+        for (int i = 0; i < h.n_peers; ++i)
+            *reinterpret_cast<uint2*>(reinterpret_cast<char*>(dst) + h.peer_delta[i]) = t;
+}
+template <bool BCAST>
+__device__ __forceinline__ void store_bf16_bcast(__nv_bfloat16* dst, float x, const AdamwHyper& h) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(x);
+    *dst = b;
+    if constexpr (BCAST)
+        for (int i = 0; i < h.n_peers; ++i)
+            *reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(dst) + h.peer_delta[i]) = b;
+}
 
 // One tensor's pointers (single-tensor launch passes this by value; the table launch
 // reads it from global memory).
@@ -167,7 +192,7 @@ __device__ __forceinline__ void expand_group_scalars(float absmax, float absmin,
 
 // ---- one group, exact arithmetic ---------------------------------------------------
 // `lane` owns elements [base, base+4) of the tensor; `nvalid` of them (0..4) exist.
-template <typename scalar_t, bool EXPAND>
+template <typename scalar_t, bool EXPAND, bool BCAST>
 __device__ __noinline__ void process_group_exact(const TensorDesc& t, int64_t group, int lane,
                                                     const AdamwHyper& h, float om_beta1,
                                                     float om_beta2, float correction1,
@@ -241,7 +266,7 @@ __device__ __noinline__ void process_group_exact(const TensorDesc& t, int64_t gr
             float q[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) q[j] = E::round(p[j]);
-            Elem4<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(t.bf16_out) + base, q);
+            store_bf16x4_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(t.bf16_out) + base, q, h);
         }
     } else {
 #pragma unroll
@@ -249,7 +274,7 @@ __device__ __noinline__ void process_group_exact(const TensorDesc& t, int64_t gr
             if (j < nvalid) {
                 E::put(pp + j, p[j]);
                 if (t.bf16_out)
-                    reinterpret_cast<__nv_bfloat16*>(t.bf16_out)[base + j] = __float2bfloat16_rn(E::round(p[j]));
+                    store_bf16_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(t.bf16_out) + base + j, E::round(p[j]), h);
             }
     }
 
@@ -604,8 +629,14 @@ __device__ __noinline__ void queue_exact(WarpTile& w, int slot, int lane, uint32
     }
 }
 
-template <typename scalar_t, bool MULTI>
-__global__ void __launch_bounds__(kTiledThreads)
+// Shared memory, not registers, limits how many CTAs share an SM; telling the compiler so lets it use the
+// registers that occupancy leaves free instead of spilling.
+constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(float));
+constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmem + 1024));
+static_assert(kTiledCtasPerSm * (kTiledSmem + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
+
+template <typename scalar_t, bool MULTI, bool BCAST>
+__global__ void __launch_bounds__(kTiledThreads, kTiledCtasPerSm)
 fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
                               const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
                               AdamwHyper h, unsigned long long* dbg) {
@@ -793,7 +824,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                         float q[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) q[j] = E::round(p[j]);
-                        Elem4<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q);
+                        store_bf16x4_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q, h);
                     }
                     w.m1[slot][lane] = make_float4(m1[0], m1[1], m1[2], m1[3]);
                     w.v1[slot][lane] = make_float4(v1[0], v1[1], v1[2], v1[3]);
@@ -811,7 +842,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             }
             if (!ok) {
                 const TensorDesc& t = MULTI ? table[w.ti[slot]] : single;
-                process_group_exact<scalar_t, true>(t, w.local[slot], lane, h, c.om_beta1, c.om_beta2, c.correction1,
+                process_group_exact<scalar_t, true, BCAST>(t, w.local[slot], lane, h, c.om_beta1, c.om_beta2, c.correction1,
                                                     c.correction2_sqrt, desc_vec_ok(t, E::kVecAlign), smem_min);
                 ++n_exact;
             }
@@ -940,7 +971,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     }
 }
 
-template <typename scalar_t, bool EXPAND, bool MULTI>
+template <typename scalar_t, bool EXPAND, bool MULTI, bool BCAST>
 __global__ void __launch_bounds__(kThreads)
 fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
                  const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
@@ -963,7 +994,7 @@ fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
     if (!MULTI) {
         const bool vec_ok = desc_vec_ok(single, Elem4<scalar_t>::kVecAlign);
         for (; gi < total_groups; gi += warps_total) {
-            process_group_exact<scalar_t, EXPAND>(single, gi, lane, h, c.om_beta1, c.om_beta2, c.correction1,
+            process_group_exact<scalar_t, EXPAND, BCAST>(single, gi, lane, h, c.om_beta1, c.om_beta2, c.correction1,
                                                   c.correction2_sqrt, vec_ok, smem_min[warp]);
             if (dbg && lane == 0) atomicAdd(dbg + 1, 1ull);
         }
@@ -982,7 +1013,7 @@ fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
             TensorDesc t = table[ti];
             const bool vec_ok = desc_vec_ok(t, Elem4<scalar_t>::kVecAlign);
             const int64_t local = gi - group_prefix[ti];
-            process_group_exact<scalar_t, EXPAND>(t, local, lane, h, c.om_beta1, c.om_beta2, c.correction1,
+            process_group_exact<scalar_t, EXPAND, BCAST>(t, local, lane, h, c.om_beta1, c.om_beta2, c.correction1,
                                                   c.correction2_sqrt, vec_ok, smem_min[warp]);
             if (dbg && lane == 0) atomicAdd(dbg + 1, 1ull);
         }
@@ -998,9 +1029,6 @@ int grid_for(int64_t total_groups) {
     return (int)(ctas_needed < cap ? (ctas_needed > 0 ? ctas_needed : 1) : cap);
 }
 
-constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(float));
-constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmem + 1024));
-static_assert(kTiledCtasPerSm * (kTiledSmem + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
 
 template <typename scalar_t, bool EXPAND, bool MULTI>
 int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_t* prefix, int n_tensors,
@@ -1009,7 +1037,9 @@ int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_
     // weight types and the COAT_ADAMW_EXACT_POW flag take the one-group-per-warp exact kernel.
     if constexpr (EXPAND && std::is_same<scalar_t, float>::value) {
         if (!(flags & COAT_ADAMW_EXACT_POW)) {
-            auto kern = fp8_adamw_expand_tiled_kernel<scalar_t, MULTI>;
+            // the broadcast variant exists for table launches only
+            auto kern = (MULTI && h.n_peers > 0) ? fp8_adamw_expand_tiled_kernel<scalar_t, MULTI, MULTI>
+                                                 : fp8_adamw_expand_tiled_kernel<scalar_t, MULTI, false>;
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTiledSmem) != cudaSuccess)
                 return COAT_E_LAUNCH;
             const int64_t tiles = (total_groups + kTile - 1) / kTile;
@@ -1021,8 +1051,10 @@ int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_
             return coat_launch_status();
         }
     }
-    fp8_adamw_kernel<scalar_t, EXPAND, MULTI><<<grid_for(total_groups), kThreads, 0, st>>>(
-        single, table, prefix, n_tensors, total_groups, h, g_debug_counters);
+    auto exact = (MULTI && h.n_peers > 0) ? fp8_adamw_kernel<scalar_t, EXPAND, MULTI, MULTI>
+                                          : fp8_adamw_kernel<scalar_t, EXPAND, MULTI, false>;
+    exact<<<grid_for(total_groups), kThreads, 0, st>>>(single, table, prefix, n_tensors, total_groups, h,
+                                                       g_debug_counters);
     return coat_launch_status();
 }
 
@@ -1084,6 +1116,32 @@ extern "C" int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int
     if (!table || !group_prefix) return COAT_E_BADARG;
     TensorDesc none = {};
     AdamwHyper h = {beta1, beta2, lr, wd, eps, step, expand_min};
+    if (expand)
+        return launch<true, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h, flags,
+                                  (cudaStream_t)stream);
+    return launch<false, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h, flags,
+                               (cudaStream_t)stream);
+}
+
+// The table launch with the bf16 copy broadcast to peer GPUs: one kernel does the step and the "all-gather"
+// (each GPU stores its slice into every peer's buffer while it computes).
+extern "C" int coat_fp8_adamw_multi_step_bcast(const CoatAdamwTensor* table, const int64_t* group_prefix,
+                                               int n_tensors, int64_t total_groups, int expand, float beta1,
+                                               float beta2, float lr, float wd, float eps, int step, int qgroup,
+                                               int expand_min, int p_dtype, int flags,
+                                               const int64_t* peer_deltas, int n_peers, void* stream) {
+    if (qgroup != kGroup) return COAT_E_QGROUP;
+    if (n_tensors < 0 || total_groups < 0 || n_peers < 0 || n_peers > COAT_MAX_PEERS) return COAT_E_BADARG;
+    if (n_peers > 0 && !peer_deltas) return COAT_E_BADARG;
+    if (n_tensors == 0 || total_groups == 0) return COAT_OK;
+    if (!table || !group_prefix) return COAT_E_BADARG;
+    TensorDesc none = {};
+    AdamwHyper h = {beta1, beta2, lr, wd, eps, step, expand_min};
+    h.n_peers = n_peers;
+    for (int i = 0; i < n_peers; ++i) {
+        if (peer_deltas[i] % 8 != 0) return COAT_E_ALIGN;   // 8-byte vector stores keep their alignment
+        h.peer_delta[i] = peer_deltas[i];
+    }
     if (expand)
         return launch<true, true>(p_dtype, none, table, group_prefix, n_tensors, total_groups, h, flags,
                                   (cudaStream_t)stream);

@@ -1,6 +1,8 @@
 // Process-wide helpers of the C ABI: version, error strings, device probing.
 #include "common.cuh"
 
+#include <cstring>
+
 int coat_sm_count() {
     static int cached[64] = {0};
     int dev = 0;
@@ -26,6 +28,7 @@ extern "C" const char* coat_strerror(int code) {
         case COAT_E_DEVICE: return "the current CUDA device is not an sm_100 (B200) device";
         case COAT_E_TOOBIG: return "size exceeds the static maximum of this entry point";
         case COAT_E_TIMEOUT: return "a bounded device-side wait ran out";
+        case COAT_E_PEER: return "peer memory could not be allocated, exported or mapped";
         default: return "unknown coat_b200 error";
     }
 }
@@ -36,4 +39,48 @@ extern "C" int coat_check_device(void) {
     int major = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return COAT_E_DEVICE;
     return major == 10 ? COAT_OK : COAT_E_DEVICE;
+}
+
+// ---- buffers that the other processes of a node can map (CUDA IPC) -----------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == COAT_PEER_HANDLE_BYTES, "handle size is part of the ABI");
+
+extern "C" int coat_peer_buffer_create(int64_t bytes, void** ptr_out, void* handle_out) {
+    if (bytes <= 0 || !ptr_out || !handle_out) return COAT_E_BADARG;
+    void* p = nullptr;
+    if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) { cudaGetLastError(); return COAT_E_PEER; }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p);
+        return COAT_E_PEER;
+    }
+    if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess) { cudaGetLastError(); cudaFree(p); return COAT_E_PEER; }
+    memcpy(handle_out, &h, sizeof(h));
+    *ptr_out = p;
+    return COAT_OK;
+}
+
+extern "C" int coat_peer_buffer_open(const void* handle, void** ptr_out) {
+    if (!handle || !ptr_out) return COAT_E_BADARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return COAT_E_PEER;
+    }
+    *ptr_out = p;
+    return COAT_OK;
+}
+
+extern "C" int coat_peer_buffer_close(void* ptr) {
+    if (!ptr) return COAT_OK;
+    if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) { cudaGetLastError(); return COAT_E_PEER; }
+    return COAT_OK;
+}
+
+extern "C" int coat_peer_buffer_free(void* ptr) {
+    if (!ptr) return COAT_OK;
+    if (cudaFree(ptr) != cudaSuccess) { cudaGetLastError(); return COAT_E_PEER; }
+    return COAT_OK;
 }

@@ -70,20 +70,98 @@ class ShardPlan:
             g = take_hi
         return out
 
+    def bucket_bounds(self, n_buckets: int) -> np.ndarray:
+        """Cuts of a rank's shard (in groups, the same for every rank) into `n_buckets` near-equal
+        ranges: bucket b of every rank is gathered by one collective while bucket b+1 is stepped."""
+        n_buckets = max(1, min(int(n_buckets), max(self.shard_groups, 1)))
+        base, rem = divmod(self.shard_groups, n_buckets)
+        sizes = [base + (1 if b < rem else 0) for b in range(n_buckets)]
+        return np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+
+    def bucket_pieces(self, rank: int, n_buckets: int) -> List[List[Piece]]:
+        """pieces(rank) cut at the bucket bounds; `offset` stays relative to the rank's shard."""
+        bounds = self.bucket_bounds(n_buckets) * GROUP
+        out = [[] for _ in range(len(bounds) - 1)]
+        for pc in self.pieces(rank):
+            span = (pc.numel + GROUP - 1) // GROUP * GROUP
+            lo = pc.offset
+            while lo < pc.offset + span:
+                b = int(np.searchsorted(bounds, lo, side="right") - 1)
+                hi = min(pc.offset + span, int(bounds[b + 1]))
+                start = pc.start + (lo - pc.offset)
+                out[b].append(Piece(pc.tensor, start, min(pc.stop, pc.start + (hi - pc.offset)), lo))
+                lo = hi
+        return out
+
+    def gathered_offset(self, rank: int, offset: int, n_buckets: int) -> int:
+        """Element offset, inside the bucket-major buffer of all ranks' bf16 weights (bucket b holds
+        world_size slots of that bucket's size, rank-major), of shard-local element `offset` of `rank`."""
+        bounds = self.bucket_bounds(n_buckets) * GROUP
+        b = int(np.searchsorted(bounds, offset, side="right") - 1)
+        size = int(bounds[b + 1] - bounds[b])
+        return int(bounds[b]) * self.world_size + rank * size + (offset - int(bounds[b]))
+
     def owner_of(self, tensor: int, element: int) -> int:
         g = int(self.group_prefix[tensor]) + element // GROUP
         return int(np.searchsorted(self.rank_group_lo, g, side="right") - 1)
 
 
-class ShardedCoatAdamW:
-    """One rank's slice of the optimizer: flat buffers, one fused launch, one all-gather.
+class _PeerBuffer:
+    """A device buffer from coat_peer_buffer_create, exposed to torch through the CUDA array interface."""
 
-    `process_group=None` with world_size 1 skips the collective.  Gradients are written by the
-    caller into `self.grad` (already reduce-scattered, as under ZeRO); the updated bf16 weights of
-    ALL ranks appear in `self.gathered` after step()."""
+    def __init__(self, lib_module, nbytes, device):
+        import ctypes
+        self._L = lib_module
+        self.nbytes = int(nbytes)
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(lib_module.PEER_HANDLE_BYTES)
+        with torch.cuda.device(device):
+            lib_module.check(lib_module.lib().coat_peer_buffer_create(self.nbytes, ctypes.byref(ptr), handle),
+                             "peer_buffer_create")
+        self.ptr = int(ptr.value)
+        self.handle = handle.raw
+        self.peers = {}   # rank -> mapped base address of that rank's buffer
+        self.__cuda_array_interface__ = {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False),
+                                         "version": 3, "strides": None}
+
+    def open_peer(self, rank, handle, device):
+        import ctypes
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            self._L.check(self._L.lib().coat_peer_buffer_open(handle, ctypes.byref(ptr)), "peer_buffer_open")
+        self.peers[rank] = int(ptr.value)
+
+    def close(self):
+        for r, p in list(self.peers.items()):
+            self._L.lib().coat_peer_buffer_close(p)
+            del self.peers[r]
+
+    def free(self):
+        if self.ptr:
+            self._L.lib().coat_peer_buffer_free(self.ptr)
+            self.ptr = 0
+
+
+class ShardedCoatAdamW:
+    """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
+    weights everywhere.
+
+    exchange="p2p" (the default with more than one rank): ONE kernel per step does both the update and
+    the exchange; it stores its bf16 slice into every peer's copy of `self.gathered` over NVLink while
+    it computes (coat_fp8_adamw_multi_step_bcast), and a one-element all-reduce after it is the
+    barrier that tells every rank that all slices have landed.
+    exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
+    that the gather of bucket b runs under the step of bucket b+1.
+
+    With world_size 1 there is one bucket and no exchange.  Gradients are written by the caller
+    into `self.grad` (already reduce-scattered, as under ZeRO); the updated bf16 weights of ALL ranks
+    appear in `self.gathered` (bucket-major, see ShardPlan.gathered_offset) after step().  No rank may
+    start step k+1 while another still reads the weights of step k from `self.gathered`; in training
+    the gradient reduce-scatter between the two provides that order."""
 
     def __init__(self, numels, rank=0, world_size=1, device="cuda", lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
-                 weight_decay=1e-2, expand_min=16, use_expansion=True, process_group=None, flags=0):
+                 weight_decay=1e-2, expand_min=16, use_expansion=True, process_group=None, flags=0,
+                 n_buckets=None, exchange=None):
         from . import _lib
         self._lib = _lib
         self.plan = ShardPlan(numels, world_size)
@@ -94,7 +172,19 @@ class ShardedCoatAdamW:
         self.process_group = process_group
         self.flags = flags
         self.step_count = 0
-        self.my_pieces = self.plan.pieces(rank)
+        if exchange is None:
+            exchange = "p2p" if world_size > 1 else "none"
+        if exchange not in ("none", "p2p", "nccl") or (exchange == "none") != (world_size == 1):
+            raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
+        if exchange == "p2p" and world_size - 1 > _lib.MAX_PEERS:
+            raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
+        self.exchange = exchange
+        if n_buckets is None:
+            n_buckets = 8 if exchange == "nccl" else 1
+        self.bounds = self.plan.bucket_bounds(n_buckets)
+        self.n_buckets = len(self.bounds) - 1
+        self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
+        self.my_pieces = [pc for b in self.my_buckets for pc in b]
         n, g = self.plan.shard_numel, self.plan.shard_groups
         dev = self.device
         self.param = torch.zeros(n, dtype=torch.float32, device=dev)
@@ -107,18 +197,196 @@ class ShardedCoatAdamW:
         self.expand_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
         self.sqrt_minmax_exp_avg = torch.ones(g, dtype=torch.float32, device=dev)
         self.sqrt_minmax_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
-        # all ranks' bf16 slices, rank-major; this rank's kernel writes straight into its own slot
-        self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
-        self.bf16_shard = self.gathered[rank * n:(rank + 1) * n]
-        self._build_table()
+        # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
+        self._peer_buffer = None
+        self._peer_deltas = None
+        if exchange == "p2p":
+            self._setup_peer_buffer(world_size * n * 2)
+        else:
+            self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
+        self._bucket_all, self._bucket_mine = [], []
+        for b in range(self.n_buckets):
+            lo, hi = int(self.bounds[b]) * GROUP, int(self.bounds[b + 1]) * GROUP
+            whole = self.gathered[lo * world_size: hi * world_size]
+            self._bucket_all.append(whole)
+            self._bucket_mine.append(whole[rank * (hi - lo):(rank + 1) * (hi - lo)])
+        self._comm = torch.cuda.Stream(device=dev) if exchange == "nccl" else None
+        self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if self._comm else []
+        self._table_cache = {}
+        self.set_grad_buffer(self.grad)
 
-    def _build_table(self):
+    def _setup_peer_buffer(self, nbytes):
+        """Allocate this rank's gathered-weights buffer so that peers can map it, swap handles (a
+        collective over the process group) and map every peer's buffer.  A failure on any rank is
+        raised on every rank (the status travels with the collectives), so that callers can switch to
+        exchange="nccl" consistently."""
+        import ctypes
+        import torch.distributed as dist
         L = self._lib
-        rows = np.zeros(len(self.my_pieces), dtype=[(k, np.uint64) for k in
+        err, buf = None, None
+        try:
+            buf = _PeerBuffer(L, nbytes, self.device)
+        except Exception as e:   # reported to every rank below
+            err = f"rank {self.rank}: {e}"
+        mine = (err, buf.handle if buf else None)
+        everyone = [None] * self.world_size
+        dist.all_gather_object(everyone, mine, group=self.process_group)
+        if not any(e for e, _ in everyone):
+            try:
+                for r in range(self.world_size):
+                    if r != self.rank:
+                        buf.open_peer(r, everyone[r][1], self.device)
+            except Exception as e:
+                err = f"rank {self.rank}: {e}"
+        status = [None] * self.world_size
+        # second collective: every rank has mapped (or failed to map) every buffer before anyone steps
+        dist.all_gather_object(status, err or everyone[self.rank][0], group=self.process_group)
+        failed = [e for e in status if e] or [e for e, _ in everyone if e]
+        if failed:
+            if buf:
+                buf.close()
+                dist.barrier(group=self.process_group)
+                buf.free()
+            raise RuntimeError("peer buffers could not be set up: " + "; ".join(failed))
+        self._peer_buffer = buf
+        self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
+        deltas = [buf.peers[r] - buf.ptr for r in range(self.world_size) if r != self.rank]
+        self._peer_deltas = (ctypes.c_int64 * len(deltas))(*deltas)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+
+    def close(self):
+        for r, p in list(self.peers.items()):
+            self._L.lib().coat_peer_buffer_close(p)
+            del self.peers[r]
+
+    def free(self):
+        if self.ptr:
+            self._L.lib().coat_peer_buffer_free(self.ptr)
+            self.ptr = 0
+
+
+class ShardedCoatAdamW:
+    """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
+    weights everywhere.
+
+    exchange="p2p" (the default with more than one rank): ONE kernel per step does both the update and
+    the exchange; it stores its bf16 slice into every peer's copy of `self.gathered` over NVLink while
+    it computes (coat_fp8_adamw_multi_step_bcast), and a one-element all-reduce after it is the
+    barrier that tells every rank that all slices have landed.
+    exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
+    that the gather of bucket b runs under the step of bucket b+1.
+
+    With world_size 1 there is one bucket and no exchange.  Gradients are written by the caller
+    into `self.grad` (already reduce-scattered, as under ZeRO); the updated bf16 weights of ALL ranks
+    appear in `self.gathered` (bucket-major, see ShardPlan.gathered_offset) after step().  No rank may
+    start step k+1 while another still reads the weights of step k from `self.gathered`; in training
+    the gradient reduce-scatter between the two provides that order."""
+
+    def __init__(self, numels, rank=0, world_size=1, device="cuda", lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
+                 weight_decay=1e-2, expand_min=16, use_expansion=True, process_group=None, flags=0,
+                 n_buckets=None, exchange=None):
+        from . import _lib
+        self._lib = _lib
+        self.plan = ShardPlan(numels, world_size)
+        self.rank, self.world_size = rank, world_size
+        self.device = torch.device(device)
+        self.hyper = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, expand_min=expand_min)
+        self.use_expansion = use_expansion
+        self.process_group = process_group
+        self.flags = flags
+        self.step_count = 0
+        if exchange is None:
+            exchange = "p2p" if world_size > 1 else "none"
+        if exchange not in ("none", "p2p", "nccl") or (exchange == "none") != (world_size == 1):
+            raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
+        if exchange == "p2p" and world_size - 1 > _lib.MAX_PEERS:
+            raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
+        self.exchange = exchange
+        if n_buckets is None:
+            n_buckets = 8 if exchange == "nccl" else 1
+        self.bounds = self.plan.bucket_bounds(n_buckets)
+        self.n_buckets = len(self.bounds) - 1
+        self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
+        self.my_pieces = [pc for b in self.my_buckets for pc in b]
+        n, g = self.plan.shard_numel, self.plan.shard_groups
+        dev = self.device
+        self.param = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.grad = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros(n, dtype=torch.uint8, device=dev)
+        self.exp_avg_sq = torch.zeros(n, dtype=torch.uint8, device=dev)
+        self.scale_exp_avg = torch.zeros(g, dtype=torch.float32, device=dev)
+        self.scale_exp_avg_sq = torch.zeros(g, dtype=torch.float32, device=dev)
+        self.expand_exp_avg = torch.ones(g, dtype=torch.float32, device=dev)
+        self.expand_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
+        self.sqrt_minmax_exp_avg = torch.ones(g, dtype=torch.float32, device=dev)
+        self.sqrt_minmax_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
+        # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
+        self._peer_buffer = None
+        self._peer_deltas = None
+        if exchange == "p2p":
+            self._setup_peer_buffer(world_size * n * 2)
+        else:
+            self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
+        self._bucket_all, self._bucket_mine = [], []
+        for b in range(self.n_buckets):
+            lo, hi = int(self.bounds[b]) * GROUP, int(self.bounds[b + 1]) * GROUP
+            whole = self.gathered[lo * world_size: hi * world_size]
+            self._bucket_all.append(whole)
+            self._bucket_mine.append(whole[rank * (hi - lo):(rank + 1) * (hi - lo)])
+        self._comm = torch.cuda.Stream(device=dev) if exchange == "nccl" else None
+        self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if self._comm else []
+        self._table_cache = {}
+        self.set_grad_buffer(self.grad)
+
+    def _setup_peer_buffer(self, nbytes):
+        """Allocate this rank's gathered-weights buffer so that peers can map it, swap handles (a
+        collective over the process group) and map every peer's buffer."""
+        import ctypes
+        import torch.distributed as dist
+        L = self._lib
+        buf = _PeerBuffer(L, nbytes, self.device)
+        self._peer_buffer = buf
+        self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
+        handles = [None] * self.world_size
+        dist.all_gather_object(handles, buf.handle, group=self.process_group)
+        deltas = []
+        for r in range(self.world_size):
+            if r != self.rank:
+                buf.open_peer(r, handles[r], self.device)
+                deltas.append(buf.peers[r] - buf.ptr)
+        self._peer_deltas = (ctypes.c_int64 * len(deltas))(*deltas)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        dist.barrier(group=self.process_group)   # every rank has mapped every buffer before anyone steps
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""
+        if self._peer_buffer is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.device)
+            self._peer_buffer.close()
+            dist.barrier(group=self.process_group)   # nobody maps this buffer any more
+            del self.gathered, self._bucket_all, self._bucket_mine
+            self._peer_buffer.free()
+            self._peer_buffer = None
+
+    def set_grad_buffer(self, grad):
+        """Point the step at another flat gradient buffer of the shard's size (the device-side tensor
+        tables are built once per buffer and reused)."""
+        if grad.numel() != self.plan.shard_numel or grad.dtype != torch.float32:
+            raise ValueError("gradient buffer must be fp32 with the shard's number of elements")
+        self.grad = grad
+        key = grad.data_ptr()
+        if key not in self._table_cache:
+            self._table_cache[key] = [self._build_table(pcs) for pcs in self.my_buckets]
+        self._tables = self._table_cache[key]
+
+    def _build_table(self, pieces):
+        L = self._lib
+        rows = np.zeros(len(pieces), dtype=[(k, np.uint64) for k in
                         ("p", "g", "m", "v", "s_m", "k_m", "r_m", "s_v", "k_v", "r_v", "bf16_out")]
                         + [("numel", np.int64)])
-        prefix = np.zeros(len(self.my_pieces) + 1, dtype=np.int64)
-        for i, pc in enumerate(self.my_pieces):
+        prefix = np.zeros(len(pieces) + 1, dtype=np.int64)
+        for i, pc in enumerate(pieces):
             o, go = pc.offset, pc.offset // GROUP
             r = rows[i]
             r["p"] = self.param.data_ptr() + 4 * o
@@ -131,45 +399,83 @@ class ShardedCoatAdamW:
             r["k_v"] = self.expand_exp_avg_sq.data_ptr() + 4 * go
             r["r_m"] = self.sqrt_minmax_exp_avg.data_ptr() + 4 * go
             r["r_v"] = self.sqrt_minmax_exp_avg_sq.data_ptr() + 4 * go
-            r["bf16_out"] = self.bf16_shard.data_ptr() + 2 * o
+            r["bf16_out"] = self.gathered.data_ptr() + 2 * self.plan.gathered_offset(self.rank, o, self.n_buckets)
             r["numel"] = pc.numel
             prefix[i + 1] = prefix[i] + (pc.numel + GROUP - 1) // GROUP
-        self._table = torch.from_numpy(rows.view(np.uint8).reshape(-1).copy()).to(self.device)
-        self._prefix = torch.from_numpy(prefix).to(self.device)
-        self._total_groups = int(prefix[-1])
         assert L.CoatAdamwTensor  # the row layout above mirrors this ctypes structure
+        return (torch.from_numpy(rows.view(np.uint8).reshape(-1).copy()).to(self.device),
+                torch.from_numpy(prefix).to(self.device), len(pieces), int(prefix[-1]))
+
+    def _launch_bucket(self, b, bcast=False):
+        L = self._lib
+        h = self.hyper
+        table, prefix, n_pieces, n_groups = self._tables[b]
+        if n_pieces == 0:
+            return
+        with torch.cuda.device(self.device):
+            if bcast:
+                rc = L.lib().coat_fp8_adamw_multi_step_bcast(
+                    table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
+                    int(self.use_expansion), h["betas"][0], h["betas"][1], h["lr"], h["weight_decay"], h["eps"],
+                    self.step_count, GROUP, h["expand_min"], L.F32, self.flags, self._peer_deltas,
+                    len(self._peer_deltas), L.stream_ptr(self.device))
+            else:
+                rc = L.lib().coat_fp8_adamw_multi_step(
+                    table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
+                    int(self.use_expansion), h["betas"][0], h["betas"][1], h["lr"], h["weight_decay"], h["eps"],
+                    self.step_count, GROUP, h["expand_min"], L.F32, self.flags, L.stream_ptr(self.device))
+        L.check(rc, "fp8_adamw_multi_step")
 
     def local_step(self):
         """The fused kernel over this rank's slice (no communication)."""
-        L = self._lib
         self.step_count += 1
-        h = self.hyper
-        if not self.my_pieces:
-            return
-        with torch.cuda.device(self.device):
-            rc = L.lib().coat_fp8_adamw_multi_step(
-                self._table.data_ptr(), self._prefix.data_ptr(), len(self.my_pieces), self._total_groups,
-                int(self.use_expansion), h["betas"][0], h["betas"][1], h["lr"], h["weight_decay"], h["eps"],
-                self.step_count, GROUP, h["expand_min"], L.F32, self.flags, L.stream_ptr(self.device))
-        L.check(rc, "fp8_adamw_multi_step")
+        for b in range(self.n_buckets):
+            self._launch_bucket(b)
 
     def gather(self):
         """All-gather of the bf16 slices, in place in `self.gathered`."""
         if self.world_size == 1:
             return
         import torch.distributed as dist
-        dist.all_gather_into_tensor(self.gathered, self.bf16_shard, group=self.process_group)
+        if self.exchange == "p2p":
+            raise RuntimeError("exchange='p2p' has no separate gather: step() does both")
+        for b in range(self.n_buckets):
+            dist.all_gather_into_tensor(self._bucket_all[b], self._bucket_mine[b], group=self.process_group)
 
     def step(self):
-        self.local_step()
-        self.gather()
+        """Step and gather, pipelined by bucket: the collective of bucket b is queued on a side stream
+        behind an event recorded after bucket b's kernel, and runs while bucket b+1 is stepped."""
+        import torch.distributed as dist
+        if self.exchange == "p2p":
+            self.step_count += 1
+            for b in range(self.n_buckets):
+                self._launch_bucket(b, bcast=True)
+            # stream-ordered barrier: it completes on a rank only after every rank's kernel has
+            dist.all_reduce(self._flag, group=self.process_group)
+            return
+        if self.world_size == 1 or self._comm is None:
+            self.local_step()
+            self.gather()
+            return
+        compute = torch.cuda.current_stream(self.device)
+        self._comm.wait_stream(compute)   # readers of the previous step's gathered weights are done
+        self.step_count += 1
+        for b in range(self.n_buckets):
+            self._launch_bucket(b)
+            self._events[b].record(compute)
+            with torch.cuda.stream(self._comm):
+                self._comm.wait_event(self._events[b])
+                dist.all_gather_into_tensor(self._bucket_all[b], self._bucket_mine[b], group=self.process_group)
+        compute.wait_stream(self._comm)
 
     def weight_views(self, shapes):
-        """bf16 views of the full parameter tensors inside `self.gathered`, for tensors that are not
-        split across ranks (a split tensor is returned as the list of its pieces' views)."""
-        n = self.plan.shard_numel
+        """bf16 views of the full parameter tensors inside `self.gathered`: one view for a tensor that
+        lies in one bucket of one rank, else the list of its pieces' views in element order."""
         out = [[] for _ in shapes]
         for r in range(self.world_size):
-            for pc in self.plan.pieces(r):
-                out[pc.tensor].append(self.gathered[r * n + pc.offset: r * n + pc.offset + pc.numel])
-        return [v[0].view(shapes[i]) if len(v) == 1 else v for i, v in enumerate(out)]
+            for pcs in self.plan.bucket_pieces(r, self.n_buckets):
+                for pc in pcs:
+                    o = self.plan.gathered_offset(r, pc.offset, self.n_buckets)
+                    out[pc.tensor].append((pc.start, self.gathered[o:o + pc.numel]))
+        views = [[v for _, v in sorted(lst, key=lambda t: t[0])] for lst in out]
+        return [v[0].view(shapes[i]) if len(v) == 1 else v for i, v in enumerate(views)]

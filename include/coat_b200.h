@@ -29,6 +29,7 @@ extern "C" {
 #define COAT_E_DEVICE (-6)  /* not an sm_100 device / no device                */
 #define COAT_E_TOOBIG (-7)  /* size beyond a documented static maximum         */
 #define COAT_E_TIMEOUT (-8) /* a bounded device-side wait ran out              */
+#define COAT_E_PEER (-9)    /* peer memory could not be allocated / mapped     */
 
 /* ---- dtype enums --------------------------------------------------------- */
 #define COAT_F32 0
@@ -115,6 +116,36 @@ int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int64_t* group
                               float beta1, float beta2, float lr, float wd, float eps,
                               int step, int qgroup, int expand_min, int p_dtype,
                               int flags, void* stream);
+
+/*
+ * The table launch fused with the exchange that follows it under ZeRO-style sharding: besides
+ * bf16_out itself, every bf16 store of the kernel is repeated at bf16_out + peer_deltas[i] bytes,
+ * i < n_peers <= COAT_MAX_PEERS, i.e. into the same slot of peer i's copy of the gathered-weights
+ * buffer (peer_deltas[i] = peer i's mapped base - this GPU's base; multiples of 8).  Plain stores
+ * over NVLink: the kernel never waits on a peer.  The stores have landed when the kernel has
+ * completed on every GPU, so a consumer needs one cross-GPU barrier after the launch (any stream-
+ * ordered collective will do).  peer_deltas is a HOST array, read during the call.  No reference
+ * counterpart (the reference leaves sharding to FSDP).
+ */
+#define COAT_MAX_PEERS 7
+int coat_fp8_adamw_multi_step_bcast(const CoatAdamwTensor* table, const int64_t* group_prefix,
+                                    int n_tensors, int64_t total_groups, int expand,
+                                    float beta1, float beta2, float lr, float wd, float eps,
+                                    int step, int qgroup, int expand_min, int p_dtype,
+                                    int flags, const int64_t* peer_deltas, int n_peers, void* stream);
+
+/*
+ * Set-up helpers for the broadcast step, the only entry points that allocate or synchronise:
+ * a device buffer that other processes of the node can map (CUDA IPC; no multicast object is
+ * created).  create: cudaMalloc + export a COAT_PEER_HANDLE_BYTES handle to send to the peers.
+ * open: map a peer's handle into this process (enables peer access lazily); the returned pointer
+ * is valid on the current device.  close / free undo them; free only after every peer closed.
+ */
+#define COAT_PEER_HANDLE_BYTES 64
+int coat_peer_buffer_create(int64_t bytes, void** ptr_out, void* handle_out);
+int coat_peer_buffer_open(const void* handle, void** ptr_out);
+int coat_peer_buffer_close(void* ptr);
+int coat_peer_buffer_free(void* ptr);
 
 /* =========================== quantizers ====================================
  * x is an M x N row-major matrix of in_dtype (COAT_BF16 / COAT_F16 / COAT_F32) with row stride ldx

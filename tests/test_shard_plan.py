@@ -46,6 +46,64 @@ def test_llama_plan_is_balanced_at_8():
     assert plan.total_groups % 8 == 0 and plan.shard_numel * 8 == 6_738_415_616
 
 
+@pytest.mark.parametrize("world,buckets", [(1, 1), (2, 3), (3, 8), (8, 4), (2, 1000)])
+def test_bucket_pieces_cover_every_element_once(world, buckets):
+    numels = [128 * 5, 77, 128 * 3 + 1, 4096, 1, 128 * 128, 300]
+    plan = ShardPlan(numels, world)
+    bounds = plan.bucket_bounds(buckets) * GROUP
+    assert bounds[0] == 0 and bounds[-1] == plan.shard_numel and (np.diff(bounds) > 0).all()
+    seen = [np.zeros(n, dtype=np.int32) for n in numels]
+    slots = np.zeros(world * plan.shard_numel, dtype=np.int32)
+    for r in range(world):
+        per_bucket = plan.bucket_pieces(r, buckets)
+        assert len(per_bucket) == len(bounds) - 1
+        for b, pcs in enumerate(per_bucket):
+            for pc in pcs:
+                assert pc.numel > 0 and pc.start % GROUP == 0 and pc.offset % GROUP == 0
+                assert bounds[b] <= pc.offset and pc.offset + pc.numel <= bounds[b + 1]
+                seen[pc.tensor][pc.start:pc.stop] += 1
+                o = plan.gathered_offset(r, pc.offset, buckets)
+                # a piece is contiguous in the gathered buffer and lies in its rank's slot of bucket b
+                size = int(bounds[b + 1] - bounds[b])
+                lo = int(bounds[b]) * world + r * size
+                assert lo <= o and o + pc.numel <= lo + size
+                slots[o:o + pc.numel] += 1
+    assert all((s == 1).all() for s in seen)
+    assert slots.max() == 1 and slots.sum() == sum(numels)
+
+
+def _bucketed_gather_worker(rank, world, port, numels, buckets):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = ShardPlan(numels, world)
+        bounds = plan.bucket_bounds(buckets) * GROUP
+        gathered = torch.zeros(world * plan.shard_numel, dtype=torch.bfloat16)
+        for pcs in plan.bucket_pieces(rank, buckets):
+            for pc in pcs:
+                o = plan.gathered_offset(rank, pc.offset, buckets)
+                gathered[o:o + pc.numel] = torch.arange(pc.start, pc.stop).to(torch.bfloat16) + pc.tensor
+        for b in range(len(bounds) - 1):
+            lo, hi = int(bounds[b]), int(bounds[b + 1])
+            whole = gathered[lo * world: hi * world]
+            mine = whole[rank * (hi - lo):(rank + 1) * (hi - lo)]
+            dist.all_gather_into_tensor(whole, mine.clone())
+        for r in range(world):
+            for pcs in plan.bucket_pieces(r, buckets):
+                for pc in pcs:
+                    o = plan.gathered_offset(r, pc.offset, buckets)
+                    want = torch.arange(pc.start, pc.stop).to(torch.bfloat16) + pc.tensor
+                    assert torch.equal(gathered[o:o + pc.numel], want)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bucketed_gather_world2_gloo():
+    numels = [128 * 5, 77, 128 * 3 + 1, 4096, 1, 128 * 9]
+    port = 31500 + os.getpid() % 2000
+    mp.spawn(_bucketed_gather_worker, args=(2, port, numels, 3), nprocs=2, join=True)
+
+
 def _gather_worker(rank, world, port, numels):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
