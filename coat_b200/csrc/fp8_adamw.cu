@@ -549,6 +549,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
 }
+// 1-D bulk copy shared -> global (this GPU's memory or a mapped peer's), tracked by the thread's bulk group.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(dst), "r"(smem_addr(src)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the sources of this thread's committed bulk stores have been read (the staging buffer may be rewritten)
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's committed bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ int g_adamw_device_status = 0;   // set to COAT_E_TIMEOUT if a bounded wait ran out
@@ -632,8 +642,13 @@ __device__ __noinline__ void queue_exact(WarpTile& w, int slot, int lane, uint32
 // Shared memory, not registers, limits how many CTAs share an SM; telling the compiler so lets it use the
 // registers that occupancy leaves free instead of spilling.
 constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(float));
-constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmem + 1024));
-static_assert(kTiledCtasPerSm * (kTiledSmem + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
+// The broadcast variant stages a tile's bf16 weights (256 bytes per group) per warp behind everything else,
+// and sends them to this GPU's buffer and to every peer's with bulk stores of up to a whole tile.
+constexpr size_t kBcastStageBytes = kTile * kGroup * sizeof(__nv_bfloat16);
+constexpr size_t kTiledSmemBcast = kTiledSmem + kTiledWarps * kBcastStageBytes;
+constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmemBcast + 1024));
+static_assert(kTiledSmem % 16 == 0 && kBcastStageBytes % 16 == 0, "bulk copies need 16-byte aligned staging");
+static_assert(kTiledCtasPerSm * (kTiledSmemBcast + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
 
 template <typename scalar_t, bool MULTI, bool BCAST>
 __global__ void __launch_bounds__(kTiledThreads, kTiledCtasPerSm)
@@ -645,6 +660,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     const int warp = threadIdx.x >> 5;
     WarpTile& w = reinterpret_cast<WarpTile*>(smem_raw)[warp];
     float* smem_min = reinterpret_cast<float*>(smem_raw + kTiledWarps * sizeof(WarpTile)) + warp * kGroup;
+    uint2* bf_stage = reinterpret_cast<uint2*>(smem_raw + kTiledSmem + warp * kBcastStageBytes);   // BCAST only
     typedef Elem4<scalar_t> E;
 
     StepConsts c;
@@ -747,6 +763,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
         if (bulk) {
             if (!mbar_wait(&w.mbar, mbar_parity)) {   // bounded; never expected
                 g_adamw_device_status = COAT_E_TIMEOUT;
+                if constexpr (BCAST) bulk_wait_all();
                 return;
             }
             mbar_parity ^= 1u;
@@ -755,6 +772,11 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
 
         // ================= phase 1: lanes over the elements of one group =================
         uint32_t live = 0;   // slots that stay on the fast path (warp-uniform)
+        uint32_t staged = 0;   // BCAST: slots whose bf16 weights wait in bf_stage (warp-uniform)
+        if constexpr (BCAST) {
+            bulk_wait_read();   // the previous tile's bulk stores have read bf_stage (no-op for other lanes)
+            __syncwarp();
+        }
 #pragma unroll 1
         for (int slot = 0; slot < n_slots; ++slot) {
             bool ok = (w.flags[slot] & 3u) == 3u;
@@ -824,7 +846,15 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                         float q[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) q[j] = E::round(p[j]);
-                        store_bf16x4_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q, h);
+                        if (BCAST && (w.ptr_bf[slot] & 15ull) == 0) {   // staged; sent after the loop
+                            uint2 t2;
+                            t2.x = (uint32_t)coat_float_to_bf16_bits(q[0]) | ((uint32_t)coat_float_to_bf16_bits(q[1]) << 16);
+                            t2.y = (uint32_t)coat_float_to_bf16_bits(q[2]) | ((uint32_t)coat_float_to_bf16_bits(q[3]) << 16);
+                            bf_stage[slot * 32 + lane] = t2;
+                            staged |= 1u << slot;
+                        } else {
+                            store_bf16x4_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q, h);
+                        }
                     }
                     w.m1[slot][lane] = make_float4(m1[0], m1[1], m1[2], m1[3]);
                     w.v1[slot][lane] = make_float4(v1[0], v1[1], v1[2], v1[3]);
@@ -848,6 +878,24 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             }
         }
         __syncwarp();
+        if constexpr (BCAST) {
+            if (staged) {
+                fence_proxy_async();   // the staged words (generic stores) become visible to the bulk copies
+                __syncwarp();
+                if (lane <= h.n_peers) {   // lane 0: this GPU's buffer; lane i: peer i-1
+                    const long long delta = lane == 0 ? 0ll : h.peer_delta[lane - 1];
+                    const uint32_t group_bytes = kGroup * (uint32_t)sizeof(__nv_bfloat16);
+                    if (bulk && staged == (1u << n_slots) - 1u) {   // one contiguous run: one store per destination
+                        bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[0]) + delta, bf_stage, (uint32_t)n_slots * group_bytes);
+                    } else {
+                        for (int slot = 0; slot < n_slots; ++slot)
+                            if (staged & (1u << slot))
+                                bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[slot]) + delta, bf_stage + slot * 32, group_bytes);
+                    }
+                    bulk_commit();
+                }
+            }
+        }
         PHASE_CLOCK(1);
         if (live == 0) continue;
         n_fast += __popc(live);
@@ -960,6 +1008,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     if (dbg && lane == 0)
         for (int i = 0; i < 6; ++i) atomicAdd(dbg + 8 + i, (unsigned long long)phase_cycles[i]);
 #endif
+    if constexpr (BCAST) bulk_wait_all();   // this thread's bulk stores are complete before the CTA retires
     if (dbg) {
         n_pend_total = __reduce_add_sync(COAT_FULL_MASK, (unsigned)n_pend_total);
         if (lane == 0) {
@@ -1040,13 +1089,15 @@ int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_
             // the broadcast variant exists for table launches only
             auto kern = (MULTI && h.n_peers > 0) ? fp8_adamw_expand_tiled_kernel<scalar_t, MULTI, MULTI>
                                                  : fp8_adamw_expand_tiled_kernel<scalar_t, MULTI, false>;
-            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTiledSmem) != cudaSuccess)
+            const bool bcast = MULTI && h.n_peers > 0;
+            const size_t smem = bcast ? kTiledSmemBcast : kTiledSmem;
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
                 return COAT_E_LAUNCH;
             const int64_t tiles = (total_groups + kTile - 1) / kTile;
             const int64_t ctas_needed = (tiles + kTiledWarps - 1) / kTiledWarps;
             const int64_t cap = (int64_t)coat_sm_count() * kTiledCtasPerSm;
             const int grid = (int)(ctas_needed < cap ? ctas_needed : cap);
-            kern<<<grid, kTiledThreads, kTiledSmem, st>>>(single, table, prefix, n_tensors, total_groups, h,
+            kern<<<grid, kTiledThreads, smem, st>>>(single, table, prefix, n_tensors, total_groups, h,
                                                           g_debug_counters);
             return coat_launch_status();
         }
@@ -1139,7 +1190,7 @@ extern "C" int coat_fp8_adamw_multi_step_bcast(const CoatAdamwTensor* table, con
     AdamwHyper h = {beta1, beta2, lr, wd, eps, step, expand_min};
     h.n_peers = n_peers;
     for (int i = 0; i < n_peers; ++i) {
-        if (peer_deltas[i] % 8 != 0) return COAT_E_ALIGN;   // 8-byte vector stores keep their alignment
+        if (peer_deltas[i] % 16 != 0) return COAT_E_ALIGN;   // bulk stores keep their 16-byte alignment
         h.peer_delta[i] = peer_deltas[i];
     }
     if (expand)

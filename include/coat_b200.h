@@ -121,8 +121,8 @@ int coat_fp8_adamw_multi_step(const CoatAdamwTensor* table, const int64_t* group
  * The table launch fused with the exchange that follows it under ZeRO-style sharding: besides
  * bf16_out itself, every bf16 store of the kernel is repeated at bf16_out + peer_deltas[i] bytes,
  * i < n_peers <= COAT_MAX_PEERS, i.e. into the same slot of peer i's copy of the gathered-weights
- * buffer (peer_deltas[i] = peer i's mapped base - this GPU's base; multiples of 8).  Plain stores
- * over NVLink: the kernel never waits on a peer.  The stores have landed when the kernel has
+ * buffer (peer_deltas[i] = peer i's mapped base - this GPU's base; multiples of 16).  Bulk
+ * (TMA, non-multicast) and plain stores over NVLink: the kernel never waits on a peer.  The stores have landed when the kernel has
  * completed on every GPU, so a consumer needs one cross-GPU barrier after the launch (any stream-
  * ordered collective will do).  peer_deltas is a HOST array, read during the call.  No reference
  * counterpart (the reference leaves sharding to FSDP).

@@ -142,7 +142,7 @@ def test_broadcast_step_argument_checks():
                                                  _lib.stream_ptr(opt.device))
     assert call([0] * 8, 8) == -1          # more than COAT_MAX_PEERS
     assert call(None, 1) == -1             # peers announced, no deltas
-    assert call([4], 1) == -3              # a delta that breaks the 8-byte store alignment
+    assert call([8], 1) == -3              # a delta that breaks the 16-byte alignment of the bulk stores
     torch.cuda.synchronize()
 
 
