@@ -47,6 +47,48 @@ struct ScaleDivider {
     }
 };
 
+// Division by a group scale that the kernel has just computed as (amax + 1e-10) / fp8_max.  Such a scale is
+// never below 2e-13 and, for finite inputs, never above 8e35, i.e. always inside the range where
+// div.full.f32 equals the multiplication by rcp.approx (and where the flush-to-zero form of the reciprocal
+// gives the same bits); for an infinite amax both forms give 0 for finite x and NaN for infinite x.  So no
+// range guard is needed, and the reciprocal is a single MUFU instruction.
+template <bool IEEE>
+struct GroupScaleDivider {
+    float s, r;
+    __device__ __forceinline__ explicit GroupScaleDivider(float scale) : s(scale), r(0.f) {
+        if (!IEEE) asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(scale));
+    }
+    __device__ __forceinline__ float operator()(float x) const { return IEEE ? __fdiv_rn(x, s) : x * r; }
+    template <int N>
+    __device__ __forceinline__ void apply(const float (&v)[N], float (&q)[N]) const {
+#pragma unroll
+        for (int i = 0; i < N; ++i) q[i] = IEEE ? __fdiv_rn(v[i], s) : v[i] * r;
+    }
+};
+
+// scale = (amax + 1e-10) / fp8_max with the division by the constant hoisted (448 and 57344 are inside the
+// range where div.full.f32 is the multiplication by rcp.approx)
+template <int FMT, bool IEEE>
+struct GroupScale {
+    float r;
+    __device__ __forceinline__ GroupScale() : r(0.f) {
+        if (!IEEE) asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(CoatFp8Max<FMT>::value));
+    }
+    __device__ __forceinline__ float operator()(float amax) const {
+        return IEEE ? __fdiv_rn(amax + kScaleMinThres, CoatFp8Max<FMT>::value) : (amax + kScaleMinThres) * r;
+    }
+};
+
+// max |x| of 16 values as a balanced tree (depth 4 instead of a chain of 16 dependent maxima)
+__device__ __forceinline__ float absmax16(const float (&x)[16]) {
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmaxf(fabsf(x[2 * i]), fabsf(x[2 * i + 1]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[2 * i], m[2 * i + 1]);
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
 // ---- typed 16-element row segments -------------------------------------------------------------
 template <typename T> struct Seg16;
 template <> struct Seg16<__nv_bfloat16> {
@@ -98,6 +140,30 @@ template <> struct Seg16<float> {
     }
     static __device__ __forceinline__ float get(const float* p) { return *p; }
 };
+
+// 8 consecutive elements (16 bytes of a 16-bit type, 32 of fp32) as floats
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(w[i] << 16);
+        x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+__device__ __forceinline__ void load8(const __half* p, float (&x)[8]) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        x[2 * i] = f.x; x[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
 
 // scale stores / loads in the caller's scale dtype (COAT_F32 / COAT_BF16 / COAT_F16)
 __device__ __forceinline__ void store_scale(void* base, int64_t idx, int dtype, float s) {

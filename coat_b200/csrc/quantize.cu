@@ -22,6 +22,7 @@
 // straight and the transposed codes leave in 128-byte rows.
 
 #include "quant_common.cuh"
+#include "tma.cuh"
 
 namespace {
 
@@ -72,6 +73,75 @@ group_quantize_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* __
             // non-negative floats order like their bit patterns
             if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
         }
+    }
+}
+
+// Tensor amax alone (pass 1 of a per-tensor quantize when the caller wants no group scales): each thread
+// takes four 16-element segments, all loads issued before any is used, and for the 16-bit types the maxima
+// are taken on packed pairs without converting to fp32 (max|x| of bf16 values is itself a bf16 value).
+template <typename T> __device__ __forceinline__ float seg_absmax(const uint4& a, const uint4& b);
+template <> __device__ __forceinline__ float seg_absmax<__nv_bfloat16>(const uint4& a, const uint4& b) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    __nv_bfloat162 m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = __hmax2(m[2 * i], m[2 * i + 1]);
+    const __nv_bfloat162 r = __hmax2(__hmax2(m[0], m[1]), __hmax2(m[2], m[3]));
+    return fmaxf(__low2float(r), __high2float(r));
+}
+template <> __device__ __forceinline__ float seg_absmax<__half>(const uint4& a, const uint4& b) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    __half2 m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = __habs2(*reinterpret_cast<const __half2*>(&w[i]));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = __hmax2(m[2 * i], m[2 * i + 1]);
+    const __half2 r = __hmax2(__hmax2(m[0], m[1]), __hmax2(m[2], m[3]));
+    return fmaxf(__low2float(r), __high2float(r));
+}
+
+constexpr int kAmaxSegs = 4;
+template <typename T>
+__global__ void __launch_bounds__(kStraightThreads)
+tensor_amax_kernel(const T* __restrict__ x, unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int64_t ldx) {
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    const int64_t first = (int64_t)blockIdx.x * (kStraightThreads * kAmaxSegs) + threadIdx.x;
+    float amax = 0.f;
+    if constexpr (sizeof(T) == 2) {
+        uint4 a[kAmaxSegs], b[kAmaxSegs];
+#pragma unroll
+        for (int k = 0; k < kAmaxSegs; ++k) {
+            const int64_t seg = first + k * kStraightThreads;
+            if (seg < total) {
+                const uint4* p = reinterpret_cast<const uint4*>(x + seg_offset(seg, segs_per_row, ldx));
+                a[k] = p[0]; b[k] = p[1];
+            } else {
+                a[k] = make_uint4(0, 0, 0, 0); b[k] = make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kAmaxSegs; ++k) amax = fmaxf(amax, seg_absmax<T>(a[k], b[k]));
+    } else {
+#pragma unroll
+        for (int k = 0; k < kAmaxSegs; ++k) {
+            const int64_t seg = first + k * kStraightThreads;
+            if (seg < total) {
+                float v[16];
+                Seg16<T>::load(x + seg_offset(seg, segs_per_row, ldx), v);
+                amax = fmaxf(amax, absmax16(v));
+            }
+        }
+    }
+    amax = coat_warp_max(amax);
+    __shared__ float wmax[kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+        m = coat_warp_max(m);
+        if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));   // non-negative floats order like their bits
     }
 }
 
@@ -251,6 +321,241 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
     }
 }
 
+// TMA-staged persistent kernel for the aligned case (M a multiple of 16, 16-byte aligned outputs).
+// CTA tile 128 x 128, 512 threads, thread = 4 rows x 8 columns, lane = 8*mb + nb (nb: 8-column segment 0..7,
+// mb: 4-row block 0..3), so a warp is 16 rows x 64 columns and warp w sits at rows 16*(w/2), columns 64*(w%2).
+// A CTA walks tiles t = blockIdx.x, + gridDim.x, ...; the 128 x 128 input tile arrives by one 2-D bulk tensor
+// copy (non-multicast) into one of two shared stages while the previous tile is being converted, so loads
+// stay in flight through the compute and store phases (a register-only kernel, which loads, waits, computes
+// and stores in turn, stayed near 40 % of the HBM rate).  Out-of-range rows / columns of edge tiles read as
+// zero.  A 1x16 row group is 2 lanes (xor 1); a 16x1 column group is the 4 lanes mb = 0..3 (xor 8, 16).
+// Packing 4 rows of one column straight into a word gives the transposed word without byte permutes.  The
+// transposed tile crosses shared memory once: row = column of x, 32 words of 4 rows each, rotated by
+// 4 * (column / 8) words so that neither the scatter nor the 16-byte gather has bank conflicts; the
+// transposed scales cross it as [column][row group].  Both are double-buffered: one barrier per tile.
+// 32 warps per SM (2 CTAs) are what hides the latencies of the short dependent chains (shuffles, MUFU,
+// shared memory) of this kernel; with 256 threads per CTA it issued only half of the time.
+constexpr int kWT = 128;
+constexpr int kTmaThreads = 512;
+constexpr int kTmaStages = 2;
+constexpr int kTmaWaitLimit = 1 << 22;
+__device__ int g_quant_device_status = 0;   // COAT_E_TIMEOUT if a bounded wait on a staging copy ran out
+
+// shared memory: input stages | two transposed tiles and two tiles of transposed scales | barriers
+constexpr size_t kTileTBytes = kWT * 32 * sizeof(uint32_t);
+constexpr size_t kScaleTBytes = kWT * 8 * sizeof(float);
+template <typename T> constexpr size_t tma_quant_smem() {
+    return (size_t)kTmaStages * kWT * kWT * sizeof(T) + 2 * kTileTBytes + 2 * kScaleTBytes + 64 + 128 /*alignment slack*/;
+}
+
+template <int FMT>
+__device__ __noinline__ uint32_t div_full_pack4(float a, float b, float c, float d, float s) {
+    return coat_float4_to_fp8x4<FMT>(coat_div_full(a, s), coat_div_full(b, s), coat_div_full(c, s), coat_div_full(d, s));
+}
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_n, int& tm, int& tn) {
+    tm = t / tiles_n;
+    tn = t - tm * tiles_n;
+}
+
+template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT>
+__global__ void __launch_bounds__(kTmaThreads, sizeof(T) == 4 ? 1 : 2)
+transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* __restrict__ y,
+                           uint8_t* __restrict__ y_t, void* __restrict__ s_y, void* __restrict__ s_y_t,
+                           const void* __restrict__ s_in, void* __restrict__ s_out, int scale_dtype,
+                           const unsigned int* __restrict__ amax_bits, int M, int N, int tiles_m, int tiles_n) {
+    const int n_tiles = tiles_m * tiles_n;
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 127) & ~(uintptr_t)127);
+    constexpr uint32_t kStageBytes = kWT * kWT * sizeof(T);
+    unsigned char* after_stages = base + (size_t)kTmaStages * kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(after_stages + 2 * kTileTBytes + 2 * kScaleTBytes);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = lane & 7, mb = lane >> 3;
+    const int m_loc = (warp >> 1) * 16 + mb * 4, n_loc = (warp & 1) * 64 + nb * 8;
+    const int word = ((m_loc >> 2) + 4 * (n_loc >> 3)) & 31;   // rotated slot of this thread's 4 rows
+    const GroupScale<FMT, IEEE> group_scale;
+    float scalar = 1.f;
+    if (!GROUPS) {
+        scalar = amax_bits ? tensor_scale_from_amax<FMT, IEEE>(amax_bits, scale_dtype) : load_scale(s_in, 0, scale_dtype);
+        if (amax_bits && s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scalar);
+    }
+    const ScaleDivider<IEEE> by_scalar(scalar);
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kTmaStages; ++s) coat_tma::mbar_init(&full[s], 1);
+        coat_tma::mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kTmaStages; ++s) {
+            const int t = blockIdx.x + s * gridDim.x;
+            if (t < n_tiles) {
+                int tm, tn;
+                tile_coords(t, tiles_n, tm, tn);
+                coat_tma::mbar_expect_tx(&full[s], kStageBytes);
+                coat_tma::load_2d(base + (size_t)s * kStageBytes, &map_x, tn * kWT, tm * kWT, &full[s]);
+            }
+        }
+    }
+    int k = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++k) {
+        const int s = k % kTmaStages;
+        const T* stage = reinterpret_cast<const T*>(base + (size_t)s * kStageBytes);
+        uint32_t (*tile_t)[32] = reinterpret_cast<uint32_t (*)[32]>(after_stages + (size_t)(k & 1) * kTileTBytes);
+        float (*scale_t)[8] = reinterpret_cast<float (*)[8]>(after_stages + 2 * kTileTBytes + (size_t)(k & 1) * kScaleTBytes);
+        const bool arrived = coat_tma::mbar_wait(&full[s], (uint32_t)(k / kTmaStages) & 1u, kTmaWaitLimit);
+        float v[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) load8(stage + (m_loc + j) * kWT + n_loc, v[j]);
+        int tm, tn;
+        tile_coords(t, tiles_n, tm, tn);
+        const int m_tile = tm * kWT, n_tile = tn * kWT;
+        const int m0 = m_tile + m_loc, n0 = n_tile + n_loc;
+        // M and N are multiples of 16 and a lane pair shares a 16-column group: a 4 x 16 block is in or out as a whole
+        const bool inside = m0 < M && n0 < N;
+        if (GROUPS) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {   // row groups: this lane's 8 columns and its neighbour's
+                float a = fmaxf(fmaxf(fmaxf(fabsf(v[j][0]), fabsf(v[j][1])), fmaxf(fabsf(v[j][2]), fabsf(v[j][3]))),
+                                fmaxf(fmaxf(fabsf(v[j][4]), fabsf(v[j][5])), fmaxf(fabsf(v[j][6]), fabsf(v[j][7]))));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 1));
+                const float rs = group_scale(a);
+                const GroupScaleDivider<IEEE> d(rs);
+                if (inside) {
+                    uint2 w;
+                    w.x = coat_float4_to_fp8x4<FMT>(d(v[j][0]), d(v[j][1]), d(v[j][2]), d(v[j][3]));
+                    w.y = coat_float4_to_fp8x4<FMT>(d(v[j][4]), d(v[j][5]), d(v[j][6]), d(v[j][7]));
+                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
+                    if ((nb & 1) == 0) store_scale(s_y, (int64_t)(m0 + j) * (N >> 4) + (n0 >> 4), scale_dtype, rs);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {   // column groups
+                float a = fmaxf(fmaxf(fabsf(v[0][i]), fabsf(v[1][i])), fmaxf(fabsf(v[2][i]), fabsf(v[3][i])));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 8));
+                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 16));
+                const float cs = group_scale(a);
+                const GroupScaleDivider<IEEE> d(cs);
+                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+                if ((i & 3) == mb) scale_t[n_loc + i][warp >> 1] = cs;   // the four lanes of a group share the stores
+            }
+        } else if (IEEE || by_scalar.fast) {
+            // the usual case, decided once per tile: one multiplication (or IEEE division) per element
+            const GroupScaleDivider<IEEE> d(scalar);
+            if (STRAIGHT && inside) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint2 w;
+                    w.x = coat_float4_to_fp8x4<FMT>(d(v[j][0]), d(v[j][1]), d(v[j][2]), d(v[j][3]));
+                    w.y = coat_float4_to_fp8x4<FMT>(d(v[j][4]), d(v[j][5]), d(v[j][6]), d(v[j][7]));
+                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+        } else {
+            // a caller's scale outside [2^-120, 2^120]: the division instruction itself, out of line
+            if (STRAIGHT && inside) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint2 w;
+                    w.x = div_full_pack4<FMT>(v[j][0], v[j][1], v[j][2], v[j][3], scalar);
+                    w.y = div_full_pack4<FMT>(v[j][4], v[j][5], v[j][6], v[j][7], scalar);
+                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                tile_t[n_loc + i][word] = div_full_pack4<FMT>(v[0][i], v[1][i], v[2][i], v[3][i], scalar);
+        }
+        // The one barrier of the tile: stage s has been read by everyone (it can be refilled) and this tile's
+        // transposed codes and scales are complete.  Tile k+1 writes the other pair of buffers, and nobody
+        // passes the barrier of tile k+1 (after which this pair is written again) before every thread has
+        // finished the readout of tile k below.
+        if (!__syncthreads_and(arrived)) {
+            if (threadIdx.x == 0) {   // never expected; leave only after our copies in flight have landed (bounded)
+                g_quant_device_status = COAT_E_TIMEOUT;
+                for (int q = 0; q < kTmaStages; ++q) {
+                    const int kq = k + q;
+                    if (blockIdx.x + (int64_t)kq * gridDim.x < n_tiles)
+                        coat_tma::mbar_wait(&full[kq % kTmaStages], (uint32_t)(kq / kTmaStages) & 1u, kTmaWaitLimit);
+                }
+            }
+            __syncthreads();
+            return;
+        }
+        if (threadIdx.x == 0) {
+            const int64_t t2 = (int64_t)t + (int64_t)kTmaStages * gridDim.x;
+            if (t2 < n_tiles) {
+                int tm2, tn2;
+                tile_coords((int)t2, tiles_n, tm2, tn2);
+                coat_tma::mbar_expect_tx(&full[s], kStageBytes);
+                coat_tma::load_2d(base + (size_t)s * kStageBytes, &map_x, tn2 * kWT, tm2 * kWT, &full[s]);
+            }
+        }
+        // transposed rows leave in 16-byte pieces: one warp instruction = 4 rows x 128 contiguous bytes
+#pragma unroll
+        for (int it = 0; it < kWT * 8 / kTmaThreads; ++it) {
+            const int idx = it * kTmaThreads + threadIdx.x;
+            const int r = idx >> 3, c = idx & 7;
+            const int n = n_tile + r, m = m_tile + c * 16;
+            if (n < N && m < M)
+                *reinterpret_cast<uint4*>(y_t + (int64_t)n * M + m) =
+                    *reinterpret_cast<const uint4*>(&tile_t[r][(4 * c + 4 * (r >> 3)) & 31]);
+        }
+        if (GROUPS && threadIdx.x < kWT) {   // transposed scales: 8 consecutive row groups per column of x
+            const int n = n_tile + threadIdx.x;
+            const int groups_left = (M - m_tile + 15) >> 4;   // row groups of this tile that exist (1..8, or <= 0)
+            if (n < N && groups_left > 0) {
+                const float4 lo = reinterpret_cast<const float4*>(scale_t[threadIdx.x])[0];
+                const float4 hi = reinterpret_cast<const float4*>(scale_t[threadIdx.x])[1];
+                const float sc[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                const int64_t idx0 = (int64_t)n * (M >> 4) + (m_tile >> 4);
+                if (groups_left >= 8 && scale_dtype == COAT_BF16 && ((idx0 & 7) == 0) &&
+                    (reinterpret_cast<uintptr_t>(s_y_t) & 15) == 0) {
+                    uint4 w;
+                    w.x = (uint32_t)coat_float_to_bf16_bits(sc[0]) | ((uint32_t)coat_float_to_bf16_bits(sc[1]) << 16);
+                    w.y = (uint32_t)coat_float_to_bf16_bits(sc[2]) | ((uint32_t)coat_float_to_bf16_bits(sc[3]) << 16);
+                    w.z = (uint32_t)coat_float_to_bf16_bits(sc[4]) | ((uint32_t)coat_float_to_bf16_bits(sc[5]) << 16);
+                    w.w = (uint32_t)coat_float_to_bf16_bits(sc[6]) | ((uint32_t)coat_float_to_bf16_bits(sc[7]) << 16);
+                    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(s_y_t) + idx0) = w;
+                } else {
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        if (g < groups_left) store_scale(s_y_t, idx0 + g, scale_dtype, sc[g]);
+                }
+            }
+        }
+    }
+}
+
+inline bool tma_tiles_fit(int64_t M, int64_t N) {   // tile counts and coordinates are 32-bit in the kernel
+    return M < (1ll << 31) && N < (1ll << 31) && ((M + kWT - 1) / kWT) * ((N + kWT - 1) / kWT) < (1ll << 30);
+}
+
+// Launch of the TMA-staged kernel; COAT_E_DEVICE when the tensor map cannot be encoded.
+template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT>
+int launch_transpose_tma(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, void* s_y_t, const void* s_in, void* s_out,
+                         int scale_dtype, const unsigned int* amax, int64_t M, int64_t N, int64_t ldx, cudaStream_t st) {
+    CUtensorMap map;
+    if (!coat_tma::make_map_2d(&map, x, (int)sizeof(T), M, N, ldx * (int64_t)sizeof(T), kWT, kWT)) return COAT_E_DEVICE;
+    auto kern = transpose_quant_tma_kernel<T, FMT, IEEE, GROUPS, STRAIGHT>;
+    constexpr size_t smem = tma_quant_smem<T>();
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return COAT_E_LAUNCH;
+    const int64_t tiles_n = (N + kWT - 1) / kWT, tiles_m = (M + kWT - 1) / kWT;
+    const int64_t n_tiles = tiles_n * tiles_m;
+    const int64_t cap = (int64_t)coat_sm_count() * (sizeof(T) == 4 ? 1 : 2);
+    const int grid = (int)(n_tiles < cap ? n_tiles : cap);
+    kern<<<grid, kTmaThreads, smem, st>>>(map, y, y_t, s_y, s_y_t, s_in, s_out, scale_dtype, amax, (int)M, (int)N,
+                                           (int)tiles_m, (int)tiles_n);
+    return coat_launch_status();
+}
+
 // =================================================================================================
 // 5. byte transpose (_transpose.py:39-82)
 // =================================================================================================
@@ -312,6 +617,10 @@ struct GroupQuantArgs {
         if (mode == 0)
             group_quantize_kernel<T, FMT, IEEE, 0><<<grid, kStraightThreads, 0, st>>>(
                 reinterpret_cast<const T*>(x), y, s, scale_dtype, nullptr, M, N, ldx, N, QB);
+        else if (!s)
+            tensor_amax_kernel<T><<<(unsigned)((M * (N / 16) + kStraightThreads * kAmaxSegs - 1) /
+                                               (kStraightThreads * kAmaxSegs)), kStraightThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), amax, M, N, ldx);
         else
             group_quantize_kernel<T, FMT, IEEE, 1><<<grid, kStraightThreads, 0, st>>>(
                 reinterpret_cast<const T*>(x), nullptr, s, scale_dtype, amax, M, N, ldx, N, QB);
@@ -328,6 +637,13 @@ struct DivisionArgs {
                 reinterpret_cast<const T*>(x), y, s_in, s_out, scale_dtype, amax, M, N, ldx, N);
             return coat_launch_status();
         }
+        if (M % 16 == 0 && coat_aligned(y_t, 16) && (!y || coat_aligned(y, 16)) && tma_tiles_fit(M, N)) {
+            if (y)
+                return launch_transpose_tma<T, FMT, IEEE, false, true>(x, y, y_t, nullptr, nullptr, s_in, s_out,
+                                                                       scale_dtype, amax, M, N, ldx, st);
+            return launch_transpose_tma<T, FMT, IEEE, false, false>(x, nullptr, y_t, nullptr, nullptr, s_in, s_out,
+                                                                    scale_dtype, amax, M, N, ldx, st);
+        }
         const dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
         if (y)
             transpose_quant_kernel<T, FMT, IEEE, false, true><<<grid, kTileThreads, 0, st>>>(
@@ -342,6 +658,9 @@ struct DivisionArgs {
 struct QuantTransposeArgs {
     const void* x; uint8_t* y; uint8_t* y_t; void* s_y; void* s_y_t; int scale_dtype; int64_t M, N, ldx; cudaStream_t st;
     template <typename T, int FMT, bool IEEE> int run() const {
+        if (coat_aligned(y, 16) && coat_aligned(y_t, 16) && tma_tiles_fit(M, N))   // M is a multiple of 16 here
+            return launch_transpose_tma<T, FMT, IEEE, true, true>(x, y, y_t, s_y, s_y_t, nullptr, nullptr, scale_dtype,
+                                                                  nullptr, M, N, ldx, st);
         const dim3 grid((unsigned)((N + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
         transpose_quant_kernel<T, FMT, IEEE, true, true><<<grid, kTileThreads, 0, st>>>(
             reinterpret_cast<const T*>(x), y, y_t, s_y, s_y_t, nullptr, nullptr, scale_dtype, nullptr, (int)M, (int)N, ldx);
