@@ -353,6 +353,74 @@ def gemm_extras(torch, device, iters=10):
     return out
 
 
+def layer_extras(torch, device, iters=5):
+    """Forward + backward of ONE Llama-2-7B decoder layer (hidden 4096, 32 heads, MLP 11008) on 4 x 2048 tokens
+    through the FP8 layer of this package, and, beside it, the same layer in plain bf16 torch (cuBLAS GEMMs,
+    SDPA, eager elementwise ops) as a yardstick on the same GPU.  Weights N(0, 0.02), input N(0, 1) * 0.5,
+    upstream gradient N(0, 1e-2); memory-efficient weight mode, first micro-batch (weight scales recomputed)."""
+    import torch.nn.functional as F
+    from coat_b200.activation.real_quantization.func_quantize import Coat_quantize_bgn, Coat_quantize_end
+    from coat_b200.models.coat_llama import CoatLlamaConfig, CoatLlamaDecoderLayer
+    from coat_b200.utils._fp8_quantization_config import QuantizationConfig
+    from coat_b200.utils._fp8manager import FP8Manager
+    Hd, I, heads, B, S = 4096, 11008, 32, 4, 2048
+    qa = dict(group_size=16, weight_memory_efficient=True)
+    cfg = CoatLlamaConfig(hidden_size=Hd, intermediate_size=I, num_attention_heads=heads, coat_fp8_args=qa)
+    torch.manual_seed(3)
+    layer = CoatLlamaDecoderLayer(cfg, 0)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02) if p.dim() == 2 else p.fill_(1.0)
+    layer = layer.to(device, torch.bfloat16).train()
+    qargs = QuantizationConfig(**qa)
+    bgn, end = Coat_quantize_bgn(qargs).train(), Coat_quantize_end(qargs).train()
+    x = (torch.randn(B, S, Hd, device=device) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    up = (torch.randn(B, S, Hd, device=device) * 1e-2).to(torch.bfloat16)
+    FP8Manager.is_first_microbatch = True
+
+    def fp8_step():
+        (h, qh, sh), = layer(*bgn(x))
+        end(h, qh, sh).backward(up)
+
+    w = {n: p.detach().clone().requires_grad_(True) for n, p in layer.named_parameters()}
+
+    def rms(t, g):
+        return F.rms_norm(t, g.shape, g, 1e-5)
+
+    def bf16_step():
+        h = rms(x, w["input_layernorm.weight"])
+        q, k, v = (F.linear(h, w[f"BeforeAttention.{n}_proj.weight"]).view(B, S, heads, Hd // heads).transpose(1, 2)
+                   for n in "qkv")
+        cos, sin = rope
+        rot = lambda t: torch.cat((-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]), dim=-1)
+        q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B, S, Hd)
+        y = x + F.linear(a, w["AfterAttention.o_proj.weight"])
+        h = rms(y, w["post_attention_layernorm.weight"])
+        y = y + F.linear(F.silu(F.linear(h, w["MLPResidual.gate_proj.weight"])) *
+                         F.linear(h, w["MLPResidual.up_proj.weight"]), w["MLPResidual.down_proj.weight"])
+        y.backward(up)
+
+    from coat_b200.models.coat_llama import llama_rotary_embeddings
+    pos = torch.arange(S, device=device)[None, :]
+    rope = tuple(t.unsqueeze(1) for t in llama_rotary_embeddings(pos, Hd // heads, 10000.0, torch.bfloat16))
+    out = {"tokens": B * S}
+    for name, fn in (("fp8_layer", fp8_step), ("bf16_torch_layer", bf16_step)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / iters
+        out[name] = {"fwd_bwd_ms": ms, "tokens_per_s": B * S / (ms / 1e3)}
+    out["fp8_over_bf16"] = out["bf16_torch_layer"]["fwd_bwd_ms"] / out["fp8_layer"]["fwd_bwd_ms"]
+    return out
+
+
 def run_kernel_workload(args):
     """`--workload quantizers|gemm`: only those kernels, for profiling captures and quick checks."""
     import torch
@@ -361,6 +429,8 @@ def run_kernel_workload(args):
     peak, kind = measured_peaks()
     if args.workload == "quantizers":
         extras = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
+    elif args.workload == "layer":
+        extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10)))}
     else:
         extras = {"fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device, iters=max(1, args.steps))}
     print(json.dumps({"metric": "extras only", "config": {"workload": args.workload}, "extras": extras}), flush=True)
@@ -490,7 +560,8 @@ def run_gpu_arm(args):
             del opt, grads
             torch.cuda.empty_cache()
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
-                              "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device)}
+                              "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
+                              "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device)}
         if cpu_v is not None:
             line["cpu_baseline"] = {
                 "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
@@ -507,7 +578,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm"],
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm", "layer"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
@@ -516,7 +587,7 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
-    elif args.workload in ("quantizers", "gemm"):
+    elif args.workload in ("quantizers", "gemm", "layer"):
         run_kernel_workload(args)
     else:
         run_gpu_arm(args)
