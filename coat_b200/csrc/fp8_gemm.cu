@@ -20,19 +20,32 @@
 // through its tear-down (tensor memory is released) before it returns.
 
 #include <cuda.h>
+#include <cstdlib>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 128;       // CTA tile; kBK bytes of K per stage (= one 128B swizzle row)
-constexpr int kStages = 4;
+constexpr int kBN = 256, kBK = 128;                   // CTA tile columns; kBK bytes of K per stage (= one 128B swizzle row)
+// Two tile heights.  BM = 256 (two M=128 MMAs per K step that share the B stage) halves the B traffic per flop:
+// 262 flop per byte pulled from L2 instead of 170, which matters because at 2.3 PFLOP/s the 128-row tile
+// draws ~13 TB/s through L2.  It uses all 512 TMEM columns for one tile, so its epilogue is not overlapped
+// with the next tile's main loop; BM = 128 keeps two accumulators and overlaps them.
+template <int BM> struct GemmShape {
+    static constexpr int kStages = BM == 128 ? 4 : 3;
+    static constexpr int kHalves = BM / 128;                 // M=128 MMAs per K step
+    static constexpr int kBufs = BM == 128 ? 2 : 1;          // accumulator sets in TMEM
+    static constexpr int kEpiWarps = 4 * kHalves;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+    static constexpr uint32_t kStageBytesA = BM * kBK, kStageBytesB = kBN * kBK;
+    static constexpr uint32_t kStageBytes = kStageBytesA + kStageBytesB;
+    // per epilogue warp: 32 rows x 128 bytes of bf16 output (64 columns), staged for a TMA store
+    static constexpr uint32_t kStagingBytes = 4096 * kEpiWarps;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + kStagingBytes + 1024 /*alignment slack*/ + 256 /*barriers*/;
+};
+constexpr int kMaxStages = 4;
 constexpr int kUmmaK = 32;                            // K per tcgen05.mma for 8-bit operands
-constexpr int kGemmThreads = 192;
 constexpr int kTmemCols = 512;                        // two 128 x 256 fp32 accumulators
-constexpr uint32_t kStageBytesA = kBM * kBK, kStageBytesB = kBN * kBK;
-constexpr uint32_t kStageBytes = kStageBytesA + kStageBytesB;
-constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*alignment slack*/ + 256 /*barriers*/;
 constexpr int kWaitLimit = 1 << 20;
 
 __device__ int g_gemm_device_status = 0;
@@ -60,6 +73,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
                  ::"r"(s2u(dst)), "l"(map), "r"(s2u(bar)), "r"(x), "r"(y) : "memory");
 }
+// 2-D tensor store shared -> global (clipped at the tensor's edges), tracked by the issuing thread's bulk group
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(map), "r"(s2u(src)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -106,6 +128,7 @@ struct GemmEpilogue {
     const void* scale_b;
     const void* bias;        // [N] or null
     int scale_dtype, bias_dtype;
+    int tma_store;           // bf16 result leaves through shared memory and TMA stores (map_c is valid)
     int quantize;            // 0: bf16 result, 1: 1xQB FP8 + scales
     int QB;
     int fmt_c;
@@ -176,21 +199,25 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, i
     }
 }
 
-template <int FMT_C>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint32_t idesc,
-                GemmEpilogue e, int tiles_m, int tiles_n) {
+template <int FMT_C, int BM>
+__global__ void __launch_bounds__(GemmShape<BM>::kThreads, 1)
+fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_c, uint32_t idesc, GemmEpilogue e, int tiles_m, int tiles_n) {
     extern __shared__ uint8_t smem_raw[];
     // 128-byte-swizzled TMA destinations and UMMA operands need 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    typedef GemmShape<BM> S;
+    constexpr int kStages = S::kStages, kHalves = S::kHalves, kBufs = S::kBufs;
+    constexpr uint32_t kStageBytesA = S::kStageBytesA, kStageBytesB = S::kStageBytesB, kStageBytes = S::kStageBytes;
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + (size_t)kStages * kStageBytesA;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);
-    uint64_t* full_bar = bars;                      // [kStages] TMA -> MMA
-    uint64_t* empty_bar = bars + kStages;           // [kStages] MMA -> TMA
-    uint64_t* acc_full = bars + 2 * kStages;        // [2] accumulator complete -> epilogue
-    uint64_t* acc_empty = bars + 2 * kStages + 2;   // [2] accumulator drained -> MMA (4 epilogue warps arrive)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 4);
+    uint8_t* staging = smem + (size_t)kStages * kStageBytes;   // 1024-byte aligned: stages are multiples of 1024
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + S::kStagingBytes);
+    uint64_t* full_bar = bars;                         // [kStages] TMA -> MMA
+    uint64_t* empty_bar = bars + kMaxStages;           // [kStages] MMA -> TMA
+    uint64_t* acc_full = bars + 2 * kMaxStages;        // [kBufs] accumulator complete -> epilogue
+    uint64_t* acc_empty = bars + 2 * kMaxStages + 2;   // [kBufs] accumulator drained -> MMA (every epilogue warp arrives)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 4);
     volatile uint32_t* abort_flag = tmem_slot + 1;  // set by whoever gives up waiting; makes every other wait bail out
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -199,7 +226,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], S::kEpiWarps); }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -224,7 +251,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     if (it >= kStages) ok = mbar_wait(&empty_bar[s], ((it / kStages) - 1) & 1, abort_flag);
                     if (!ok) break;
                     mbar_expect_tx(&full_bar[s], kStageBytes);
-                    tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * kBM, &full_bar[s]);
+                    tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * BM, &full_bar[s]);
                     tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, tile_n * kBN, &full_bar[s]);
                 }
             }
@@ -234,11 +261,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             // ---------------- MMA issuer ----------------
             int it = 0, local = 0;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
-                const int buf = local & 1, use = local >> 1;
+                const int buf = local % kBufs, use = local / kBufs;
                 if (use >= 1) ok = mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_flag);   // epilogue has drained it
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t tmem_d = tmem_base + (uint32_t)(buf * kBN);
+                const uint32_t tmem_d = tmem_base + (uint32_t)(buf * kHalves * kBN);
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % kStages;
                     ok = mbar_wait(&full_bar[s], (it / kStages) & 1, abort_flag);
@@ -248,9 +275,13 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                     const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kStageBytesB));
 #pragma unroll
                     for (int k = 0; k < kBK / kUmmaK; ++k) {
-                        // advancing K inside the 128-byte swizzle row: +32 bytes = +2 in the (>>4) address field
-                        umma_f8(tmem_d, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc,
-                                (kb | k) != 0);
+                        // advancing K inside the 128-byte swizzle row: +32 bytes = +2 in the (>>4) address field;
+                        // the second half of a 256-row A stage starts 128 rows x 128 bytes further on
+#pragma unroll
+                        for (int h = 0; h < kHalves; ++h)
+                            umma_f8(tmem_d + (uint32_t)(h * kBN),
+                                    da + (uint64_t)(k * (kUmmaK >> 4)) + (uint64_t)(h * ((128 * kBK) >> 4)),
+                                    db + (uint64_t)(k * (kUmmaK >> 4)), idesc, (kb | k) != 0);
                     }
                     umma_commit(&empty_bar[s]);      // frees the stage once these MMAs have read it
                 }
@@ -258,35 +289,77 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2 .. 2 + 4*kHalves - 1) ----------------
         const int quarter = warp & 3;                         // TMEM lanes this warp may read
+        const int half = (warp - 2) >> 2;                     // which M=128 accumulator of the tile
         const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
         int local = 0;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
             const int tile_m = t % tiles_m, tile_n = t / tiles_m;
-            const int buf = local & 1, use = local >> 1;
+            const int buf = local % kBufs, use = local / kBufs;
             ok = __all_sync(COAT_FULL_MASK, mbar_wait(&acc_full[buf], use & 1, abort_flag));   // warp-uniform
             if (!ok) break;
             tc_fence_after();
-            const int row = tile_m * kBM + quarter * 32 + lane;
+            const int row0 = tile_m * BM + half * 128 + quarter * 32;
+            const int row = row0 + lane;
+            const uint32_t tmem_tile = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((buf * kHalves + half) * kBN);
+            if (e.tma_store) {
+                // bf16 rows are staged 64 columns (128 bytes) at a time in this warp's 32 x 128-byte buffer, in the
+                // 128-byte swizzle the tensor map expects (16-byte unit u of row r sits at unit u ^ (r & 7): the 8
+                // lanes of a quarter-warp hit 8 different bank groups), and one lane hands the box to the TMA unit
+                uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kBN + c * 32), r);
-                float v[32];
-                const int col0 = tile_n * kBN + c * 32;
+                for (int cc = 0; cc < kBN / 64; ++cc) {
+                    if (lane == 0) bulk_wait_read();   // the previous store has read the buffer
+                    __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    v[i] = __uint_as_float(r[i]) * sab;
-                    if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t r[32];
+                        tmem_ld32(tmem_tile + (uint32_t)(cc * 64 + hh * 32), r);
+                        const int col0 = tile_n * kBN + cc * 64 + hh * 32;
+                        uint32_t o[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float a = __uint_as_float(r[2 * i]) * sab, b = __uint_as_float(r[2 * i + 1]) * sab;
+                            if (e.bias) {
+                                if (col0 + 2 * i < e.N) a += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i);
+                                if (col0 + 2 * i + 1 < e.N) b += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i + 1);
+                            }
+                            o[i] = (uint32_t)coat_float_to_bf16_bits(a) | ((uint32_t)coat_float_to_bf16_bits(b) << 16);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            *reinterpret_cast<uint4*>(stg + lane * 128 + (((hh * 4 + j) ^ (lane & 7)) << 4)) =
+                                make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                    }
+                    fence_async_smem();   // this lane's staged words become visible to the TMA unit
+                    __syncwarp();
+                    if (lane == 0 && row0 < e.M && tile_n * kBN + cc * 64 < e.N) {
+                        tma_store_2d(&map_c, stg, tile_n * kBN + cc * 64, row0);
+                        bulk_commit();
+                    }
                 }
-                epilogue_store<FMT_C>(e, row, col0, v);
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem_tile + (uint32_t)(c * 32), r);
+                    float v[32];
+                    const int col0 = tile_n * kBN + c * 32;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        v[i] = __uint_as_float(r[i]) * sab;
+                        if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
+                    }
+                    epilogue_store<FMT_C>(e, row, col0, v);
+                }
             }
             // all of this warp's reads of the accumulator are complete (tcgen05.wait::ld inside tmem_ld32)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s2u(&acc_empty[buf])) : "memory");
         }
+        if (lane == 0) bulk_wait_all();   // this warp's TMA stores are complete before the CTA retires
     }
     if (!ok) { *abort_flag = 1; g_gemm_device_status = COAT_E_TIMEOUT; }
     tc_fence_before();
@@ -314,6 +387,18 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+// Tile height for a problem: 256 rows when COAT_GEMM_BM=256 is set in the environment (experiment switch),
+// else 128.
+int coat_gemm_tile_rows(int64_t M, int64_t N) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char* v = getenv("COAT_GEMM_BM");
+        forced = v ? atoi(v) : 0;
+    }
+    (void)N;
+    return (forced == 256 && M >= 256) ? 256 : 128;
+}
+
 // K-major byte matrix [rows, K] with row pitch K; box = 128 bytes of K x box_rows rows, 128-byte swizzle
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int box_rows) {
     EncodeTiledFn enc = encode_tiled();
@@ -324,6 +409,20 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int bo
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? COAT_OK : COAT_E_BADARG;
+}
+
+// bf16 output [M, N] (row pitch 2N bytes, a multiple of 16): box = 64 columns x 32 rows, 128-byte swizzle
+int make_map_c(CUtensorMap* map, void* base, int64_t M, int64_t N) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return COAT_E_DEVICE;
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)N * 2};
+    const cuuint32_t box[2] = {64, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? COAT_OK : COAT_E_BADARG;
 }
@@ -342,29 +441,40 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     if (!coat_aligned(a, 16) || !coat_aligned(b, 16) || !coat_aligned(c, 16)) return COAT_E_ALIGN;
     if (output_quantize && ((QB != 16 && QB != 32) || N % QB != 0)) return COAT_E_SHAPE;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return COAT_E_TOOBIG;
+    const int bm = coat_gemm_tile_rows(M, N);
     CUtensorMap map_a, map_b;
-    if (int rc = make_map(&map_a, a, M, K, kBM)) return rc;
+    if (int rc = make_map(&map_a, a, M, K, bm)) return rc;
     if (int rc = make_map(&map_b, b, N, K, kBN)) return rc;
     GemmEpilogue e = {};
+    CUtensorMap map_c = map_a;   // placeholder when the TMA-store epilogue is not used
+    if (!output_quantize && N % 8 == 0) {
+        if (int rc = make_map_c(&map_c, c, M, N)) return rc;
+        e.tma_store = 1;
+    }
     e.c = c; e.scale_c = scale_c; e.scale_a = scale_a; e.scale_b = scale_b; e.bias = bias;
     e.scale_dtype = scale_dtype; e.bias_dtype = bias_dtype; e.quantize = output_quantize; e.QB = QB;
     e.fmt_c = fmt_a; e.ieee_div = (flags & COAT_QUANT_IEEE_DIV) ? 1 : 0;
     e.M = (int)M; e.N = (int)N; e.K = (int)K;
-    const uint32_t idesc = make_idesc(fmt_a, fmt_b, kBM, kBN);
-    const int tiles_m = (int)((M + kBM - 1) / kBM), tiles_n = (int)((N + kBN - 1) / kBN);
+    const uint32_t idesc = make_idesc(fmt_a, fmt_b, 128, kBN);
+    const int tiles_m = (int)((M + bm - 1) / bm), tiles_n = (int)((N + kBN - 1) / kBN);
     const int64_t n_tiles = (int64_t)tiles_m * tiles_n;
     const int sms = coat_sm_count();
     const unsigned grid = (unsigned)(n_tiles < sms ? n_tiles : sms);
     cudaStream_t st = (cudaStream_t)stream;
+#define COAT_GEMM_LAUNCH(FMT, BMV)                                                                          \
+    do {                                                                                                  \
+        auto kern = fp8_gemm_kernel<FMT, BMV>;                                                            \
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                       \
+                                 (int)GemmShape<BMV>::kSmem) != cudaSuccess)                              \
+            return COAT_E_LAUNCH;                                                                         \
+        kern<<<grid, GemmShape<BMV>::kThreads, GemmShape<BMV>::kSmem, st>>>(map_a, map_b, map_c, idesc, e, tiles_m, tiles_n); \
+    } while (0)
     if (fmt_a == COAT_E4M3) {
-        if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E4M3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
-            return COAT_E_LAUNCH;
-        fp8_gemm_kernel<COAT_E4M3><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e, tiles_m, tiles_n);
+        if (bm == 256) COAT_GEMM_LAUNCH(COAT_E4M3, 256); else COAT_GEMM_LAUNCH(COAT_E4M3, 128);
     } else {
-        if (cudaFuncSetAttribute(fp8_gemm_kernel<COAT_E5M2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
-            return COAT_E_LAUNCH;
-        fp8_gemm_kernel<COAT_E5M2><<<grid, kGemmThreads, kGemmSmem, st>>>(map_a, map_b, idesc, e, tiles_m, tiles_n);
+        if (bm == 256) COAT_GEMM_LAUNCH(COAT_E5M2, 256); else COAT_GEMM_LAUNCH(COAT_E5M2, 128);
     }
+#undef COAT_GEMM_LAUNCH
     return coat_launch_status();
 }
 
