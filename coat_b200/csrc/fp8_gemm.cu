@@ -121,6 +121,51 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The sequence of work items of one CTA.  A unit is a 128-row x 256-column block of C; tiles are numbered down
+// the rows first, and CTA b takes tiles b, b + gridDim, ... so that the tiles in flight at any time are
+// neighbours that share operand tiles in L2 (handing each CTA a contiguous range instead was measured 5-10 %
+// slower).  BM = 128: a tile is one unit.  BM = 256: a tile is two vertically adjacent units (one at an odd
+// matrix edge); when the last, partial round has at most gridDim / 2 tiles, they are split into their units
+// so that the round costs half a tile.
+template <int BM>
+struct TileWalk {
+    int k, rounds, rest, units_m, tiles_m;
+    __device__ TileWalk(int units_m_, int units_n) : k(0), units_m(units_m_) {
+        tiles_m = BM == 128 ? units_m_ : (units_m_ + 1) / 2;
+        const int total = tiles_m * units_n;
+        rounds = total / (int)gridDim.x;
+        rest = total - rounds * (int)gridDim.x;
+    }
+    __device__ void decode(int t, int& unit_m, int& unit_n, int& halves) const {
+        const int tm = t % tiles_m;
+        unit_n = t / tiles_m;
+        unit_m = BM == 128 ? tm : 2 * tm;
+        halves = BM == 128 ? 1 : (units_m - unit_m >= 2 ? 2 : 1);
+    }
+    // false when the CTA is done; else the item's first block row, its block column and its height in units
+    __device__ bool next(int& unit_m, int& unit_n, int& halves) {
+        const int b = blockIdx.x, P = gridDim.x;
+        if (k < rounds) {
+            decode(b + k * P, unit_m, unit_n, halves);
+            ++k;
+            return true;
+        }
+        if (k > rounds || rest == 0) return false;
+        ++k;
+        if (BM == 256 && 2 * rest <= P) {   // split the last tiles into their units
+            if (b >= 2 * rest) return false;
+            decode(rounds * P + (b >> 1), unit_m, unit_n, halves);
+            if ((b & 1) >= halves) return false;
+            unit_m += b & 1;
+            halves = 1;
+            return true;
+        }
+        if (b >= rest) return false;
+        decode(rounds * P + b, unit_m, unit_n, halves);
+        return true;
+    }
+};
+
 struct GemmEpilogue {
     void* c;                 // bf16 [M,N] or FP8 codes [M,N]
     void* scale_c;           // bf16 [M, N/QB] when quantising
@@ -222,7 +267,6 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int k_blocks = (e.K + kBK - 1) / kBK;
-    const int n_tiles = tiles_m * tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
@@ -244,15 +288,18 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             int it = 0;
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            TileWalk<BM> walk(tiles_m, tiles_n);
+            int unit_m, unit_n, halves;
+            while (ok && walk.next(unit_m, unit_n, halves)) {
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % kStages;
                     if (it >= kStages) ok = mbar_wait(&empty_bar[s], ((it / kStages) - 1) & 1, abort_flag);
                     if (!ok) break;
-                    mbar_expect_tx(&full_bar[s], kStageBytes);
-                    tma_load_2d(smem_a + (size_t)s * kStageBytesA, &map_a, kb * kBK, tile_m * BM, &full_bar[s]);
-                    tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, tile_n * kBN, &full_bar[s]);
+                    mbar_expect_tx(&full_bar[s], (uint32_t)halves * (128 * kBK) + kStageBytesB);
+                    for (int h = 0; h < halves; ++h)   // A arrives in 128-row boxes, one per unit of the item
+                        tma_load_2d(smem_a + (size_t)s * kStageBytesA + (size_t)h * (128 * kBK), &map_a, kb * kBK,
+                                    (unit_m + h) * 128, &full_bar[s]);
+                    tma_load_2d(smem_b + (size_t)s * kStageBytesB, &map_b, kb * kBK, unit_n * kBN, &full_bar[s]);
                 }
             }
         }
@@ -260,7 +307,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             int it = 0, local = 0;
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
+            TileWalk<BM> walk(tiles_m, tiles_n);
+            int unit_m, unit_n, halves;
+            for (; ok && walk.next(unit_m, unit_n, halves); ++local) {
                 const int buf = local % kBufs, use = local / kBufs;
                 if (use >= 1) ok = mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_flag);   // epilogue has drained it
                 if (!ok) break;
@@ -279,7 +328,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
                         // the second half of a 256-row A stage starts 128 rows x 128 bytes further on
 #pragma unroll
                         for (int h = 0; h < kHalves; ++h)
-                            umma_f8(tmem_d + (uint32_t)(h * kBN),
+                            if (h < halves) umma_f8(tmem_d + (uint32_t)(h * kBN),
                                     da + (uint64_t)(k * (kUmmaK >> 4)) + (uint64_t)(h * ((128 * kBK) >> 4)),
                                     db + (uint64_t)(k * (kUmmaK >> 4)), idesc, (kb | k) != 0);
                     }
@@ -294,16 +343,19 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         const int half = (warp - 2) >> 2;                     // which M=128 accumulator of the tile
         const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
         int local = 0;
-        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++local) {
-            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+        TileWalk<BM> walk(tiles_m, tiles_n);
+        int unit_m, tile_n, halves;
+        for (; ok && walk.next(unit_m, tile_n, halves); ++local) {
             const int buf = local % kBufs, use = local / kBufs;
             ok = __all_sync(COAT_FULL_MASK, mbar_wait(&acc_full[buf], use & 1, abort_flag));   // warp-uniform
             if (!ok) break;
             tc_fence_after();
-            const int row0 = tile_m * BM + half * 128 + quarter * 32;
+            const int row0 = (unit_m + half) * 128 + quarter * 32;
             const int row = row0 + lane;
             const uint32_t tmem_tile = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((buf * kHalves + half) * kBN);
-            if (e.tma_store) {
+            if (half >= halves) {
+                // a single unit: the warps of the second accumulator have nothing to drain
+            } else if (e.tma_store) {
                 // bf16 rows are staged 64 columns (128 bytes) at a time in this warp's 32 x 128-byte buffer, in the
                 // 128-byte swizzle the tensor map expects (16-byte unit u of row r sits at unit u ^ (r & 7): the 8
                 // lanes of a quarter-warp hit 8 different bank groups), and one lane hands the box to the TMA unit
@@ -387,16 +439,27 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// Tile height for a problem: 256 rows when COAT_GEMM_BM=256 is set in the environment (experiment switch),
-// else 128.
-int coat_gemm_tile_rows(int64_t M, int64_t N) {
+// Tile height for a problem.  Cost model in units of "one 128-row unit done by the 128-row kernel": that kernel
+// overlaps its epilogue and takes ceil(units / SMs) rounds of one unit; the 256-row kernel does a unit in about
+// 0.785 + 939 / K of that time (less shared-memory traffic per flop, but an exposed epilogue; fitted to
+// measurements at K = 4096, 8192 and 11008), takes rounds of two units and, when its last round is at most half
+// full, finishes it in about 1.5 units' time (a single unit still loads a whole B stage per K block).
+// COAT_GEMM_BM=128|256 in the environment overrides the choice.
+int coat_gemm_tile_rows(int64_t M, int64_t N, int64_t K) {
     static int forced = -1;
     if (forced < 0) {
         const char* v = getenv("COAT_GEMM_BM");
         forced = v ? atoi(v) : 0;
     }
-    (void)N;
-    return (forced == 256 && M >= 256) ? 256 : 128;
+    if (M <= 128) return 128;
+    if (forced == 128 || forced == 256) return forced;
+    const int64_t units_m = (M + 127) / 128, units_n = (N + kBN - 1) / kBN, sms = coat_sm_count();
+    const int64_t units = units_m * units_n, tiles = ((units_m + 1) / 2) * units_n;
+    const double cost128 = (double)((units + sms - 1) / sms);
+    const int64_t full = tiles / sms, rest = tiles % sms;
+    const double rounds256 = 2.0 * full + (rest == 0 ? 0.0 : (2 * rest <= sms ? 1.5 : 2.0));
+    const double cost256 = rounds256 * (0.785 + 939.0 / (double)K);
+    return cost256 < cost128 ? 256 : 128;
 }
 
 // K-major byte matrix [rows, K] with row pitch K; box = 128 bytes of K x box_rows rows, 128-byte swizzle
@@ -441,9 +504,9 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     if (!coat_aligned(a, 16) || !coat_aligned(b, 16) || !coat_aligned(c, 16)) return COAT_E_ALIGN;
     if (output_quantize && ((QB != 16 && QB != 32) || N % QB != 0)) return COAT_E_SHAPE;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return COAT_E_TOOBIG;
-    const int bm = coat_gemm_tile_rows(M, N);
+    const int bm = coat_gemm_tile_rows(M, N, K);
     CUtensorMap map_a, map_b;
-    if (int rc = make_map(&map_a, a, M, K, bm)) return rc;
+    if (int rc = make_map(&map_a, a, M, K, 128)) return rc;   // A always arrives in 128-row boxes
     if (int rc = make_map(&map_b, b, N, K, kBN)) return rc;
     GemmEpilogue e = {};
     CUtensorMap map_c = map_a;   // placeholder when the TMA-store epilogue is not used
@@ -456,10 +519,12 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     e.fmt_c = fmt_a; e.ieee_div = (flags & COAT_QUANT_IEEE_DIV) ? 1 : 0;
     e.M = (int)M; e.N = (int)N; e.K = (int)K;
     const uint32_t idesc = make_idesc(fmt_a, fmt_b, 128, kBN);
-    const int tiles_m = (int)((M + bm - 1) / bm), tiles_n = (int)((N + kBN - 1) / kBN);
-    const int64_t n_tiles = (int64_t)tiles_m * tiles_n;
+    // work is counted in units of 128 rows x 256 columns for both tile heights
+    const int tiles_m = (int)((M + 127) / 128), tiles_n = (int)((N + kBN - 1) / kBN);
+    const int64_t n_units = (int64_t)tiles_m * tiles_n;
+    if (n_units > 0x7fffffff) return COAT_E_TOOBIG;
     const int sms = coat_sm_count();
-    const unsigned grid = (unsigned)(n_tiles < sms ? n_tiles : sms);
+    const unsigned grid = (unsigned)(n_units < sms ? n_units : sms);
     cudaStream_t st = (cudaStream_t)stream;
 #define COAT_GEMM_LAUNCH(FMT, BMV)                                                                          \
     do {                                                                                                  \
