@@ -422,6 +422,216 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     }
 }
 
+// =====================================================================================================
+// CTA-pair kernel: two CTAs of a cluster (two SMs) work on one 256 x 256 tile with tcgen05.mma.cta_group::2.
+// CTA r of the pair stages rows [128 r, 128 r + 128) of the A tile and of the B tile (so each SM writes and
+// reads half of B: 128 B/clk of shared-memory traffic per SM instead of 192), its tensor memory holds rows
+// [128 r, 128 r + 128) x 256 columns of the accumulator (two buffers), and its four epilogue warps drain and
+// store them.  Only the leader (rank 0) issues MMAs.  Signalling:
+//   full[s]      (leader's only) one expect_tx by the leader's producer for the bytes of BOTH CTAs; the peer's
+//                loads complete on the leader's barrier too (TMA loads with .cta_group::2, no multicast)
+//   empty[s]     in both CTAs, arrived by the leader's tcgen05.commit with a CTA mask of both
+//   acc_full[b]  in both CTAs, same mechanism
+//   acc_empty[b] (leader's only) 8 arrivals: the 4 epilogue warps of each CTA (the peer's arrive remotely)
+// Every wait is bounded as in the single-CTA kernel; the pair synchronises (barrier.cluster) after set-up and
+// before tensor memory is released, so that neither CTA leaves while its partner may still signal or read it.
+// =====================================================================================================
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStageA = 128 * kBK, kPairStageB = 128 * kBK, kPairStageBytes = kPairStageA + kPairStageB;
+constexpr uint32_t kPairStaging = 4 * 4096;
+constexpr size_t kPairSmem = (size_t)kPairStages * kPairStageBytes + kPairStaging + 1024 + 256;
+constexpr int kPairThreads = 192;
+
+__device__ __forceinline__ uint32_t cluster_rank() { uint32_t r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load of a CTA of a pair: data into this CTA's shared memory, completion bytes onto `bar_cluster_addr`,
+// which may be the partner's barrier
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster_addr) {
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 ::"r"(s2u(dst)), "l"(map), "r"(bar_cluster_addr), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void umma_f8_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p; }"
+                 ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on the barrier at this shared-memory offset in every CTA of `mask` once the MMAs issued so far are done
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(s2u(bar)), "h"(mask) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
+template <int FMT_C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_c, uint32_t idesc, GemmEpilogue e, int tiles_m, int tiles_n) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + (size_t)kPairStages * kPairStageA;
+    uint8_t* staging = smem + (size_t)kPairStages * kPairStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + kPairStaging);
+    uint64_t* full_bar = bars;                          // [kPairStages] used in the leader only
+    uint64_t* empty_bar = bars + kPairStages;           // [kPairStages] both CTAs
+    uint64_t* acc_full = bars + 2 * kPairStages;        // [2] both CTAs
+    uint64_t* acc_empty = bars + 2 * kPairStages + 2;   // [2] used in the leader only
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kPairStages + 4);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int k_blocks = (e.K + kBK - 1) / kBK;
+    const int n_tiles = tiles_m * tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {   // one warp of EACH CTA of the pair takes part in the allocation
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s2u(tmem_slot)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();   // both CTAs' barriers exist before anything signals them
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int it = 0;
+            for (int t = pair; t < n_tiles && ok; t += n_pairs) {
+                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    if (it >= kPairStages) ok = mbar_wait(&empty_bar[s], ((it / kPairStages) - 1) & 1, abort_flag);
+                    if (!ok) break;
+                    if (rank == 0) mbar_expect_tx(&full_bar[s], 2 * kPairStageBytes);
+                    const uint32_t leader_full = map_to_cta(s2u(&full_bar[s]), 0);
+                    tma_load_2d_pair(smem_a + (size_t)s * kPairStageA, &map_a, kb * kBK, tile_m * 256 + (int)rank * 128, leader_full);
+                    tma_load_2d_pair(smem_b + (size_t)s * kPairStageB, &map_b, kb * kBK, tile_n * 256 + (int)rank * 128, leader_full);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (leader only) ----------------
+            int it = 0, local = 0;
+            for (int t = pair; t < n_tiles && ok; t += n_pairs, ++local) {
+                const int buf = local & 1, use = local >> 1;
+                if (use >= 1) ok = mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)(buf * kBN);
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    ok = mbar_wait(&full_bar[s], (it / kPairStages) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t da = make_smem_desc(s2u(smem_a + (size_t)s * kPairStageA));
+                    const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kPairStageB));
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k)
+                        umma_f8_pair(tmem_d, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc,
+                                     (kb | k) != 0);
+                    umma_commit_pair(&empty_bar[s], 3);      // frees the stage in both CTAs
+                }
+                if (ok) umma_commit_pair(&acc_full[buf], 3);  // both CTAs' epilogues may drain their halves
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        const int quarter = warp & 3;
+        const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
+        uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
+        int local = 0;
+        for (int t = pair; t < n_tiles && ok; t += n_pairs, ++local) {
+            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            const int buf = local & 1, use = local >> 1;
+            ok = __all_sync(COAT_FULL_MASK, mbar_wait(&acc_full[buf], use & 1, abort_flag));
+            if (!ok) break;
+            tc_fence_after();
+            const int row0 = tile_m * 256 + (int)rank * 128 + quarter * 32;
+            const int row = row0 + lane;
+            const uint32_t tmem_tile = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kBN);
+            if (e.tma_store) {
+#pragma unroll 1
+                for (int cc = 0; cc < kBN / 64; ++cc) {
+                    if (lane == 0) bulk_wait_read();
+                    __syncwarp();
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t r[32];
+                        tmem_ld32(tmem_tile + (uint32_t)(cc * 64 + hh * 32), r);
+                        const int col0 = tile_n * kBN + cc * 64 + hh * 32;
+                        uint32_t o[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float a = __uint_as_float(r[2 * i]) * sab, b = __uint_as_float(r[2 * i + 1]) * sab;
+                            if (e.bias) {
+                                if (col0 + 2 * i < e.N) a += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i);
+                                if (col0 + 2 * i + 1 < e.N) b += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i + 1);
+                            }
+                            o[i] = (uint32_t)coat_float_to_bf16_bits(a) | ((uint32_t)coat_float_to_bf16_bits(b) << 16);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            *reinterpret_cast<uint4*>(stg + lane * 128 + (((hh * 4 + j) ^ (lane & 7)) << 4)) =
+                                make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && row0 < e.M && tile_n * kBN + cc * 64 < e.N) {
+                        tma_store_2d(&map_c, stg, tile_n * kBN + cc * 64, row0);
+                        bulk_commit();
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem_tile + (uint32_t)(c * 32), r);
+                    float v[32];
+                    const int col0 = tile_n * kBN + c * 32;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        v[i] = __uint_as_float(r[i]) * sab;
+                        if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
+                    }
+                    epilogue_store<FMT_C>(e, row, col0, v);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_cta(s2u(&acc_empty[buf]), 0));   // the leader's barrier
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+    if (!ok) { *abort_flag = 1; g_gemm_device_status = COAT_E_TIMEOUT; }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();   // the partner has finished signalling this CTA and reading its shared memory
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
 // ---- host side ------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -490,6 +700,50 @@ int make_map_c(CUtensorMap* map, void* base, int64_t M, int64_t N) {
     return r == CUDA_SUCCESS ? COAT_OK : COAT_E_BADARG;
 }
 
+// Which kernel serves a problem.  Measured on the Llama-2-7B MLP shapes (burst / sustained under the 1 kW power
+// cap, TFLOP/s): forward K=4096: pair 2869 / 2551, 128-row 2798 / 2471, 256-row 2655 / 2349; dgrad K=11008:
+// 256-row 2720 / 2392, pair 2640 / 2333, 128-row 2535 / 2263; wgrad K=8192: 256-row 2650 / 2330, pair 2507 /
+// 2230, 128-row 2339 / 2117.  So: CTA pairs for short reductions, the 256-row tile for long ones, the 128-row
+// tile for matrices of at most 128 rows.  COAT_GEMM_PAIR=0|1 and COAT_GEMM_BM=128|256 in the environment
+// override the choice (experiments).
+bool coat_gemm_use_pair(int64_t M, int64_t K) {
+    static int pair = -2, bm = -1;
+    if (pair == -2) {
+        const char* v = getenv("COAT_GEMM_PAIR");
+        pair = v ? atoi(v) : -1;
+        const char* w = getenv("COAT_GEMM_BM");
+        bm = w ? atoi(w) : 0;
+    }
+    if (M <= 128) return false;
+    if (pair == 0 || pair == 1) return pair == 1;
+    if (bm == 128 || bm == 256) return false;
+    return K < 6144;
+}
+
+template <int FMT_C>
+int launch_pair(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_c, uint32_t idesc,
+                const GemmEpilogue& e, int tiles_m, int tiles_n, int64_t tiles, cudaStream_t st) {
+    auto kern = fp8_gemm_pair_kernel<FMT_C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem) != cudaSuccess)
+        return COAT_E_LAUNCH;
+    // how many pairs the device can hold at once (SM counts per GPC need not be even)
+    static int max_pairs[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return COAT_E_DEVICE;
+    if (max_pairs[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)(coat_sm_count() / 2));
+        cfg.blockDim = dim3(kPairThreads);
+        cfg.dynamicSmemBytes = kPairSmem;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) { cudaGetLastError(); return COAT_E_LAUNCH; }
+        max_pairs[dev] = n;
+    }
+    const int64_t pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
+    kern<<<(unsigned)(2 * pairs), kPairThreads, kPairSmem, st>>>(map_a, map_b, map_c, idesc, e, tiles_m, tiles_n);
+    return coat_launch_status();
+}
+
 }  // namespace
 
 extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* scale_c, const void* scale_a,
@@ -526,6 +780,18 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     const int sms = coat_sm_count();
     const unsigned grid = (unsigned)(n_units < sms ? n_units : sms);
     cudaStream_t st = (cudaStream_t)stream;
+    if (coat_gemm_use_pair(M, K)) {
+        // CTA pairs: 256 x 256 tiles, A and B both in 128-row boxes, instruction shape M256 N256
+        CUtensorMap map_b2;
+        if (int rc = make_map(&map_b2, b, N, K, 128)) return rc;
+        const uint32_t idesc2 = make_idesc(fmt_a, fmt_b, 256, kBN);
+        const int tm = (int)((M + 255) / 256);
+        const int64_t tiles = (int64_t)tm * tiles_n;
+        int rc = COAT_E_LAUNCH;
+        if (fmt_a == COAT_E4M3) rc = launch_pair<COAT_E4M3>(map_a, map_b2, map_c, idesc2, e, tm, tiles_n, tiles, st);
+        else rc = launch_pair<COAT_E5M2>(map_a, map_b2, map_c, idesc2, e, tm, tiles_n, tiles, st);
+        return rc;
+    }
 #define COAT_GEMM_LAUNCH(FMT, BMV)                                                                          \
     do {                                                                                                  \
         auto kern = fp8_gemm_kernel<FMT, BMV>;                                                            \
