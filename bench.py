@@ -186,7 +186,7 @@ def fill_synthetic(opt, shapes, torch):
 def e2e_public_api(torch, device, steps, warmup):
     """params/s through the public optimizer API (CoatAdamW.step) with HOST gradients: every step copies
     the gradients of one Llama-2-7B decoder layer (9 tensors, 202 383 360 params) from pinned host memory
-    and reads the updated fp32 weights back to pinned host memory."""
+    and reads the updated fp32 weights back to pinned host memory (all of both inside the timed region)."""
     from coat_b200.optimizer import CoatAdamW
     H, I = 4096, 11008
     shapes = [(H, H)] * 4 + [(I, H), (I, H), (H, I), (H,), (H,)]
@@ -199,23 +199,49 @@ def e2e_public_api(torch, device, steps, warmup):
     opt = CoatAdamW(params, **HYPER)
     n = sum(numel(s) for s in shapes)
 
+    # Three streams: gradients in, step, weights out.  The copy-in of step k+1 and the copy-out of step k both
+    # wait only for the kernel of step k, so they share the two directions of the link; the kernel of step k+1
+    # waits for both (it overwrites the weights that are being read out and consumes the new gradients).
+    s_in, s_step, s_out = (torch.cuda.Stream(device=device) for _ in range(3))
+    ev_in, ev_step, ev_out = (torch.cuda.Event() for _ in range(3))
+    s_step.wait_stream(torch.cuda.current_stream(device))
+    ev_step.record(s_step)
+    ev_out.record(s_out)
+
     def one():
-        for p, hg in zip(params, host_g):
-            p.grad.copy_(hg, non_blocking=True)
-        opt.step()
-        for p, hp in zip(params, host_p):
-            hp.copy_(p.detach(), non_blocking=True)
+        s_in.wait_event(ev_step)            # the previous step no longer reads the gradient buffers
+        with torch.cuda.stream(s_in):
+            for p, hg in zip(params, host_g):
+                p.grad.copy_(hg, non_blocking=True)
+            ev_in.record(s_in)
+        s_step.wait_event(ev_in)
+        s_step.wait_event(ev_out)           # the previous weights have been read out
+        with torch.cuda.stream(s_step):
+            opt.step()
+            ev_step.record(s_step)
+        s_out.wait_event(ev_step)
+        with torch.cuda.stream(s_out):
+            for p, hp in zip(params, host_p):
+                hp.copy_(p.detach(), non_blocking=True)
+            ev_out.record(s_out)
+
+    def drain():
+        for st in (s_in, s_step, s_out):
+            st.synchronize()
 
     for _ in range(max(warmup, 2)):
         one()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    drain()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(s_step)
+    s_in.wait_event(t0)
     for _ in range(steps):
         one()
-    e1.record()
-    torch.cuda.synchronize(device)
-    ms = e0.elapsed_time(e1) / steps
+    s_step.wait_stream(s_out)               # the timed region ends when the last weights have arrived
+    t1.record(s_step)
+    drain()
+    ms = t0.elapsed_time(t1) / steps
     return n / (ms / 1e3), 4 * n, 4 * n, n
 
 
