@@ -169,7 +169,7 @@ def run_reference_arm(args):
 # GPU arm
 # ------------------------------------------------------------------------------------------------
 
-NCU_DRAM_BYTES_PER_PARAM = 261.86e6 / (4096 * 4096)
+NCU_DRAM_BYTES_PER_PARAM = 264.47e6 / (4096 * 4096)
 
 
 def fill_synthetic(opt, shapes, torch):
@@ -564,7 +564,7 @@ def run_gpu_arm(args):
         peak, peak_kind = measured_peaks()
         achieved = my_params * BYTES_PER_PARAM_BF16 / (kernel_ms / 1e3) / 1e9
         # DRAM bytes per parameter of this kernel as ncu measured them on the 4096x4096 case
-        # (dram__bytes_read.sum + dram__bytes_write.sum = 261.9 MB for 16 777 216 parameters,
+        # (dram__bytes_read.sum + dram__bytes_write.sum = 264.5 MB for 16 777 216 parameters,
         # profiles/fp8_adamw_expand_tiled_c1.md), scaled to this launch by its parameter count
         traffic = NCU_DRAM_BYTES_PER_PARAM * my_params
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
