@@ -242,7 +242,7 @@ def e2e_public_api(torch, device, steps, warmup):
     t1.record(s_step)
     drain()
     ms = t0.elapsed_time(t1) / steps
-    return n / (ms / 1e3), 4 * n, 4 * n, n
+    return ms, 4 * n, 4 * n, n
 
 
 def quantizer_extras(torch, device, peak):
@@ -560,6 +560,16 @@ def run_gpu_arm(args):
     n_launches = args.steps * opt.n_buckets
     opt.close()   # collective: unmaps the peers' buffers
 
+    # end to end through the public API with host buffers: every rank steps its own copy of one decoder layer
+    # over its own PCIe link at the same time; the job's rate is all ranks' parameters over the slowest rank's time
+    e2e_v, h2d, d2h, e2e_n = None, 0, 0, 0
+    if not args.kernel_only:
+        e2e_ms, h2d, d2h, e2e_n = e2e_public_api(torch, device, max(3, min(args.steps, 10)), args.warmup)
+        t2 = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_v = world * e2e_n / (t2.item() / 1e3)
+
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = my_params * BYTES_PER_PARAM_BF16 / (kernel_ms / 1e3) / 1e9
@@ -570,12 +580,10 @@ def run_gpu_arm(args):
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_kernel<float,expand,table>",
                     "kernel_ms": kernel_ms, "algorithmic_bytes_per_param": BYTES_PER_PARAM_BF16}
-        if args.kernel_only:  # profiling runs: nothing but the fused kernel
-            e2e_v, h2d, d2h, e2e_n = None, 0, 0, 0
+        if args.kernel_only or world > 1:  # profiling runs: nothing but the fused kernel; the CPU leg runs at N = 1
             cpu_v = cpu_steps = cpu_dt = cores = None
         else:
-            e2e_v, h2d, d2h, e2e_n = e2e_public_api(torch, device, max(3, min(args.steps, 10)), args.warmup)
-            cpu_v, cpu_steps, cpu_dt, cores = cpu_reference_steps(4096 * 4096, 10.0) if world == 1 else (None,) * 4
+            cpu_v, cpu_steps, cpu_dt, cores = cpu_reference_steps(4096 * 4096, 10.0)
         line = {
             "metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -595,12 +603,12 @@ def run_gpu_arm(args):
                        "hyper": {"lr": 1e-4, "betas": [0.9, 0.95], "wd": 0.1, "eps": 1e-8, "expand_min": 16}},
             "roofline": roofline,
             "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "workload": f"CoatAdamW.step on one decoder layer ({e2e_n} params), grads from pinned host "
-                                "memory, updated fp32 weights read back"},
+                    "workload": f"CoatAdamW.step on one decoder layer ({e2e_n} params) per GPU, grads from pinned "
+                                "host memory, updated fp32 weights read back; bytes are per GPU"},
             "gpu_launches": n_launches,
             "clocks": clocks,
         }
-        if not args.kernel_only and args.workload == "llama2-7b":
+        if not args.kernel_only and args.workload == "llama2-7b" and world == 1:
             del opt, grads
             torch.cuda.empty_cache()
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
