@@ -397,6 +397,46 @@ def gemm_extras(torch, device, iters=10):
     return out
 
 
+def blockscaled_extras(torch, device, peak, iters=10):
+    """The DeepSeek-style block-scaled path on the Llama-2-7B MLP forward shape: the 128-granular quantizers
+    (GB/s of algorithmic bytes) and the block-scaled GEMM (TFLOP/s), CUDA-event time of the public python calls."""
+    from coat_b200.activation.deepseek import gemm_fp8_fp8_bf16_nt
+    from coat_b200.activation.real_quantization import fp8_quantize_perblock, fp8_quantize_transpose
+    T, H, I = 8192, 4096, 11008
+    gen = torch.Generator(device=device).manual_seed(4)
+    x = torch.randn(T, H, generator=gen, device=device).to(torch.bfloat16)
+    w = (torch.randn(I, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / n
+
+    out = {}
+    ms = timed(lambda: fp8_quantize_transpose(x, 128, "E4M3", scale_dtype=torch.float32), iters)
+    by = T * H * (2 + 1 + 1 + 8.0 / 128)
+    out["quantize_transpose_1x128"] = {"us": ms * 1e3, "GB/s": by / ms / 1e6, "frac_of_measured_hbm": by / ms / 1e6 / peak}
+    ms = timed(lambda: fp8_quantize_perblock(w, 128, "E4M3", scale_dtype=torch.float32), iters)
+    by = I * H * 3.0
+    out["quantize_perblock_128x128"] = {"us": ms * 1e3, "GB/s": by / ms / 1e6, "frac_of_measured_hbm": by / ms / 1e6 / peak}
+    (qx, sx), _ = fp8_quantize_transpose(x, 128, "E4M3", scale_dtype=torch.float32)
+    sx = sx.t().contiguous().t()
+    qw, sw = fp8_quantize_perblock(w, 128, "E4M3", scale_dtype=torch.float32)
+    c = torch.empty(T, I, dtype=torch.bfloat16, device=device)
+    ms = timed(lambda: gemm_fp8_fp8_bf16_nt((qx, sx), (qw, sw), c), iters)
+    tf = 2.0 * T * I * H / (ms / 1e3) / 1e12
+    out["gemm_blockscaled_forward"] = {"M": T, "N": I, "K": H, "us": ms * 1e3, "TFLOP/s": tf,
+                                       "frac_of_nominal_fp8": tf / 4500.0}
+    return out
+
+
 def layer_extras(torch, device, iters=5):
     """Forward + backward of ONE Llama-2-7B decoder layer (hidden 4096, 32 heads, MLP 11008) on 4 x 2048 tokens
     through the FP8 layer of this package, and, beside it, the same layer in plain bf16 torch (cuBLAS GEMMs,
@@ -473,6 +513,8 @@ def run_kernel_workload(args):
     peak, kind = measured_peaks()
     if args.workload == "quantizers":
         extras = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
+    elif args.workload == "blockscaled":
+        extras = {"deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
     elif args.workload == "layer":
         extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10)))}
     else:
@@ -613,7 +655,8 @@ def run_gpu_arm(args):
             torch.cuda.empty_cache()
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
-                              "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device)}
+                              "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device),
+                              "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
         if cpu_v is not None:
             line["cpu_baseline"] = {
                 "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
@@ -630,7 +673,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm", "layer"],
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm", "layer", "blockscaled"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
@@ -639,7 +682,7 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
-    elif args.workload in ("quantizers", "gemm", "layer"):
+    elif args.workload in ("quantizers", "gemm", "layer", "blockscaled"):
         run_kernel_workload(args)
     else:
         run_gpu_arm(args)

@@ -4,6 +4,9 @@ from ._dequantize import fp8_dequantize  # noqa: F401
 from ._division import fp8_division  # noqa: F401
 from ._division_transpose import fp8_division_transpose  # noqa: F401
 from ._quantize import fp8_quantize  # noqa: F401
+from ._quantize_perblock import fp8_quantize_perblock  # noqa: F401
+from ._quantize_perblock_transpose import fp8_quantize_perblock_transpose  # noqa: F401
+from ._quantize_perblock_transpose_pergroup import fp8_quantize_perblock_transpose_pergroup  # noqa: F401
 from ._quantize_pertensor import fp8_quantize_pertensor  # noqa: F401
 from ._quantize_pertensor_transpose import fp8_quantize_pertensor_transpose  # noqa: F401
 from ._transpose import fp8_transpose  # noqa: F401
@@ -17,3 +20,4 @@ from .mul_fwd import fp8_mul_forward  # noqa: F401
 from .silu_bwd import fp8_silu_backward  # noqa: F401
 from .silu_fwd import fp8_silu_forward  # noqa: F401
 from .linear import fp8_linear_backward, fp8_linear_forward  # noqa: F401
+from ._quantize_transpose import fp8_quantize_transpose  # noqa: F401

@@ -165,10 +165,64 @@ def fp8_division_transpose(x, QB, fp8type, s_y=None, stochastic=False, only_tran
     return y, s_y, y_t   # y_t stays 2-D
 
 
+def _block128(x, fp8type, scale_dtype, flags, block=False, block_t=False, rows=False, cols_t=False):
+    """One call of coat_fp8_quantize_block128; returns the four (codes, scales) pairs, None where not asked for."""
+    M, N = x.shape
+    dev = x.device
+
+    def pair(want, shape, sshape):
+        if not want:
+            return None, None
+        return torch.empty(shape, dtype=fp8type, device=dev), torch.empty(sshape, dtype=scale_dtype, device=dev)
+
+    y_b, s_b = pair(block, (M, N), (M // 128, N // 128))
+    y_bt, s_bt = pair(block_t, (N, M), (N // 128, M // 128))
+    y_r, s_r = pair(rows, (M, N), (M, N // 128))
+    y_ct, s_ct = pair(cols_t, (N, M), (N, M // 128))
+    ptr = lambda t: None if t is None else t.data_ptr()
+    with torch.cuda.device(dev):
+        _call("coat_fp8_quantize_block128", x.data_ptr(), M, N, x.stride(0), ptr(y_b), ptr(s_b), ptr(y_bt), ptr(s_bt),
+              ptr(y_r), ptr(s_r), ptr(y_ct), ptr(s_ct), _lib.fp8_format(fp8type)[0], _lib.float_dtype(x),
+              _lib.float_dtype(scale_dtype), _flags(flags), _lib.stream_ptr(dev))
+    return (y_b, s_b), (y_bt, s_bt), (y_r, s_r), (y_ct, s_ct)
+
+
+def fp8_quantize_perblock(x, QB, fp8type, scale_dtype=torch.bfloat16, *, flags=None):
+    """One scale per QB x QB block, QB = 128 (_quantize_perblock.py:115-150).  -> (y, s_y[M/QB, N/QB]), 2-D."""
+    if QB != 128:
+        raise RuntimeError("coat_b200: per-block quantization is provided for QB = 128")
+    x, _ = _prep(x)
+    return _block128(x, _fp8_dtype(fp8type), scale_dtype, flags, block=True)[0]
+
+
+def fp8_quantize_perblock_transpose(x, QB, fp8type, scale_dtype=torch.bfloat16, only_transposed=False, *, flags=None):
+    """-> (y, s_y), (y_t, s_y_t), or only the transposed pair (_quantize_perblock_transpose.py:127-190)."""
+    if QB != 128:
+        raise RuntimeError("coat_b200: per-block quantization is provided for QB = 128")
+    x, _ = _prep(x)
+    out = _block128(x, _fp8_dtype(fp8type), scale_dtype, flags, block=not only_transposed, block_t=True)
+    return out[1] if only_transposed else (out[0], out[1])
+
+
+def fp8_quantize_perblock_transpose_pergroup(x, QB, fp8type, scale_dtype=torch.bfloat16, only_transposed=False, *,
+                                             flags=None):
+    """-> (y, s_y), (y_t, s_y_t), (y_pg, s_y_pg): block-scaled codes, their transpose, and 1 x QB row-group codes
+    (_quantize_perblock_transpose_pergroup.py:183-246).  With only_transposed the first pair is not computed
+    (the reference returns uninitialised buffers there); None is returned in its place."""
+    if QB != 128:
+        raise RuntimeError("coat_b200: per-block quantization is provided for QB = 128")
+    x, _ = _prep(x)
+    out = _block128(x, _fp8_dtype(fp8type), scale_dtype, flags, block=not only_transposed, block_t=True, rows=True)
+    return out[0], out[1], out[2]
+
+
 def fp8_quantize_transpose(x, QB, fp8type, scale_dtype=torch.bfloat16, *, flags=None):
     x, _ = _prep(x)
     M, N = x.shape
     fp8type = _fp8_dtype(fp8type)
+    if QB == 128:
+        out = _block128(x, fp8type, scale_dtype, flags, rows=True, cols_t=True)
+        return out[2], out[3]
     y = torch.empty((M, N), dtype=fp8type, device=x.device)
     y_t = torch.empty((N, M), dtype=fp8type, device=x.device)
     s_y = torch.empty((M, N // QB), dtype=scale_dtype, device=x.device)

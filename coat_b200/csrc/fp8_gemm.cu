@@ -632,6 +632,176 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
     }
 }
 
+// =====================================================================================================
+// Block-scaled GEMM (the DeepSeek-style recipe that the reference reaches through deep_gemm.gemm_fp8_fp8_bf16_nt,
+// coat/activation/deepseek/linear.py:10-36):
+//     C[m, n] = sum over K blocks kb of  sa[m, kb] * sb[n / 128, kb] * sum_{k in kb} A[m, k] * B[n, k]
+// with one scale per 1 x 128 segment of A and per 128 x 128 block of B.  The tensor core cannot apply a
+// scale per K block inside its accumulation, so every K block is multiplied into a FRESH 128 x 128 fp32
+// buffer in tensor memory (four of them rotate) and eight "promotion" warps add it, times its two scales,
+// into fp32 accumulators they hold in registers (one row per thread, 64 columns per warp of a lane quarter)
+// while the tensor core works on the next K blocks.  After the last K block the same warps convert to bf16
+// and store through shared memory and the TMA unit.
+//   warp 0      TMA producer: A and B stages of 128 rows x 128 bytes (5 stages)
+//   warp 1      MMA issuer: 4 x (M128 N128 K32) per K block, commit -> stage empty, commit -> partial full
+//   warps 2..9  promotion + epilogue; they arrive on `partial empty` when a buffer has been read
+// Every wait is bounded as in the other kernels.
+// =====================================================================================================
+constexpr int kBsBN = 128, kBsStages = 5, kBsParts = 4, kBsEpiWarps = 8, kBsThreads = 64 + 32 * kBsEpiWarps;
+constexpr uint32_t kBsStageA = 128 * kBK, kBsStageB = kBsBN * kBK, kBsStageBytes = kBsStageA + kBsStageB;
+constexpr uint32_t kBsStaging = 4096 * kBsEpiWarps;   // per warp: 32 rows x 64 bf16 columns
+constexpr size_t kBsSmem = (size_t)kBsStages * kBsStageBytes + kBsStaging + 1024 + 256;
+
+struct BlockScaledArgs {
+    const float* sa;      // [K/128][lds_a]: scale of row m for K block kb at sa[kb * lds_a + m]
+    const float* sb;      // [N/128][K/128] row-major
+    int64_t lds_a;
+    void* c;              // bf16 [M, N]
+    int tma_store;
+    int M, N, K;
+};
+
+__global__ void __launch_bounds__(kBsThreads, 1)
+fp8_gemm_blockscaled_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                            const __grid_constant__ CUtensorMap map_c, uint32_t idesc, BlockScaledArgs e, int tiles_m,
+                            int tiles_n) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + (size_t)kBsStages * kBsStageA;
+    uint8_t* staging = smem + (size_t)kBsStages * kBsStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + kBsStaging);
+    uint64_t* full_bar = bars;                               // [kBsStages] TMA -> MMA
+    uint64_t* empty_bar = bars + kBsStages;                  // [kBsStages] MMA -> TMA
+    uint64_t* part_full = bars + 2 * kBsStages;              // [kBsParts] K block's product complete -> promotion
+    uint64_t* part_empty = bars + 2 * kBsStages + kBsParts;  // [kBsParts] promotion has read it -> MMA
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kBsStages + 2 * kBsParts);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int k_blocks = e.K / kBK;
+    const int n_tiles = tiles_m * tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBsStages; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int i = 0; i < kBsParts; ++i) { mbar_init(&part_full[i], 1); mbar_init(&part_empty[i], kBsEpiWarps); }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s2u(tmem_slot)), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kBsStages;
+                    if (it >= kBsStages) ok = mbar_wait(&empty_bar[s], ((it / kBsStages) - 1) & 1, abort_flag);
+                    if (!ok) break;
+                    mbar_expect_tx(&full_bar[s], kBsStageBytes);
+                    tma_load_2d(smem_a + (size_t)s * kBsStageA, &map_a, kb * kBK, tile_m * 128, &full_bar[s]);
+                    tma_load_2d(smem_b + (size_t)s * kBsStageB, &map_b, kb * kBK, tile_n * kBsBN, &full_bar[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int it = 0;   // K blocks issued so far: stage it % kBsStages, partial buffer it % kBsParts
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % kBsStages, pb = it % kBsParts;
+                    if (it >= kBsParts) ok = mbar_wait(&part_empty[pb], ((it / kBsParts) - 1) & 1, abort_flag);
+                    if (ok) ok = mbar_wait(&full_bar[s], (it / kBsStages) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t tmem_d = tmem_base + (uint32_t)(pb * kBsBN);
+                    const uint64_t da = make_smem_desc(s2u(smem_a + (size_t)s * kBsStageA));
+                    const uint64_t db = make_smem_desc(s2u(smem_b + (size_t)s * kBsStageB));
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k)
+                        umma_f8(tmem_d, da + (uint64_t)(k * (kUmmaK >> 4)), db + (uint64_t)(k * (kUmmaK >> 4)), idesc, k != 0);
+                    umma_commit(&empty_bar[s]);
+                    umma_commit(&part_full[pb]);
+                }
+            }
+        }
+    } else {
+        // ---------------- promotion + epilogue (warps 2..9) ----------------
+        const int quarter = warp & 3;            // TMEM lanes this warp may read
+        const int chalf = (warp - 2) >> 2;       // which 64 of the tile's 128 columns
+        uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
+        int it = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            const int row0 = tile_m * 128 + quarter * 32, row = row0 + lane;
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int kb = 0; kb < k_blocks && ok; ++kb, ++it) {
+                const int pb = it % kBsParts;
+                // the two scales of this K block (rows beyond M contribute nothing and are never stored)
+                const float s_row = row < e.M ? e.sa[(int64_t)kb * e.lds_a + row] : 0.f;
+                const float scale = s_row * e.sb[(int64_t)tile_n * k_blocks + kb];
+                ok = __all_sync(COAT_FULL_MASK, mbar_wait(&part_full[pb], (it / kBsParts) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(pb * kBsBN + chalf * 64);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t r[32];
+                    tmem_ld32(taddr + (uint32_t)(hh * 32), r);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[hh * 32 + i] = __fmaf_rn(__uint_as_float(r[i]), scale, acc[hh * 32 + i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s2u(&part_empty[pb])) : "memory");
+            }
+            if (!ok) break;
+            const int col0 = tile_n * kBsBN + chalf * 64;
+            if (e.tma_store) {
+                if (lane == 0) bulk_wait_read();
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t o[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        o[q] = (uint32_t)coat_float_to_bf16_bits(acc[8 * j + 2 * q]) |
+                               ((uint32_t)coat_float_to_bf16_bits(acc[8 * j + 2 * q + 1]) << 16);
+                    *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 < e.M) {
+                    tma_store_2d(&map_c, stg, col0, row0);
+                    bulk_commit();
+                }
+            } else if (row < e.M) {
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.c) + (int64_t)row * e.N + col0;
+                for (int i = 0; i < 64; ++i) dst[i] = __float2bfloat16_rn(acc[i]);
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+    if (!ok) { *abort_flag = 1; g_gemm_device_status = COAT_E_TIMEOUT; }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    }
+}
+
 // ---- host side ------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -815,4 +985,33 @@ extern "C" int coat_fp8_gemm_device_status(void) {
     if (cudaMemcpyFromSymbol(&v, g_gemm_device_status, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
     if (v != 0 && cudaMemcpyToSymbol(g_gemm_device_status, &zero, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
     return v;
+}
+
+extern "C" int coat_fp8_gemm_blockscaled(const uint8_t* a, const float* scale_a, int64_t lds_a, const uint8_t* b,
+                                         const float* scale_b, void* c, int64_t M, int64_t N, int64_t K, int fmt_a,
+                                         int fmt_b, void* stream) {
+    if (M < 0 || N < 0 || K < 0) return COAT_E_BADARG;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!a || !b || !c || !scale_a || !scale_b || lds_a < M) return COAT_E_BADARG;
+    if ((fmt_a != COAT_E4M3 && fmt_a != COAT_E5M2) || (fmt_b != COAT_E4M3 && fmt_b != COAT_E5M2)) return COAT_E_BADARG;
+    if (K == 0 || K % 128 != 0 || N % 128 != 0) return COAT_E_SHAPE;   // whole scale blocks only
+    if (!coat_aligned(a, 16) || !coat_aligned(b, 16) || !coat_aligned(c, 16)) return COAT_E_ALIGN;
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return COAT_E_TOOBIG;
+    CUtensorMap map_a, map_b, map_c;
+    if (int rc = make_map(&map_a, a, M, K, 128)) return rc;
+    if (int rc = make_map(&map_b, b, N, K, kBsBN)) return rc;
+    if (int rc = make_map_c(&map_c, c, M, N)) return rc;
+    BlockScaledArgs e = {scale_a, scale_b, lds_a, c, 1, (int)M, (int)N, (int)K};
+    const uint32_t idesc = make_idesc(fmt_a, fmt_b, 128, kBsBN);
+    const int tiles_m = (int)((M + 127) / 128), tiles_n = (int)(N / kBsBN);
+    const int64_t tiles = (int64_t)tiles_m * tiles_n;
+    if (tiles > 0x7fffffff) return COAT_E_TOOBIG;
+    const int sms = coat_sm_count();
+    const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+    if (cudaFuncSetAttribute(fp8_gemm_blockscaled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBsSmem) !=
+        cudaSuccess)
+        return COAT_E_LAUNCH;
+    fp8_gemm_blockscaled_kernel<<<grid, kBsThreads, kBsSmem, (cudaStream_t)stream>>>(map_a, map_b, map_c, idesc, e,
+                                                                                   tiles_m, tiles_n);
+    return coat_launch_status();
 }

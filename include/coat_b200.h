@@ -208,6 +208,21 @@ int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, 
                                        int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
                                        int flags, void* stream);
 
+/* Quantizers with 128-wide granularity (the DeepSeek-style block-scaled linear layer): from one read of x
+ * (M, N multiples of 128) any subset of
+ *   y_b  [M,N] + s_b  [M/128, N/128]  one scale per 128x128 block      (fp8_quantize_perblock,
+ *                                      coat/activation/real_quantization/_quantize_perblock.py:115-150)
+ *   y_bt [N,M] + s_bt [N/128, M/128]  the same codes transposed        (fp8_quantize_perblock_transpose,
+ *                                      _quantize_perblock_transpose.py:127-190)
+ *   y_r  [M,N] + s_r  [M, N/128]      one scale per 1x128 row group    (fp8_quantize_transpose with QB = 128,
+ *                                      _quantize_transpose.py:39-173, and the per-group output of
+ *                                      fp8_quantize_perblock_transpose_pergroup, ..._pergroup.py:145-246)
+ *   y_ct [N,M] + s_ct [N, M/128]      one scale per 128x1 column group, transposed (_quantize_transpose.py)
+ * Outputs not wanted are NULL (codes and scales together).  Scales are row-major in scale_dtype. */
+int coat_fp8_quantize_block128(const void* x, int64_t M, int64_t N, int64_t ldx, uint8_t* y_b, void* s_b,
+                               uint8_t* y_bt, void* s_bt, uint8_t* y_r, void* s_r, uint8_t* y_ct, void* s_ct,
+                               int fmt, int in_dtype, int scale_dtype, int flags, void* stream);
+
 /* =========================== fused quantize-on-save operators =================================
  * Inputs x, x1, x2 are M x N code matrices quantised in 1xQB groups with scales s_* of shape [M, N/QB];
  * g is a floating (bf16 by default) M x N matrix.  Where an amax_bits pointer is given, the call zeroes
@@ -285,6 +300,17 @@ int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* scale_c, co
                   int fmt_b, int scale_dtype, int bias_dtype, int output_quantize, int QB, int flags,
                   void* stream);
 int coat_fp8_gemm_device_status(void);
+
+/* Block-scaled GEMM of the DeepSeek-style linear layer:
+ *   C[m, n] = sum over K blocks kb of scale_a[m, kb] * scale_b[n / 128, kb] * sum_{k in kb} A[m, k] * B[n, k]
+ * A [M,K] and B [N,K] FP8 codes with K contiguous; scale_a fp32 with one scale per 1x128 segment of A, stored
+ * with the rows contiguous (element (m, kb) at scale_a[kb * lds_a + m], the layout deep_gemm asks for);
+ * scale_b fp32 [N/128, K/128] row-major, one scale per 128x128 block of B; C bf16 [M,N].  K and N multiples
+ * of 128.  Replaces deep_gemm.gemm_fp8_fp8_bf16_nt as called by fp8_deepseek_linear_forward / _backward
+ * (coat/activation/deepseek/linear.py:10-36).  Status word shared with coat_fp8_gemm. */
+int coat_fp8_gemm_blockscaled(const uint8_t* a, const float* scale_a, int64_t lds_a, const uint8_t* b,
+                              const float* scale_b, void* c, int64_t M, int64_t N, int64_t K, int fmt_a,
+                              int fmt_b, void* stream);
 
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).

@@ -22,3 +22,14 @@ def within_tolerance(c, ref):
     err = (c.double() - ref).abs()
     tol = 2.0 ** -7 * ref.abs() + 2.0 ** -7 * ref.pow(2).mean().sqrt()
     return err <= tol
+
+
+def blockscaled_matmul_fp64(a, sa, b, sb):
+    """a [M,K], b [N,K] fp8; sa [M, K/128], sb [N/128, K/128] fp32 -> fp64 [M,N]: every 1x128 segment of a and
+    128x128 block of b dequantised exactly, products summed exactly (what deep_gemm.gemm_fp8_fp8_bf16_nt computes
+    up to its fp32 accumulation order, coat/activation/deepseek/linear.py:10-16)."""
+    M, K = a.shape
+    N = b.shape[0]
+    ad = a.to(torch.float32).double().reshape(M, K // 128, 128) * sa.double()[:, :, None]
+    bd = b.to(torch.float32).double().reshape(N // 128, 128, K // 128, 128) * sb.double()[:, None, :, None]
+    return ad.reshape(M, K) @ bd.reshape(N, K).t()

@@ -78,3 +78,24 @@ def near_rounding_boundary(x_over_s, fp8type, ulps=4):
     lo = cast_fp8(q * (1 - ulps * 2.0 ** -23), fp8type).view(torch.uint8)
     hi = cast_fp8(q * (1 + ulps * 2.0 ** -23), fp8type).view(torch.uint8)
     return lo != hi
+
+
+def fp8_quantize_block128(x, fp8type, scale_dtype=torch.float32):
+    """128-wide granularities of the block-scaled linear layer, IEEE division
+    (coat/activation/real_quantization/_quantize_perblock.py:70-84, _quantize_perblock_transpose_pergroup.py:145-160,
+    _quantize_transpose.py with QB = 128).  Returns a dict of (codes, scales):
+      "block"  [M,N], [M/128, N/128];   "block_t" [N,M], [N/128, M/128]
+      "rows"   [M,N], [M, N/128];       "cols_t"  [N,M], [N, M/128]"""
+    M, N = x.shape
+    xf = x.float()
+    fmax = FP8_MAX[fp8type]
+    xb = xf.reshape(M // 128, 128, N // 128, 128)
+    s_b = (xb.abs().amax(dim=(1, 3)) + 1e-10) / fmax
+    q_b = cast_fp8((xb / s_b[:, None, :, None]).reshape(M, N), fp8type)
+    s_r = (xf.reshape(M, N // 128, 128).abs().amax(dim=2) + 1e-10) / fmax
+    q_r = cast_fp8((xf.reshape(M, N // 128, 128) / s_r[:, :, None]).reshape(M, N), fp8type)
+    xt = xf.t().contiguous()
+    s_c = (xt.reshape(N, M // 128, 128).abs().amax(dim=2) + 1e-10) / fmax
+    q_c = cast_fp8((xt.reshape(N, M // 128, 128) / s_c[:, :, None]).reshape(N, M), fp8type)
+    return {"block": (q_b, s_b.to(scale_dtype)), "block_t": (q_b.t().contiguous(), s_b.t().contiguous().to(scale_dtype)),
+            "rows": (q_r, s_r.to(scale_dtype)), "cols_t": (q_c, s_c.to(scale_dtype))}

@@ -192,3 +192,57 @@ def test_quantizer_error_conventions():
         r.fp8_quantize(x.cpu(), 16, "E4M3")
     y, s = r.fp8_quantize(x[:0], 16, torch.float8_e5m2)   # empty input, dtype given as torch dtype
     assert y.shape == (0, 48) and y.dtype == torch.float8_e5m2
+
+
+# ---- 128-wide granularities (block-scaled linear layer) --------------------------------------------
+@pytest.mark.parametrize("fp8type", [torch.float8_e4m3fn, torch.float8_e5m2])
+@pytest.mark.parametrize("shape", [(128, 128), (256, 384), (1024, 512)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_block128_quantizers_bit_exact_ieee(fp8type, shape, dtype):
+    from coat_b200 import _lib
+    from coat_b200.activation.real_quantization import (fp8_quantize_perblock, fp8_quantize_perblock_transpose,
+                                                        fp8_quantize_perblock_transpose_pergroup,
+                                                        fp8_quantize_transpose)
+    from oracle import quant as OQ
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(shape, generator=gen)
+    x = torch.where(torch.rand(shape, generator=gen) < 1e-3, x * 100, x).to(dtype)
+    want = OQ.fp8_quantize_block128(x, fp8type, torch.float32)
+    xd = x.cuda()
+    F = _lib.QUANT_IEEE_DIV
+
+    def same(got, key):
+        q, s = got
+        wq, ws = want[key]
+        assert torch.equal(q.cpu().view(torch.uint8), wq.view(torch.uint8)), key
+        assert torch.equal(s.cpu(), ws), key
+
+    same(fp8_quantize_perblock(xd, 128, fp8type, scale_dtype=torch.float32, flags=F), "block")
+    b, bt = fp8_quantize_perblock_transpose(xd, 128, fp8type, scale_dtype=torch.float32, flags=F)
+    same(b, "block"); same(bt, "block_t")
+    same(fp8_quantize_perblock_transpose(xd, 128, fp8type, scale_dtype=torch.float32, only_transposed=True, flags=F), "block_t")
+    b, bt, pg = fp8_quantize_perblock_transpose_pergroup(xd, 128, fp8type, scale_dtype=torch.float32, flags=F)
+    same(b, "block"); same(bt, "block_t"); same(pg, "rows")
+    r, ct = fp8_quantize_transpose(xd, 128, fp8type, scale_dtype=torch.float32, flags=F)
+    same(r, "rows"); same(ct, "cols_t")
+
+
+def test_block128_default_division_differs_only_at_rounding_boundaries():
+    from coat_b200.activation.real_quantization import fp8_quantize_perblock
+    from oracle import quant as OQ
+    gen = torch.Generator().manual_seed(12)
+    x = torch.randn(512, 512, generator=gen).to(torch.bfloat16)
+    q, s = fp8_quantize_perblock(x.cuda(), 128, "E4M3", scale_dtype=torch.float32)
+    wq, ws = OQ.fp8_quantize_block128(x, torch.float8_e4m3fn)["block"]
+    assert torch.allclose(s.cpu(), ws, rtol=2e-7)
+    diff = q.cpu().view(torch.uint8) != wq.view(torch.uint8)
+    assert diff.float().mean() < 2e-3
+    assert (q.cpu().float() - wq.float()).abs().max() <= 32   # one code step at most
+
+
+def test_block128_rejects_ragged_shapes():
+    from coat_b200.activation.real_quantization import fp8_quantize_perblock
+    with pytest.raises(RuntimeError):
+        fp8_quantize_perblock(torch.zeros(128, 192, dtype=torch.bfloat16, device="cuda"), 128, "E4M3")
+    with pytest.raises(RuntimeError):
+        fp8_quantize_perblock(torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda"), 64, "E4M3")
