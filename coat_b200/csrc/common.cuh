@@ -2,6 +2,8 @@
 #pragma once
 
 #include <cuda.h>
+#include <cstdio>
+#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -16,8 +18,13 @@
 // Number of SMs of the current device, cached per process (B200: 148).
 int coat_sm_count();
 
+// COAT_B200_DEBUG=1 in the environment prints CUDA's own message for a failed launch to stderr.
 static inline int coat_launch_status() {
-    return cudaGetLastError() == cudaSuccess ? COAT_OK : COAT_E_LAUNCH;
+    const cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) return COAT_OK;
+    const char* dbg = getenv("COAT_B200_DEBUG");
+    if (dbg && dbg[0] == '1') fprintf(stderr, "coat_b200: launch failed: %s\n", cudaGetErrorString(err));
+    return COAT_E_LAUNCH;
 }
 
 static inline bool coat_aligned(const void* p, size_t a) {

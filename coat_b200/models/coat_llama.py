@@ -382,6 +382,42 @@ def _rotate_half(x):
     return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
 
 
+class _FusedRotary(torch.autograd.Function):
+    """y = x * cos + rotate_half(x) * sin on bf16 [B, S, H, D] in one kernel (coat_rope_bf16); the backward pass is
+    the same kernel with the transposed rotation."""
+
+    @staticmethod
+    def _run(x4, cos, sin, backward):
+        from .. import _lib
+        B, S, H, D = x4.shape
+        y = torch.empty((B, S, H, D), dtype=x4.dtype, device=x4.device)
+        with torch.cuda.device(x4.device):
+            rc = _lib.lib().coat_rope_bf16(x4.data_ptr(), x4.stride(0), x4.stride(1), x4.stride(2), cos.data_ptr(),
+                                           sin.data_ptr(), y.data_ptr(), B, S, H, D,
+                                           0 if cos.shape[0] == 1 else cos.stride(0), int(backward),
+                                           _lib.stream_ptr(x4.device))
+        _lib.check(rc, "rope_bf16")
+        return y
+
+    @staticmethod
+    def forward(ctx, x4, cos, sin):
+        ctx.save_for_backward(cos, sin)
+        return _FusedRotary._run(x4, cos, sin, False)
+
+    @staticmethod
+    def backward(ctx, dy):
+        cos, sin = ctx.saved_tensors
+        if dy.stride(3) != 1 or any(st % 8 for st in dy.stride()[:3]):
+            dy = dy.contiguous()
+        return _FusedRotary._run(dy, cos, sin, True), None, None
+
+
+def _fused_rotary_ok(x, cos, sin):
+    return (x.is_cuda and x.dtype == torch.bfloat16 and cos.dtype == torch.bfloat16 and sin.dtype == torch.bfloat16
+            and cos.dim() == 3 and cos.is_contiguous() and sin.is_contiguous() and cos.shape == sin.shape
+            and cos.shape[0] in (1, x.shape[0]) and x.shape[-1] % 16 == 0)
+
+
 def llama_rotary_embeddings(position_ids, head_dim, rope_theta, dtype):
     """cos / sin of shape [batch, seq, head_dim] for integer positions [batch, seq] (default Llama RoPE)."""
     inv_freq = 1.0 / (rope_theta ** (torch.arange(0, head_dim, 2, device=position_ids.device, dtype=torch.float32)
@@ -414,16 +450,22 @@ class LlamaSdpaAttentionWithoutLinear(nn.Module):
         if output_attentions or use_cache or past_key_value is not None:
             raise NotImplementedError("the training layer returns no attention weights and keeps no KV cache")
         bsz, q_len, _ = query_states.size()
-        q = query_states.view(bsz, q_len, self.num_heads, self.head_dim).transpose(1, 2)
-        k = key_states.view(bsz, q_len, self.num_key_value_heads, self.head_dim).transpose(1, 2)
+        q = query_states.view(bsz, q_len, self.num_heads, self.head_dim)
+        k = key_states.view(bsz, q_len, self.num_key_value_heads, self.head_dim)
         v = value_states.view(bsz, q_len, self.num_key_value_heads, self.head_dim).transpose(1, 2)
         if position_embeddings is None:
             if position_ids is None:
-                position_ids = torch.arange(q_len, device=q.device)[None, :].expand(bsz, -1)
+                position_ids = torch.arange(q_len, device=q.device)[None, :]
             position_embeddings = llama_rotary_embeddings(position_ids, self.head_dim, self.rope_theta, q.dtype)
-        cos, sin = (t.unsqueeze(1) for t in position_embeddings)
-        q = q * cos + _rotate_half(q) * sin
-        k = k * cos + _rotate_half(k) * sin
+        cos, sin = position_embeddings
+        if _fused_rotary_ok(q, cos, sin):
+            q = _FusedRotary.apply(q, cos, sin).transpose(1, 2)
+            k = _FusedRotary.apply(k, cos, sin).transpose(1, 2)
+        else:   # other dtypes / devices: the eager form
+            q, k = q.transpose(1, 2), k.transpose(1, 2)
+            cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+            q = q * cos + _rotate_half(q) * sin
+            k = k * cos + _rotate_half(k) * sin
         if self.num_key_value_groups > 1:
             k = k.repeat_interleave(self.num_key_value_groups, dim=1)
             v = v.repeat_interleave(self.num_key_value_groups, dim=1)

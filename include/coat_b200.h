@@ -312,6 +312,16 @@ int coat_fp8_gemm_blockscaled(const uint8_t* a, const float* scale_a, int64_t ld
                               const float* scale_b, void* c, int64_t M, int64_t N, int64_t K, int fmt_a,
                               int fmt_b, void* stream);
 
+/* Rotary position embedding of bf16 q or k: x element (b, s, h, d) at x[b*sxb + s*sxs + h*sxh + d] (strides in
+ * elements, multiples of 8), output y contiguous [B, S, H, D], D a multiple of 16:
+ *   y = x * cos + rotate_half(x) * sin      (backward != 0: the transposed rotation, for the gradient)
+ * cos / sin: bf16 [Bc, S, D], Bc = 1 (cos_batch_stride = 0) or B (cos_batch_stride = S * D).  One fused pass in
+ * place of the eager apply_rotary_pos_emb of the attention block (coat/models/coat_llama.py:1031-1036); not
+ * part of the quantization path.  y may equal x when x is contiguous. */
+int coat_rope_bf16(const void* x, int64_t sxb, int64_t sxs, int64_t sxh, const void* cos_t, const void* sin_t,
+                   void* y, int64_t B, int64_t S, int64_t H, int64_t D, int64_t cos_batch_stride, int backward,
+                   void* stream);
+
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
  * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded

@@ -121,3 +121,24 @@ def test_eval_mode_is_the_plain_bf16_layer():
     yr = reference_layer(x.detach().float(), {k: v.detach() for k, v in weights_of(layer, torch.float32).items()},
                          HEADS, HEADS, eps=torch.finfo(torch.bfloat16).eps)
     close(h.float() - x.detach().float(), yr - x.detach().float(), "eval-mode update")
+
+
+def test_fused_rotary_matches_the_eager_form():
+    """One rounding to bf16 instead of one per operation: within 2 bf16 ulps of the eager result, and the
+    backward kernel is the exact transpose (checked against autograd of the eager form in fp32)."""
+    from coat_b200.models.coat_llama import _FusedRotary, _rotate_half, llama_rotary_embeddings
+    gen = torch.Generator().manual_seed(21)
+    B, S, Hh, D = 2, 96, 4, 64
+    x = torch.randn(B, S, Hh, D, generator=gen).to(torch.bfloat16).cuda()
+    dy = torch.randn(B, Hh, S, D, generator=gen).to(torch.bfloat16).cuda().transpose(1, 2)   # a transposed view
+    cos, sin = llama_rotary_embeddings(torch.arange(S, device="cuda")[None, :], D, 10000.0, torch.bfloat16)
+    xg = x.clone().requires_grad_(True)
+    y = _FusedRotary.apply(xg, cos, sin)
+    y.backward(dy)
+    xr = x.float().requires_grad_(True)
+    c, s = cos.float().unsqueeze(2), sin.float().unsqueeze(2)
+    yr = xr * c + _rotate_half(xr) * s
+    yr.backward(dy.float())
+    ulp = lambda t: torch.exp2(torch.floor(torch.log2(t.abs().clamp_min(1e-30))) - 7)
+    assert bool(((y.float() - yr.detach()).abs() <= 2 * ulp(yr.detach()) + 1e-6).all())
+    assert bool(((xg.grad.float() - xr.grad).abs() <= 2 * ulp(xr.grad) + 1e-6).all())
