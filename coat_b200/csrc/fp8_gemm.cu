@@ -265,6 +265,64 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, i
     }
 }
 
+// Drains one warp's 32 rows x 256 columns of an accumulator (tensor-memory address `tmem_tile` = lane quarter
+// and first column) into C, rows row0 .. row0 + 31, columns tile_col0 .. tile_col0 + 255.
+//   TMA path (bf16 output): rows are staged 64 columns (128 bytes) at a time in the warp's 32 x 128-byte buffer, in
+//   the 128-byte swizzle the tensor map expects (16-byte unit u of row r sits at unit u ^ (r & 7): the 8 lanes of
+//   a quarter-warp hit 8 different bank groups), and one lane hands the box to the TMA unit.
+//   Register path (quantising epilogue, or N not a multiple of 8): each lane writes its own row.
+template <int FMT_C>
+__device__ __forceinline__ void drain_accumulator(const CUtensorMap* map_c, const GemmEpilogue& e, uint8_t* stg,
+                                                  uint32_t tmem_tile, int tile_col0, int row0, int lane, float sab) {
+    if (e.tma_store) {
+#pragma unroll 1
+        for (int cc = 0; cc < kBN / 64; ++cc) {
+            if (lane == 0) bulk_wait_read();   // the previous store has read the buffer
+            __syncwarp();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t r[32];
+                tmem_ld32(tmem_tile + (uint32_t)(cc * 64 + hh * 32), r);
+                const int col0 = tile_col0 + cc * 64 + hh * 32;
+                uint32_t o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float a = __uint_as_float(r[2 * i]) * sab, b = __uint_as_float(r[2 * i + 1]) * sab;
+                    if (e.bias) {
+                        if (col0 + 2 * i < e.N) a += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i);
+                        if (col0 + 2 * i + 1 < e.N) b += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i + 1);
+                    }
+                    o[i] = (uint32_t)coat_float_to_bf16_bits(a) | ((uint32_t)coat_float_to_bf16_bits(b) << 16);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint4*>(stg + lane * 128 + (((hh * 4 + j) ^ (lane & 7)) << 4)) =
+                        make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+            }
+            fence_async_smem();   // this lane's staged words become visible to the TMA unit
+            __syncwarp();
+            if (lane == 0 && row0 < e.M && tile_col0 + cc * 64 < e.N) {
+                tma_store_2d(map_c, stg, tile_col0 + cc * 64, row0);
+                bulk_commit();
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem_tile + (uint32_t)(c * 32), r);
+            float v[32];
+            const int col0 = tile_col0 + c * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                v[i] = __uint_as_float(r[i]) * sab;
+                if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
+            }
+            epilogue_store<FMT_C>(e, row0 + lane, col0, v);
+        }
+    }
+}
+
 template <int FMT_C, int BM>
 __global__ void __launch_bounds__(GemmShape<BM>::kThreads, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -372,61 +430,10 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
             if (!ok) break;
             tc_fence_after();
             const int row0 = (unit_m + half) * 128 + quarter * 32;
-            const int row = row0 + lane;
             const uint32_t tmem_tile = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((buf * kHalves + half) * kBN);
-            if (half >= halves) {
-                // a single unit: the warps of the second accumulator have nothing to drain
-            } else if (e.tma_store) {
-                // bf16 rows are staged 64 columns (128 bytes) at a time in this warp's 32 x 128-byte buffer, in the
-                // 128-byte swizzle the tensor map expects (16-byte unit u of row r sits at unit u ^ (r & 7): the 8
-                // lanes of a quarter-warp hit 8 different bank groups), and one lane hands the box to the TMA unit
-                uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
-#pragma unroll 1
-                for (int cc = 0; cc < kBN / 64; ++cc) {
-                    if (lane == 0) bulk_wait_read();   // the previous store has read the buffer
-                    __syncwarp();
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        uint32_t r[32];
-                        tmem_ld32(tmem_tile + (uint32_t)(cc * 64 + hh * 32), r);
-                        const int col0 = tile_n * kBN + cc * 64 + hh * 32;
-                        uint32_t o[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            float a = __uint_as_float(r[2 * i]) * sab, b = __uint_as_float(r[2 * i + 1]) * sab;
-                            if (e.bias) {
-                                if (col0 + 2 * i < e.N) a += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i);
-                                if (col0 + 2 * i + 1 < e.N) b += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i + 1);
-                            }
-                            o[i] = (uint32_t)coat_float_to_bf16_bits(a) | ((uint32_t)coat_float_to_bf16_bits(b) << 16);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            *reinterpret_cast<uint4*>(stg + lane * 128 + (((hh * 4 + j) ^ (lane & 7)) << 4)) =
-                                make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-                    }
-                    fence_async_smem();   // this lane's staged words become visible to the TMA unit
-                    __syncwarp();
-                    if (lane == 0 && row0 < e.M && tile_n * kBN + cc * 64 < e.N) {
-                        tma_store_2d(&map_c, stg, tile_n * kBN + cc * 64, row0);
-                        bulk_commit();
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem_tile + (uint32_t)(c * 32), r);
-                    float v[32];
-                    const int col0 = tile_n * kBN + c * 32;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        v[i] = __uint_as_float(r[i]) * sab;
-                        if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
-                    }
-                    epilogue_store<FMT_C>(e, row, col0, v);
-                }
-            }
+            if (half < halves)   // (a single unit: the warps of the second accumulator have nothing to drain)
+                drain_accumulator<FMT_C>(&map_c, e, staging + (size_t)(warp - 2) * 4096, tmem_tile, tile_n * kBN, row0,
+                                         lane, sab);
             // all of this warp's reads of the accumulator are complete (tcgen05.wait::ld inside tmem_ld32)
             tc_fence_before();
             __syncwarp();
@@ -588,55 +595,8 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
             if (!ok) break;
             tc_fence_after();
             const int row0 = tile_m * 256 + (int)rank * 128 + quarter * 32;
-            const int row = row0 + lane;
             const uint32_t tmem_tile = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kBN);
-            if (e.tma_store) {
-#pragma unroll 1
-                for (int cc = 0; cc < kBN / 64; ++cc) {
-                    if (lane == 0) bulk_wait_read();
-                    __syncwarp();
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        uint32_t r[32];
-                        tmem_ld32(tmem_tile + (uint32_t)(cc * 64 + hh * 32), r);
-                        const int col0 = tile_n * kBN + cc * 64 + hh * 32;
-                        uint32_t o[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            float a = __uint_as_float(r[2 * i]) * sab, b = __uint_as_float(r[2 * i + 1]) * sab;
-                            if (e.bias) {
-                                if (col0 + 2 * i < e.N) a += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i);
-                                if (col0 + 2 * i + 1 < e.N) b += ld_scalar(e.bias, e.bias_dtype, col0 + 2 * i + 1);
-                            }
-                            o[i] = (uint32_t)coat_float_to_bf16_bits(a) | ((uint32_t)coat_float_to_bf16_bits(b) << 16);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            *reinterpret_cast<uint4*>(stg + lane * 128 + (((hh * 4 + j) ^ (lane & 7)) << 4)) =
-                                make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-                    }
-                    fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0 && row0 < e.M && tile_n * kBN + cc * 64 < e.N) {
-                        tma_store_2d(&map_c, stg, tile_n * kBN + cc * 64, row0);
-                        bulk_commit();
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem_tile + (uint32_t)(c * 32), r);
-                    float v[32];
-                    const int col0 = tile_n * kBN + c * 32;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        v[i] = __uint_as_float(r[i]) * sab;
-                        if (e.bias && col0 + i < e.N) v[i] += ld_scalar(e.bias, e.bias_dtype, col0 + i);
-                    }
-                    epilogue_store<FMT_C>(e, row, col0, v);
-                }
-            }
+            drain_accumulator<FMT_C>(&map_c, e, stg, tmem_tile, tile_n * kBN, row0, lane, sab);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(map_to_cta(s2u(&acc_empty[buf]), 0));   // the leader's barrier

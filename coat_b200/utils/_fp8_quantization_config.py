@@ -1,62 +1,56 @@
-"""QuantizationConfig: the knob set the reference passes around as `qargs`.
+"""QuantizationConfig: the knob set the reference passes around as `qargs`
+(coat/utils/_fp8_quantization_config.py:6-80).  Field names, types, defaults, their order (it is the positional
+order of the constructor) and the tolerance for unknown keyword arguments follow the reference, so that configs,
+HfArgumentParser command lines and `coat_fp8_args` dictionaries written for it keep working.  One quirk is kept:
+the dataclass default of `pad_to_multiple_of` is 8 while the constructor's default is 0.
 
-Field names, defaults and the constructor signature follow
-coat/utils/_fp8_quantization_config.py:6-80 so that configs, HF argument parsing
-and checkpoints written for the reference keep working.
-"""
-from dataclasses import dataclass
+The class is generated from the table below instead of being spelled out three times."""
+import dataclasses
 
-
-@dataclass
-class QuantizationConfig:
-    quantize_model: str = "true"
-    symm: bool = True
-    epsilon: float = 1e-10
-    fabit: str = "E4M3"
-    fwbit: str = "E4M3"
-    fobit: str = "E4M3"
-    babit: str = "E5M2"
-    bwbit: str = "E5M2"
-    bobit: str = "E5M2"
-    group_size: int = 16
-    pad_to_multiple_of: int = 8
-    weight_memory_efficient: bool = True
-
+# name, type, dataclass default, constructor default
+_FIELDS = [
+    # activations and linears
+    ("quantize_model", str, "true", "true"),
+    ("symm", bool, True, True),
+    ("epsilon", float, 1e-10, 1e-10),
+    ("fabit", str, "E4M3", "E4M3"),
+    ("fwbit", str, "E4M3", "E4M3"),
+    ("fobit", str, "E4M3", "E4M3"),
+    ("babit", str, "E5M2", "E5M2"),
+    ("bwbit", str, "E5M2", "E5M2"),
+    ("bobit", str, "E5M2", "E5M2"),
+    ("group_size", int, 16, 16),
+    ("pad_to_multiple_of", int, 8, 0),
+    ("weight_memory_efficient", bool, True, True),
     # optimizer states
-    first_order_expansion: str = "true"
-    second_order_expansion: str = "true"
-    first_order_bit: str = "E4M3"
-    second_order_bit: str = "E4M3"
-    qgroup_size: int = 128
-    expand_min: int = 16
-
+    ("first_order_expansion", str, "true", "true"),
+    ("second_order_expansion", str, "true", "true"),
+    ("first_order_bit", str, "E4M3", "E4M3"),
+    ("second_order_bit", str, "E4M3", "E4M3"),
+    ("qgroup_size", int, 128, 128),
+    ("expand_min", int, 16, 16),
     # legacy
-    row_blocksize: int = -1
-    col_blocksize: int = -1
+    ("row_blocksize", int, -1, -1),
+    ("col_blocksize", int, -1, -1),
+]
 
-    def __init__(self, quantize_model="true", symm=True, epsilon=1e-10, fabit="E4M3", fwbit="E4M3",
-                 fobit="E4M3", babit="E5M2", bwbit="E5M2", bobit="E5M2", group_size=16,
-                 pad_to_multiple_of=0, weight_memory_efficient=True, first_order_expansion="true",
-                 second_order_expansion="true", first_order_bit="E4M3", second_order_bit="E4M3",
-                 qgroup_size=128, expand_min=16, row_blocksize=-1, col_blocksize=-1, **kwargs):
-        super().__init__()
-        self.quantize_model = quantize_model
-        self.symm = symm
-        self.epsilon = epsilon
-        self.fabit = fabit
-        self.fwbit = fwbit
-        self.fobit = fobit
-        self.babit = babit
-        self.bwbit = bwbit
-        self.bobit = bobit
-        self.group_size = group_size
-        self.pad_to_multiple_of = pad_to_multiple_of
-        self.weight_memory_efficient = weight_memory_efficient
-        self.first_order_expansion = first_order_expansion
-        self.second_order_expansion = second_order_expansion
-        self.first_order_bit = first_order_bit
-        self.second_order_bit = second_order_bit
-        self.qgroup_size = qgroup_size
-        self.expand_min = expand_min
-        self.row_blocksize = row_blocksize
-        self.col_blocksize = col_blocksize
+
+def _init(self, *args, **kwargs):
+    if len(args) > len(_FIELDS):
+        raise TypeError(f"QuantizationConfig takes at most {len(_FIELDS)} positional arguments")
+    values = {name: ctor_default for name, _, _, ctor_default in _FIELDS}
+    for (name, _, _, _), value in zip(_FIELDS, args):
+        values[name] = value
+    for name in values:
+        if name in kwargs:
+            values[name] = kwargs[name]   # keys that are not fields are ignored, as in the reference
+    for name, value in values.items():
+        setattr(self, name, value)
+
+
+QuantizationConfig = dataclasses.make_dataclass(
+    "QuantizationConfig",
+    [(name, typ, dataclasses.field(default=default)) for name, typ, default, _ in _FIELDS],
+    namespace={"__init__": _init, "__module__": __name__, "__doc__": __doc__},
+    init=False,
+)
