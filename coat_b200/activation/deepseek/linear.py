@@ -33,23 +33,22 @@ def gemm_fp8_fp8_bf16_nt(lhs, rhs, out):
     return out
 
 
+def _nt(lhs, rhs):
+    """out[M, N] = lhs[M, K] @ rhs[N, K]^T for (codes, scales) pairs in the layouts deepseek_check_stride asks for."""
+    deepseek_check_stride(lhs, rhs)
+    out = torch.empty((lhs[0].shape[0], rhs[0].shape[0]), device=lhs[0].device, dtype=torch.bfloat16)
+    return gemm_fp8_fp8_bf16_nt(lhs, rhs, out)
+
+
 def fp8_deepseek_linear_forward(x, s, w, s_w, QB, bias=None):
-    x_fp8, w_fp8 = (x, s), (w, s_w)
-    out = torch.empty((x.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
-    deepseek_check_stride(x_fp8, w_fp8)
-    gemm_fp8_fp8_bf16_nt(x_fp8, w_fp8, out)
-    return out
+    """x [tokens, in] with 1x128 scales, w [out, in] with 128x128 scales -> [tokens, out].  `QB` and `bias` are
+    accepted and ignored, as in the reference."""
+    return _nt((x, s), (w, s_w))
 
 
 def fp8_deepseek_linear_backward(x_t, s_t, g, s_g, g_t, s_g_t, w_t, s_w_t):
-    # dgrad
-    g_fp8, w_t_fp8 = (g, s_g), (w_t, s_w_t)
-    y = torch.empty((g.shape[0], w_t.shape[0]), device=x_t.device, dtype=torch.bfloat16)
-    deepseek_check_stride(g_fp8, w_t_fp8)
-    gemm_fp8_fp8_bf16_nt(g_fp8, w_t_fp8, y)
-    # wgrad, produced transposed ([in, out]) as in the reference and turned round at the end
-    x_t_fp8, g_t_fp8 = (x_t, s_t), (g_t, s_g_t)
-    w_g_t = torch.empty((x_t.shape[0], g_t.shape[0]), device=x_t.device, dtype=torch.bfloat16)
-    deepseek_check_stride(x_t_fp8, g_t_fp8)
-    gemm_fp8_fp8_bf16_nt(x_t_fp8, g_t_fp8, w_g_t)
-    return y, w_g_t.t().contiguous()
+    """dgrad = g [tokens, out] @ w_t [in, out]^T; wgrad comes out transposed ([in, out] = x_t [in, tokens] @
+    g_t [out, tokens]^T) and is turned round, as in the reference."""
+    d_input = _nt((g, s_g), (w_t, s_w_t))
+    d_weight_t = _nt((x_t, s_t), (g_t, s_g_t))
+    return d_input, d_weight_t.t().contiguous()

@@ -1,39 +1,37 @@
-"""Per-module cache of quantised weights / weight scales, as coat/utils/_fp8_weightcache.py:5-43.
+"""Per-module cache of quantised weights / weight scales (coat/utils/_fp8_weightcache.py:5-43).
 
-`prepare_weight(weight, name, is_first_microbatch)`:
-  * first micro-batch: quantise the bf16 weight per tensor (one fused amax pass + one division /
-    transpose pass on the GPU) and remember the result under `<name>_fp8`, `<name>_fp8_t`,
-    `<name>_fp8_scale`;
-  * later micro-batches: return what was remembered.
-With `qargs.weight_memory_efficient` only the scale is kept (and returned); the autograd blocks then
-re-derive the codes from the bf16 weight with `fp8_division[_transpose]` where they need them.
-"""
+`prepare_weight(weight, name, is_first_microbatch)` quantises a bf16 weight per tensor on the first
+micro-batch after an optimizer step (one fused amax pass + one division / transpose pass on the GPU) and
+hands back what it remembered on the following ones.  What is remembered, as module attributes with the
+reference's names: `<name>_fp8_scale` always, `<name>_fp8` and `<name>_fp8_t` unless
+`qargs.weight_memory_efficient` (then only the scale is returned and the autograd blocks re-derive the
+codes from the bf16 weight where they need them)."""
 import torch.nn as nn
 
 from ..activation.real_quantization import fp8_division_transpose
+
+_SUFFIXES = ("_fp8", "_fp8_t", "_fp8_scale")
 
 
 class FP8CacheWeightModule(nn.Module):
     def __init__(self, config, qargs, layer_id):
         super().__init__()
-        self.config = config
-        self.qargs = qargs
-        self.layer_id = layer_id
+        self.config, self.qargs, self.layer_id = config, qargs, layer_id
+
+    def _recall(self, weight_name):
+        return tuple(getattr(self, weight_name + suffix) for suffix in _SUFFIXES)
 
     def prepare_weight(self, weight, weight_name, is_first_microbatch):
-        efficient = self.qargs.weight_memory_efficient
+        scale_only = self.qargs.weight_memory_efficient
         if is_first_microbatch:
-            w_fp8, w_s, w_fp8_t = fp8_division_transpose(weight, self.qargs.group_size, self.fwobits["fwbit"])
-            setattr(self, f"{weight_name}_fp8_scale", w_s)
-            if efficient:
-                return w_s
-            setattr(self, f"{weight_name}_fp8", w_fp8)
-            setattr(self, f"{weight_name}_fp8_t", w_fp8_t)
-            return w_fp8, w_fp8_t, w_s
-        if efficient:
-            return getattr(self, f"{weight_name}_fp8_scale")
-        return (getattr(self, f"{weight_name}_fp8"), getattr(self, f"{weight_name}_fp8_t"),
-                getattr(self, f"{weight_name}_fp8_scale"))
+            codes, scale, codes_t = fp8_division_transpose(weight, self.qargs.group_size, self.fwobits["fwbit"])
+            kept = (None, None, scale) if scale_only else (codes, codes_t, scale)
+            for suffix, value in zip(_SUFFIXES, kept):
+                if value is not None:
+                    setattr(self, weight_name + suffix, value)
+        if scale_only:
+            return getattr(self, weight_name + "_fp8_scale")
+        return self._recall(weight_name)
 
     def forward(self, x):
         pass
