@@ -135,3 +135,29 @@ def test_llama_mlp_shapes_sampled():
     check(dx, g, w_t, sg, sw, rows)
     check(dw, g_t, x_t, sg, sx, rows[:32] % I)
     assert _lib.lib().coat_fp8_gemm_device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K,quantize", [
+    (2112, 5200, 512, False),     # CTA pairs (K < 6144): 9 x 21 pair tiles on 74 pairs, ragged in M and N, several rounds
+    (4000, 2832, 6272, False),    # 256-row tiles (K >= 6144): 16 x 12 tiles on 148 SMs, a split last round, ragged edges
+    (128, 40192, 256, False),     # 128-row tiles (M <= 128): 157 tiles, two rounds
+    (1536, 4096, 384, True),      # quantising epilogue over several rounds of the pair kernel
+])
+def test_many_tiles_per_sm(M, N, K, quantize):
+    """More tiles than SMs, so that the persistent loops, the barrier phases across tiles and the tile walks of all
+    three kernels are exercised; checked against an fp64 GEMM of the same codes computed on the GPU."""
+    linear, _lib = mods()
+    a, b = codes(M, K, 11, torch.float8_e4m3fn, 20.0).cuda(), codes(N, K, 12, torch.float8_e4m3fn, 1.0).cuda()
+    sa, sb = sc(0.01), sc(0.25)
+    ref = G.fp8_matmul_fp64(a, b, sa, sb)
+    if not quantize:
+        c = linear.fp8matmul(a, b.t(), False, sa, sb, 16)
+        assert bool(G.within_tolerance(c, ref).all())
+    else:
+        q, s = linear.fp8matmul(a, b.t(), True, sa, sb, 16)
+        deq = (q.float().reshape(M, N // 16, 16) * s.float().unsqueeze(-1)).reshape(M, N).double()
+        # one E4M3 rounding of a value scaled into [0, 448]: half a step of 2^-3 relative, plus the bf16 scale
+        assert bool(((deq - ref).abs() <= 0.07 * ref.abs().reshape(M, N // 16, 16).amax(-1, keepdim=True)
+                     .expand(-1, -1, 16).reshape(M, N) + 1e-6).all())
+    torch.cuda.synchronize()
+    assert _lib.lib().coat_fp8_gemm_device_status() == 0
