@@ -33,6 +33,23 @@ def test_blockscaled_gemm_against_exact_arithmetic(M, N, K, fmt_a):
     assert bool(OG.within_tolerance(out.cpu(), ref).all())
 
 
+def test_blockscaled_gemm_many_tiles_and_ragged_rows():
+    """More tiles than SMs (persistent loop, barrier phases across tiles) and a row count that is not a multiple
+    of 128 (rows beyond M are neither scaled nor stored); checker computed in fp64 on the GPU."""
+    M, N, K = 2000, 2560, 384
+    gen = torch.Generator().manual_seed(6)
+    qx = (torch.randn(M, K, generator=gen) * 40).to(torch.float8_e4m3fn).cuda()
+    sx = (torch.rand(M, K // 128, generator=gen) * 0.05 + 0.001).cuda().t().contiguous().t()
+    qw = (torch.randn(N, K, generator=gen) * 40).to(torch.float8_e4m3fn).cuda()
+    sw = (torch.rand(N // 128, K // 128, generator=gen) * 0.02 + 0.001).cuda()
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gemm_fp8_fp8_bf16_nt((qx, sx), (qw, sw), out)
+    torch.cuda.synchronize()
+    assert _lib.lib().coat_fp8_gemm_device_status() == 0
+    ref = OG.blockscaled_matmul_fp64(qx, sx, qw, sw)
+    assert bool(OG.within_tolerance(out, ref).all())
+
+
 def test_blockscaled_gemm_scales_are_applied_per_k_block():
     """One K block scaled by 1000: the result must follow (a kernel that scaled per tile would not)."""
     M, N, K = 128, 128, 512
