@@ -336,7 +336,6 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
 // 32 warps per SM (2 CTAs) are what hides the latencies of the short dependent chains (shuffles, MUFU,
 // shared memory) of this kernel; with 256 threads per CTA it issued only half of the time.
 constexpr int kWT = 128;
-constexpr int kTmaThreads = 512;
 constexpr int kTmaStages = 2;
 constexpr int kTmaWaitLimit = 1 << 22;
 __device__ int g_quant_device_status = 0;   // COAT_E_TIMEOUT if a bounded wait on a staging copy ran out
@@ -348,22 +347,69 @@ template <typename T> constexpr size_t tma_quant_smem() {
     return (size_t)kTmaStages * kWT * kWT * sizeof(T) + 2 * kTileTBytes + 2 * kScaleTBytes + 64 + 128 /*alignment slack*/;
 }
 
-template <int FMT>
-__device__ __noinline__ uint32_t div_full_pack4(float a, float b, float c, float d, float s) {
-    return coat_float4_to_fp8x4<FMT>(coat_div_full(a, s), coat_div_full(b, s), coat_div_full(c, s), coat_div_full(d, s));
-}
+__device__ __noinline__ float div_full_outlined(float x, float s) { return coat_div_full(x, s); }
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_n, int& tm, int& tn) {
     tm = t / tiles_n;
     tn = t - tm * tiles_n;
 }
 
-template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT>
-__global__ void __launch_bounds__(kTmaThreads, sizeof(T) == 4 ? 1 : 2)
+// C = columns per thread: 8 (512 threads; more warps to hide latencies: best for the scalar-scale variant) or
+// 16 (256 threads; a 1x16 row group is thread-local and per-column work is shared by fewer threads: best for
+// the 1x16 quantize+transpose, 28.6 us against 31.3 us at 8192 x 4096).
+template <int C> struct TmaShape {
+    static constexpr int kThreads = kWT * kWT / (4 * C);
+};
+
+// rows / columns of the tile that a thread owns: warps tile the 128 x 128 tile in bands of 16 rows
+template <int C>
+__device__ __forceinline__ void tma_thread_origin(int warp, int lane, int& m_loc, int& n_loc) {
+    const int nb = lane & 7, mb = lane >> 3;
+    if (C == 8) { m_loc = (warp >> 1) * 16 + mb * 4; n_loc = (warp & 1) * 64 + nb * 8; }
+    else { m_loc = warp * 16 + mb * 4; n_loc = nb * 16; }
+}
+
+template <typename T, int C>
+__device__ __forceinline__ void load_cols(const T* p, float (&v)[C]) {
+    if constexpr (C == 8) load8(p, v);
+    else Seg16<T>::load(p, v);
+}
+
+template <int C>
+__device__ __forceinline__ float absmax_cols(const float (&v)[C]) {
+    float m[C / 2];
+#pragma unroll
+    for (int i = 0; i < C / 2; ++i) m[i] = fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+#pragma unroll
+    for (int w = C / 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) m[i] = fmaxf(m[2 * i], m[2 * i + 1]);
+    return m[0];
+}
+
+// C codes of one row, divided by `d`, to global memory (8 or 16 bytes)
+template <int FMT, int C, typename Divider>
+__device__ __forceinline__ void store_row_codes(uint8_t* dst, const float (&v)[C], const Divider& d) {
+    uint32_t w[C / 4];
+#pragma unroll
+    for (int i = 0; i < C / 4; ++i)
+        w[i] = coat_float4_to_fp8x4<FMT>(d(v[4 * i]), d(v[4 * i + 1]), d(v[4 * i + 2]), d(v[4 * i + 3]));
+    if constexpr (C == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+struct DivFullDivider {   // the division instruction itself, out of line (scales outside [2^-120, 2^120])
+    float s;
+    __device__ __forceinline__ float operator()(float x) const { return div_full_outlined(x, s); }
+};
+
+template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT, int C>
+__global__ void __launch_bounds__(TmaShape<C>::kThreads, sizeof(T) == 4 ? 1 : 2)
 transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* __restrict__ y,
                            uint8_t* __restrict__ y_t, void* __restrict__ s_y, void* __restrict__ s_y_t,
                            const void* __restrict__ s_in, void* __restrict__ s_out, int scale_dtype,
                            const unsigned int* __restrict__ amax_bits, int M, int N, int tiles_m, int tiles_n) {
+    constexpr int kThreads = TmaShape<C>::kThreads;
     const int n_tiles = tiles_m * tiles_n;
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 127) & ~(uintptr_t)127);
@@ -372,9 +418,11 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
     uint64_t* full = reinterpret_cast<uint64_t*>(after_stages + 2 * kTileTBytes + 2 * kScaleTBytes);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nb = lane & 7, mb = lane >> 3;
-    const int m_loc = (warp >> 1) * 16 + mb * 4, n_loc = (warp & 1) * 64 + nb * 8;
-    const int word = ((m_loc >> 2) + 4 * (n_loc >> 3)) & 31;   // rotated slot of this thread's 4 rows
+    const int mb = lane >> 3;
+    int m_loc, n_loc;
+    tma_thread_origin<C>(warp, lane, m_loc, n_loc);
+    // rotated slot of this thread's 4 rows in a transposed row: 4 words further per C columns
+    const int word = ((m_loc >> 2) + 4 * (n_loc / C)) & 31;
     const GroupScale<FMT, IEEE> group_scale;
     float scalar = 1.f;
     if (!GROUPS) {
@@ -407,70 +455,57 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
         uint32_t (*tile_t)[32] = reinterpret_cast<uint32_t (*)[32]>(after_stages + (size_t)(k & 1) * kTileTBytes);
         float (*scale_t)[8] = reinterpret_cast<float (*)[8]>(after_stages + 2 * kTileTBytes + (size_t)(k & 1) * kScaleTBytes);
         const bool arrived = coat_tma::mbar_wait(&full[s], (uint32_t)(k / kTmaStages) & 1u, kTmaWaitLimit);
-        float v[4][8];
+        float v[4][C];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) load8(stage + (m_loc + j) * kWT + n_loc, v[j]);
+        for (int j = 0; j < 4; ++j) load_cols<T, C>(stage + (m_loc + j) * kWT + n_loc, v[j]);
         int tm, tn;
         tile_coords(t, tiles_n, tm, tn);
         const int m_tile = tm * kWT, n_tile = tn * kWT;
         const int m0 = m_tile + m_loc, n0 = n_tile + n_loc;
-        // M and N are multiples of 16 and a lane pair shares a 16-column group: a 4 x 16 block is in or out as a whole
+        // M and N are multiples of 16 and the lanes of a 16-column group sit side by side: a 4 x 16 block is in the
+        // matrix or outside it as a whole
         const bool inside = m0 < M && n0 < N;
         if (GROUPS) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {   // row groups: this lane's 8 columns and its neighbour's
-                float a = fmaxf(fmaxf(fmaxf(fabsf(v[j][0]), fabsf(v[j][1])), fmaxf(fabsf(v[j][2]), fabsf(v[j][3]))),
-                                fmaxf(fmaxf(fabsf(v[j][4]), fabsf(v[j][5])), fmaxf(fabsf(v[j][6]), fabsf(v[j][7]))));
-                a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 1));
+            for (int j = 0; j < 4; ++j) {   // row groups (C = 8: this lane's columns and its neighbour's)
+                float a = absmax_cols<C>(v[j]);
+                if (C == 8) a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 1));
                 const float rs = group_scale(a);
-                const GroupScaleDivider<IEEE> d(rs);
                 if (inside) {
-                    uint2 w;
-                    w.x = coat_float4_to_fp8x4<FMT>(d(v[j][0]), d(v[j][1]), d(v[j][2]), d(v[j][3]));
-                    w.y = coat_float4_to_fp8x4<FMT>(d(v[j][4]), d(v[j][5]), d(v[j][6]), d(v[j][7]));
-                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
-                    if ((nb & 1) == 0) store_scale(s_y, (int64_t)(m0 + j) * (N >> 4) + (n0 >> 4), scale_dtype, rs);
+                    store_row_codes<FMT, C>(y + (int64_t)(m0 + j) * N + n0, v[j], GroupScaleDivider<IEEE>(rs));
+                    if (C == 16 || (lane & 1) == 0)
+                        store_scale(s_y, (int64_t)(m0 + j) * (N >> 4) + (n0 >> 4), scale_dtype, rs);
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {   // column groups
+            for (int i = 0; i < C; ++i) {   // column groups: the 4 lanes mb = 0..3
                 float a = fmaxf(fmaxf(fabsf(v[0][i]), fabsf(v[1][i])), fmaxf(fabsf(v[2][i]), fabsf(v[3][i])));
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 8));
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 16));
                 const float cs = group_scale(a);
                 const GroupScaleDivider<IEEE> d(cs);
                 tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
-                if ((i & 3) == mb) scale_t[n_loc + i][warp >> 1] = cs;   // the four lanes of a group share the stores
+                if ((i & 3) == mb) scale_t[n_loc + i][m_loc >> 4] = cs;   // the four lanes of a group share the stores
             }
         } else if (IEEE || by_scalar.fast) {
             // the usual case, decided once per tile: one multiplication (or IEEE division) per element
             const GroupScaleDivider<IEEE> d(scalar);
             if (STRAIGHT && inside) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint2 w;
-                    w.x = coat_float4_to_fp8x4<FMT>(d(v[j][0]), d(v[j][1]), d(v[j][2]), d(v[j][3]));
-                    w.y = coat_float4_to_fp8x4<FMT>(d(v[j][4]), d(v[j][5]), d(v[j][6]), d(v[j][7]));
-                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
-                }
+                for (int j = 0; j < 4; ++j) store_row_codes<FMT, C>(y + (int64_t)(m0 + j) * N + n0, v[j], d);
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < C; ++i)
                 tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
         } else {
-            // a caller's scale outside [2^-120, 2^120]: the division instruction itself, out of line
+            const DivFullDivider d{scalar};
             if (STRAIGHT && inside) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint2 w;
-                    w.x = div_full_pack4<FMT>(v[j][0], v[j][1], v[j][2], v[j][3], scalar);
-                    w.y = div_full_pack4<FMT>(v[j][4], v[j][5], v[j][6], v[j][7], scalar);
-                    *reinterpret_cast<uint2*>(y + (int64_t)(m0 + j) * N + n0) = w;
-                }
+                for (int j = 0; j < 4; ++j) store_row_codes<FMT, C>(y + (int64_t)(m0 + j) * N + n0, v[j], d);
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                tile_t[n_loc + i][word] = div_full_pack4<FMT>(v[0][i], v[1][i], v[2][i], v[3][i], scalar);
+            for (int i = 0; i < C; ++i)
+                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
         }
         // The one barrier of the tile: stage s has been read by everyone (it can be refilled) and this tile's
         // transposed codes and scales are complete.  Tile k+1 writes the other pair of buffers, and nobody
@@ -499,13 +534,13 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
         }
         // transposed rows leave in 16-byte pieces: one warp instruction = 4 rows x 128 contiguous bytes
 #pragma unroll
-        for (int it = 0; it < kWT * 8 / kTmaThreads; ++it) {
-            const int idx = it * kTmaThreads + threadIdx.x;
+        for (int it = 0; it < kWT * 8 / kThreads; ++it) {
+            const int idx = it * kThreads + threadIdx.x;
             const int r = idx >> 3, c = idx & 7;
             const int n = n_tile + r, m = m_tile + c * 16;
             if (n < N && m < M)
                 *reinterpret_cast<uint4*>(y_t + (int64_t)n * M + m) =
-                    *reinterpret_cast<const uint4*>(&tile_t[r][(4 * c + 4 * (r >> 3)) & 31]);
+                    *reinterpret_cast<const uint4*>(&tile_t[r][(4 * c + 4 * (r / C)) & 31]);
         }
         if (GROUPS && threadIdx.x < kWT) {   // transposed scales: 8 consecutive row groups per column of x
             const int n = n_tile + threadIdx.x;
@@ -543,7 +578,8 @@ int launch_transpose_tma(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, voi
                          int scale_dtype, const unsigned int* amax, int64_t M, int64_t N, int64_t ldx, cudaStream_t st) {
     CUtensorMap map;
     if (!coat_tma::make_map_2d(&map, x, (int)sizeof(T), M, N, ldx * (int64_t)sizeof(T), kWT, kWT)) return COAT_E_DEVICE;
-    auto kern = transpose_quant_tma_kernel<T, FMT, IEEE, GROUPS, STRAIGHT>;
+    constexpr int C = GROUPS ? 16 : 8;
+    auto kern = transpose_quant_tma_kernel<T, FMT, IEEE, GROUPS, STRAIGHT, C>;
     constexpr size_t smem = tma_quant_smem<T>();
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return COAT_E_LAUNCH;
@@ -551,7 +587,7 @@ int launch_transpose_tma(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, voi
     const int64_t n_tiles = tiles_n * tiles_m;
     const int64_t cap = (int64_t)coat_sm_count() * (sizeof(T) == 4 ? 1 : 2);
     const int grid = (int)(n_tiles < cap ? n_tiles : cap);
-    kern<<<grid, kTmaThreads, smem, st>>>(map, y, y_t, s_y, s_y_t, s_in, s_out, scale_dtype, amax, (int)M, (int)N,
+    kern<<<grid, TmaShape<C>::kThreads, smem, st>>>(map, y, y_t, s_y, s_y_t, s_in, s_out, scale_dtype, amax, (int)M, (int)N,
                                            (int)tiles_m, (int)tiles_n);
     return coat_launch_status();
 }
