@@ -6,3 +6,9 @@ from .coat_llama import (  # noqa: F401
     CoatLlamaMLPResidual,
     LlamaSdpaAttentionWithoutLinear,
 )
+from .coat_llama_model import (  # noqa: F401
+    CoatLlamaForCausalLM,
+    CoatLlamaModel,
+    chunked_causal_lm_loss,
+    make_state_dict_compatible,
+)

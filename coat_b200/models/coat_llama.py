@@ -13,8 +13,8 @@ coat/models/coat_llama.py of the reference: a decoder layer is three autograd bl
 
 and whose backward passes run the mirrored chain on E5M2 gradients.  What is saved for backward is what
 the reference saves (FP8 activations and transposed FP8 copies, never a bf16 activation except the
-attention output).  Only the layer is provided: the HF model / tokenizer / generation plumbing around it
-is not part of this package, and `CoatLlamaConfig` is a plain attribute bag (any object with the same
+attention output).  The model around the layers is in coat_llama_model.py; tokenizer and generation
+plumbing are not part of this package, and `CoatLlamaConfig` is a plain attribute bag (any object with the same
 attributes, e.g. a transformers LlamaConfig carrying `coat_fp8_args`, works).
 
 FP8 tensors cross autograd boundaries viewed as float8_e4m3fn whatever their real format (autograd
@@ -50,13 +50,14 @@ from ..utils._fp8manager import FP8Manager
 
 class CoatLlamaConfig:
     """The attributes of the reference's CoatLlamaConfig (a transformers LlamaConfig plus `coat_fp8_args`,
-    coat_llama.py:106-107) that the decoder layer reads."""
+    coat_llama.py:106-107) that the decoder layer and the model read."""
     model_type = "fp8_llama"
 
     def __init__(self, hidden_size=4096, intermediate_size=11008, num_attention_heads=32, num_key_value_heads=None,
                  head_dim=None, rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=4096,
                  attention_bias=False, attention_dropout=0.0, mlp_bias=False, hidden_act="silu",
-                 coat_fp8_args=None, _attn_implementation="sdpa", **kwargs):
+                 coat_fp8_args=None, _attn_implementation="sdpa", vocab_size=32000, num_hidden_layers=32,
+                 pad_token_id=None, initializer_range=0.02, tie_word_embeddings=False, **kwargs):
         self.hidden_size = hidden_size
         self.intermediate_size = intermediate_size
         self.num_attention_heads = num_attention_heads
@@ -71,6 +72,11 @@ class CoatLlamaConfig:
         self.hidden_act = hidden_act
         self.coat_fp8_args = dict(coat_fp8_args or {})
         self._attn_implementation = _attn_implementation
+        self.vocab_size = vocab_size
+        self.num_hidden_layers = num_hidden_layers
+        self.pad_token_id = pad_token_id
+        self.initializer_range = initializer_range
+        self.tie_word_embeddings = tie_word_embeddings
         for k, v in kwargs.items():
             setattr(self, k, v)
 
