@@ -17,6 +17,7 @@ ADAMW_EXACT_POW = 1
 MAX_PEERS = 7            # COAT_MAX_PEERS
 PEER_HANDLE_BYTES = 64   # COAT_PEER_HANDLE_BYTES
 QUANT_IEEE_DIV = 1
+QUANT_STOCHASTIC = 2
 
 # Default flags of the quantizer entry points: 0 = the reference's (Triton's) division, QUANT_IEEE_DIV
 # = IEEE division.  Tests that compare with the CPU checker switch it.

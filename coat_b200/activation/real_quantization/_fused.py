@@ -35,7 +35,7 @@ def _amax_word(device):
     return torch.empty(1, dtype=torch.int32, device=device)
 
 
-def _divide(y_bf16, fp8type, amax, want_transposed, flags, scale_dtype=torch.bfloat16):
+def _divide(y_bf16, fp8type, amax, want_transposed, flags, scale_dtype=torch.bfloat16, stochastic=False):
     """Per-tensor quantize of a bf16 intermediate with the scale derived from the amax word."""
     M, N = y_bf16.shape
     dev = y_bf16.device
@@ -44,7 +44,8 @@ def _divide(y_bf16, fp8type, amax, want_transposed, flags, scale_dtype=torch.bfl
     s_max = torch.empty((), dtype=scale_dtype, device=dev)
     _call("coat_fp8_division", y_bf16.data_ptr(), q.data_ptr(), None if q_t is None else q_t.data_ptr(), None,
           s_max.data_ptr(), amax.data_ptr(), M, N, N, _lib.fp8_format(fp8type)[0], _lib.BF16,
-          _lib.float_dtype(scale_dtype), _flags(flags), _lib.stream_ptr(dev))
+          _lib.float_dtype(scale_dtype), _flags(flags) | (_lib.QUANT_STOCHASTIC if stochastic else 0),
+          _lib.stream_ptr(dev))
     return q, s_max, q_t
 
 
@@ -73,8 +74,7 @@ def _act_backward(gelu, x, s_x, g, QB, fp8type, flags):
 
 
 def fp8_silu_backward(x, s_x, g, QB, fp8type, stochastic=False, output_quantized_transpose=False, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
+    # `stochastic` is accepted and has no effect, as in the reference (silu_bwd.py:170-238 never reads it)
     with torch.cuda.device(x.device):
         y, s_y, amax, bs, fp8type = _act_backward(False, x, s_x, g, QB, fp8type, flags)
         if not output_quantized_transpose:
@@ -124,8 +124,8 @@ def fp8_mul_forward(x1, s_x1, x2, s_x2, QB, transpose_output_2d=False, *, flags=
 
 def fp8_mul_backward(x1, s_x1, x2, s_x2, g, QB, fp8type, stochastic=False, output_quantized_transpose=False, *,
                      flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
+    # `stochastic` is accepted and has no effect on the results, as in the reference (mul_bwd.py:236-290 draws
+    # a noise tensor and hands the kernel a flag that the kernel never reads)
     (a, sa, b, sb, g2), bs = _flat(x1, s_x1, x2, s_x2, g)
     assert a.shape == b.shape and sa.shape == sb.shape
     M, N = a.shape
@@ -169,12 +169,10 @@ def fp8_add_Ifp_Ifp_Ofp_Og16(x1, x2, fp8type, QB, *, flags=None):
 
 
 def fp8_add_Ifp_Ifp_Ofp_Opt(x1, x2, QB, fp8type, stochastic=False, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
     fp8type = _fp8_dtype(fp8type)
     with torch.cuda.device(x1.device):
         y1, _, s_y2, amax, bs = _add(x1, x2, QB, fp8type, False, True, flags)
-        qy2, s_max, _ = _divide(y1, fp8type, amax, False, flags)
+        qy2, s_max, _ = _divide(y1, fp8type, amax, False, flags, stochastic=stochastic)   # add_bwd.py:192
     return _unflat(y1, bs), (_unflat(qy2, bs), s_max, _unflat(s_y2, bs))
 
 

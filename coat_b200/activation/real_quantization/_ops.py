@@ -66,7 +66,12 @@ def fp8_quantize(x, QB, fp8type, scale_dtype=torch.bfloat16, *, flags=None):
     return y, s_y
 
 
-def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_transposed, flags):
+def _flags_stochastic(flags, stochastic):
+    """Division flags with the reference's stochastic rounding (_division.py:96-150) switched on or not."""
+    return _flags(flags) | (_lib.QUANT_STOCHASTIC if stochastic else 0)
+
+
+def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_transposed, flags, stochastic=False):
     """Pass 1 (tensor amax, optional group scales) + pass 2 (division by the one scale)."""
     M, N = x.shape
     fmt = _lib.fp8_format(fp8type)[0]
@@ -82,16 +87,15 @@ def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_tra
         _call("coat_fp8_group_scales_amax", x.data_ptr(), P(s_y), amax.data_ptr(), M, N, x.stride(0), QB, fmt,
               _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
         _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), None, s_max.data_ptr(), amax.data_ptr(), M, N,
-              x.stride(0), fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
+              x.stride(0), fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags_stochastic(flags, stochastic),
+              st)
     return y, s_max, s_y, y_t
 
 
 def fp8_quantize_pertensor(x, QB, fp8type, stochastic=False, scale_dtype=torch.bfloat16, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
     x, bs = _prep(x)
     fp8type = _fp8_dtype(fp8type)
-    y, s_max, s_y, _ = _pertensor(x, QB, fp8type, scale_dtype, True, True, False, flags)
+    y, s_max, s_y, _ = _pertensor(x, QB, fp8type, scale_dtype, True, True, False, flags, stochastic)
     if bs is not None:
         y = y.reshape(bs, -1, y.shape[-1])
         s_y = s_y.reshape(bs, -1, s_y.shape[-1])
@@ -100,11 +104,9 @@ def fp8_quantize_pertensor(x, QB, fp8type, stochastic=False, scale_dtype=torch.b
 
 def fp8_quantize_pertensor_transpose(x, QB, fp8type, transpose_output_2d=False, stochastic=False,
                                      scale_dtype=torch.bfloat16, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
     x, bs = _prep(x)
     fp8type = _fp8_dtype(fp8type)
-    qy, s_max, _, qy_t = _pertensor(x, QB, fp8type, scale_dtype, False, True, True, flags)
+    qy, s_max, _, qy_t = _pertensor(x, QB, fp8type, scale_dtype, False, True, True, flags, stochastic)
     if bs is not None:
         qy = qy.reshape(bs, -1, qy.shape[-1])
         if not transpose_output_2d:
@@ -123,8 +125,9 @@ def _default_scale(x, fp8type, flags):
     return (amax.view(torch.float32)[0].to(x.dtype) + SCALE_MIN_THRES) / FP8_MAX_VALUE[fp8type]
 
 
-def _division(x, fp8type, s_y, want_straight, want_transposed, flags):
+def _division(x, fp8type, s_y, want_straight, want_transposed, flags, stochastic=False):
     M, N = x.shape
+    want_straight = want_straight or stochastic   # the stochastic transposed copy is made from the straight one
     if s_y is None:
         s_y = _default_scale(x, fp8type, flags)
     if not torch.is_tensor(s_y):
@@ -136,28 +139,24 @@ def _division(x, fp8type, s_y, want_straight, want_transposed, flags):
     P = lambda t: None if t is None else t.data_ptr()
     with torch.cuda.device(x.device):
         _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), s_y.data_ptr(), None, None, M, N, x.stride(0),
-              _lib.fp8_format(fp8type)[0], _lib.float_dtype(x), _lib.float_dtype(s_y), _flags(flags),
-              _lib.stream_ptr(x.device))
+              _lib.fp8_format(fp8type)[0], _lib.float_dtype(x), _lib.float_dtype(s_y),
+              _flags_stochastic(flags, stochastic), _lib.stream_ptr(x.device))
     return y, s_y, y_t
 
 
 def fp8_division(x, QB, fp8type, s_y=None, stochastic=False, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
     x, bs = _prep(x)
     fp8type = _fp8_dtype(fp8type)
-    y, s_y, _ = _division(x, fp8type, s_y, True, False, flags)
+    y, s_y, _ = _division(x, fp8type, s_y, True, False, flags, stochastic)
     if bs is not None:
         y = y.reshape(bs, -1, y.shape[-1])
     return y, s_y
 
 
 def fp8_division_transpose(x, QB, fp8type, s_y=None, stochastic=False, only_transposed=False, *, flags=None):
-    if stochastic:
-        raise NotImplementedError("stochastic rounding is not provided")
     x, bs = _prep(x)
     fp8type = _fp8_dtype(fp8type)
-    y, s_y, y_t = _division(x, fp8type, s_y, not only_transposed, True, flags)
+    y, s_y, y_t = _division(x, fp8type, s_y, not only_transposed, True, flags, stochastic)
     if only_transposed:
         return y_t, s_y
     if bs is not None:

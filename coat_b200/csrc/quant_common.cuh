@@ -192,6 +192,40 @@ __device__ __forceinline__ uint4 pack16(const float (&q)[16]) {
     return r;
 }
 
+// ---- stochastic rounding of the reference (_division.py:96-150) ---------------------------------------
+// Its noise is Triton's tl.rand(0, offset): Philox-4x32 with 10 rounds (Salmon et al., SC'11), key = the two
+// words of the seed (0 here), counter = (offset, 0, 0, 0), first output word w mapped to [0, 1) as
+// int32 w -> (w >= 0 ? w : -w - 1) * 4.6566127342e-10.
+__device__ __forceinline__ float triton_rand_seed0(uint32_t offset) {
+    uint32_t c0 = offset, c1 = 0, c2 = 0, c3 = 0, k0 = 0, k1 = 0;
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t a = c0, b = c2;
+        c0 = __umulhi(0xCD9E8D57u, b) ^ c1 ^ k0;
+        c2 = __umulhi(0xD2511F53u, a) ^ c3 ^ k1;
+        c1 = 0xCD9E8D57u * b;
+        c3 = 0xD2511F53u * a;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    const int32_t w = (int32_t)c0;
+    return __int2float_rn(w < 0 ? -w - 1 : w) * 4.6566127342e-10f;
+}
+
+// |q| + noise * (one step of the FP8 format at q's exponent), clamped to q's binade (below the normal range:
+// to [smallest subnormal, smallest normal], which also turns zeros into the smallest subnormal, as the
+// reference does), with q's sign.  The saturating round-to-nearest cast follows at the caller.
+template <int FMT>
+__device__ __forceinline__ float stochastic_perturb(float q, float noise) {
+    constexpr float kSubMin = FMT == COAT_E4M3 ? 0.001953125f : 1.52587890625e-05f;   // 2^-9, 2^-16
+    constexpr float kStep = FMT == COAT_E4M3 ? 0.125f : 0.25f;                         // 2^-m
+    constexpr float kSubSpan = FMT == COAT_E4M3 ? 8.f : 4.f;                           // 2^m
+    const float e = fmaxf(__uint_as_float(__float_as_uint(q) & 0x7f800000u), kSubMin);
+    const bool sub = e == kSubMin;
+    const float a = fabsf(q) + __fmul_rn(__fmul_rn(e, noise), sub ? 1.f : kStep);
+    return copysignf(fminf(fmaxf(a, e), __fmul_rn(sub ? kSubSpan : 2.f, e)), q);
+}
+
 // max over the `lanes` (power of two <= 8) neighbouring lanes that share a group
 __device__ __forceinline__ float subgroup_max(float v, int lanes) {
     for (int o = 1; o < lanes; o <<= 1) v = fmaxf(v, __shfl_xor_sync(COAT_FULL_MASK, v, o));

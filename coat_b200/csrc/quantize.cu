@@ -160,7 +160,9 @@ __device__ __forceinline__ float tensor_scale_from_amax(const unsigned int* amax
 // =================================================================================================
 // The scale is either a device scalar in `scale_dtype` (scale_from_amax == 0) or derived from the amax word
 // of pass 1, in which case block 0 also writes it to `s_out` (in `scale_dtype`).
-template <typename T, int FMT, bool IEEE>
+// STOCH: the reference's stochastic rounding; the noise of element (m, n) is drawn at offset m * ldx + n
+// (32-bit arithmetic, as in the reference's kernel).
+template <typename T, int FMT, bool IEEE, bool STOCH>
 __global__ void __launch_bounds__(kStraightThreads)
 division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __restrict__ s_in, void* __restrict__ s_out,
                 int scale_dtype, const unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int64_t ldx,
@@ -176,6 +178,11 @@ division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __
     float v[16], q[16];
     Seg16<T>::load(x + seg_offset(seg, segs_per_row, ldx), v);
     divide.apply(v, q);
+    if (STOCH) {
+        const uint32_t off0 = (uint32_t)seg_offset(seg, segs_per_row, ldx);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = stochastic_perturb<FMT>(q[i], triton_rand_seed0(off0 + (uint32_t)i));
+    }
     *reinterpret_cast<uint4*>(y + seg_offset(seg, segs_per_row, ldy)) = pack16<FMT>(q);
 }
 
@@ -666,10 +673,18 @@ struct GroupQuantArgs {
 
 struct DivisionArgs {
     const void* x; uint8_t* y; uint8_t* y_t; const void* s_in; void* s_out; int scale_dtype; const unsigned int* amax;
-    int64_t M, N, ldx; cudaStream_t st;
+    int64_t M, N, ldx; cudaStream_t st; bool stochastic;
     template <typename T, int FMT, bool IEEE> int run() const {
+        if (stochastic) {
+            // rare path: the straight kernel, then (the noise depends on the element's position only, so the
+            // transposed copy holds the same codes) a byte transpose of its output
+            division_kernel<T, FMT, IEEE, true><<<straight_grid(M * (N / 16)), kStraightThreads, 0, st>>>(
+                reinterpret_cast<const T*>(x), y, s_in, s_out, scale_dtype, amax, M, N, ldx, N);
+            if (int rc = coat_launch_status()) return rc;
+            return y_t ? coat_fp8_transpose(y, y_t, M, N, st) : COAT_OK;
+        }
         if (!y_t) {
-            division_kernel<T, FMT, IEEE><<<straight_grid(M * (N / 16)), kStraightThreads, 0, st>>>(
+            division_kernel<T, FMT, IEEE, false><<<straight_grid(M * (N / 16)), kStraightThreads, 0, st>>>(
                 reinterpret_cast<const T*>(x), y, s_in, s_out, scale_dtype, amax, M, N, ldx, N);
             return coat_launch_status();
         }
@@ -743,7 +758,9 @@ extern "C" int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const 
     if (!x || (!y && !y_t) || (!s_in && !amax_bits) || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
     if (int rc = check_2d(x, M, N, ldx, in_dtype, 16)) return rc;
     if ((y && !coat_aligned(y, 16)) || (y_t && (!coat_aligned(y_t, 4) || M % 4 != 0))) return COAT_E_ALIGN;
-    DivisionArgs a{x, y, y_t, s_in, s_out, scale_dtype, amax_bits, M, N, ldx, (cudaStream_t)stream};
+    const bool stochastic = flags & COAT_QUANT_STOCHASTIC;
+    if (stochastic && !y) return COAT_E_BADARG;   // the transposed copy is made from y
+    DivisionArgs a{x, y, y_t, s_in, s_out, scale_dtype, amax_bits, M, N, ldx, (cudaStream_t)stream, stochastic};
     return dispatch(in_dtype, fmt, flags, a);
 }
 
@@ -913,6 +930,7 @@ extern "C" int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uin
     StaticAmaxArgs a{x, scratch, M, N, ldx, n_ctas, (cudaStream_t)stream};
     if (int rc = dispatch(in_dtype, fmt, flags, a)) return rc;
     DivisionArgs d{x, y, y_t, nullptr, s_out, scale_dtype,
-                   reinterpret_cast<const unsigned int*>(scratch) + kStaticMaxCtas, M, N, ldx, (cudaStream_t)stream};
+                   reinterpret_cast<const unsigned int*>(scratch) + kStaticMaxCtas, M, N, ldx, (cudaStream_t)stream,
+                   false};
     return dispatch(in_dtype, fmt, flags, d);
 }

@@ -8,6 +8,8 @@ depend on it; `coat_optimizer_groups` and `build_coat_optimizer` hold the logic 
 """
 import os
 
+import torch
+
 from .optimizer.fp8_adamw import CoatAdamW
 
 
@@ -33,6 +35,51 @@ def build_coat_optimizer(model, args, decay_parameter_names, qargs=None):
     if qargs is not None:
         kwargs["qargs"] = qargs
     return CoatAdamW(groups, **kwargs)
+
+
+class MasterWeights:
+    """fp32 master copies of a bf16 model's parameters.  CoatAdamW steps fp32 parameters (like the reference's
+    kernel, whose per-group vectors are float32 by contract) while the FP8 layers compute on bf16 weights; in
+    the reference the surrounding framework (DeepSpeed / FSDP mixed precision) holds the masters.  This is
+    the single-process form: the optimizer is built over `named_parameters()` of this object, `copy_grads()`
+    hands it the model's gradients in fp32, and after `attach(optimizer)` every step writes the bf16 model
+    weights from inside the optimizer kernel."""
+
+    def __init__(self, model):
+        self.names, self.model_params, self.masters = [], [], []
+        for name, p in model.named_parameters():
+            if not p.requires_grad:
+                continue
+            self.names.append(name)
+            self.model_params.append(p)
+            self.masters.append(torch.nn.Parameter(p.detach().float().clone()))
+
+    def named_parameters(self):
+        return list(zip(self.names, self.masters))
+
+    def attach(self, optimizer):
+        optimizer.attach_bf16_weights(
+            (m, p.data) for m, p in zip(self.masters, self.model_params) if p.dtype == torch.bfloat16)
+
+    @torch.no_grad()
+    def copy_grads(self, zero_model_grads=True):
+        for m, p in zip(self.masters, self.model_params):
+            if p.grad is None:
+                m.grad = None
+                continue
+            if m.grad is None:
+                m.grad = p.grad.float()
+            else:
+                m.grad.copy_(p.grad)
+            if zero_model_grads:
+                p.grad = None
+
+    @torch.no_grad()
+    def write_back(self):
+        """For parameters that are not bf16 (no fused copy): master -> model."""
+        for m, p in zip(self.masters, self.model_params):
+            if p.dtype != torch.bfloat16:
+                p.copy_(m)
 
 
 _trainer_class = None

@@ -66,12 +66,26 @@ class CoatAdamW(Optimizer):
         super().__init__(params, defaults)
         self.multi_tensor = multi_tensor
         self._tables = {}
+        self._bf16_copies = {}
+
+    def attach_bf16_weights(self, pairs):
+        """Mixed-precision training: `pairs` = iterable of (fp32 parameter of this optimizer, bf16 tensor of the
+        same number of elements).  From now on each step also writes the updated weights, rounded to bf16, into
+        the bf16 tensor, inside the same kernel (no separate cast pass).  An extension: the reference leaves the
+        cast to the surrounding framework."""
+        for master, copy in pairs:
+            if copy.dtype != torch.bfloat16 or copy.numel() != master.numel() or not copy.is_contiguous() \
+                    or copy.device != master.device:
+                raise ValueError("a bf16 copy must be a contiguous bfloat16 tensor of the parameter's size and device")
+            self._bf16_copies[id(master)] = copy
+        self._tables = {}
 
     # ---- (de)serialisation -------------------------------------------------------------
     def __setstate__(self, state):
         super().__setstate__(state)
         self.__dict__.setdefault("multi_tensor", True)
         self.__dict__["_tables"] = {}
+        self.__dict__.setdefault("_bf16_copies", {})
         for group in self.param_groups:
             group.setdefault("amsgrad", False)
             group.setdefault("fused", None)
@@ -214,6 +228,10 @@ class CoatAdamW(Optimizer):
                     [], key(states, "step"), amsgrad=group["amsgrad"], use_expansion=exp, **hyper,
                     fused=group["fused"], grad_scale=getattr(self, "grad_scale", None),
                     found_inf=getattr(self, "found_inf", None))
+                for p in params:   # the per-tensor entry points keep the reference's signature: cast afterwards
+                    copy = self._bf16_copies.get(id(p))
+                    if copy is not None:
+                        copy.view(-1).copy_(p.detach().view(-1))
         return loss
 
     def _multi_tensor_step(self, gi, params, states, use_expansion, *, beta1, beta2, lr, weight_decay, eps,
@@ -247,6 +265,9 @@ class CoatAdamW(Optimizer):
                         r["r_m"] = _lib.dev_ptr(st["sqrt_minmax_exp_avg"])
                         r["k_v"] = _lib.dev_ptr(st["expand_exp_avg_sq"])
                         r["r_v"] = _lib.dev_ptr(st["sqrt_minmax_exp_avg_sq"])
+                    copy = self._bf16_copies.get(id(p))
+                    if copy is not None:
+                        r["bf16_out"] = _lib.dev_ptr(copy)
                     r["numel"] = p.numel()
                     prefix[row + 1] = prefix[row] + (p.numel() + 127) // 128
                 pinned = torch.from_numpy(host.view(np.uint8).reshape(-1)).pin_memory()

@@ -48,6 +48,7 @@ extern "C" {
  * PTX div.full.f32 the reference's Triton kernels compile to (a CPU can reproduce IEEE
  * division bit for bit; div.full.f32 differs from it in the last place now and then).   */
 #define COAT_QUANT_IEEE_DIV 1
+#define COAT_QUANT_STOCHASTIC 2   /* coat_fp8_division only: the reference's stochastic rounding */
 
 const char* coat_b200_version(void);
 const char* coat_strerror(int code);
@@ -173,8 +174,11 @@ int coat_fp8_group_scales_amax(const void* x, void* s_y, unsigned int* amax_bits
  * NULL (y == NULL is the reference's only_transposed=True).  The scale is the device scalar *s_in of
  * scale_dtype, or, if amax_bits != NULL, round_to_scale_dtype((amax + 1e-10) / fp8_max) taken from pass 1,
  * which is then also written to *s_out.  Replaces fp8_division (_division.py:153-207, kernel :45-126) and
- * fp8_division_transpose (_division_transpose.py:147-210, kernel :48-144); stochastic rounding is not
- * provided (no caller in the reference's models enables it). */
+ * fp8_division_transpose (_division_transpose.py:147-210, kernel :48-144).  With COAT_QUANT_STOCHASTIC in
+ * flags the quotient is perturbed before the cast as the reference's `stochastic=True` does
+ * (_division.py:96-150: noise = Triton's rand(seed 0, offset m * ldx + n), i.e. Philox-4x32-10, scaled to one
+ * step of the format and clamped to the quotient's binade); y must then be given (y_t, if wanted, is its
+ * byte transpose). */
 int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const void* s_in, void* s_out,
                       const unsigned int* amax_bits, int64_t M, int64_t N, int64_t ldx, int fmt,
                       int in_dtype, int scale_dtype, int flags, void* stream);

@@ -99,3 +99,67 @@ def fp8_quantize_block128(x, fp8type, scale_dtype=torch.float32):
     q_c = cast_fp8((xt.reshape(N, M // 128, 128) / s_c[:, :, None]).reshape(N, M), fp8type)
     return {"block": (q_b, s_b.to(scale_dtype)), "block_t": (q_b.t().contiguous(), s_b.t().contiguous().to(scale_dtype)),
             "rows": (q_r, s_r.to(scale_dtype)), "cols_t": (q_c, s_c.to(scale_dtype))}
+
+
+# ---- stochastic rounding (_division.py:96-112, 129-150) -------------------------------------------------
+# The reference draws its noise with tl.rand(0, offset): Triton's counter-based generator, i.e. the published
+# Philox-4x32 with 10 rounds (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3", SC'11; Triton
+# 3.x, triton/language/random.py) with key = (seed low word, seed high word), counter = (offset, 0, 0, 0),
+# the first output word mapped to [0, 1) as int32 x -> (x if x >= 0 else -x - 1) * 4.6566127342e-10.
+import numpy as np  # noqa: E402
+
+_PHILOX_KEY_A, _PHILOX_KEY_B = 0x9E3779B9, 0xBB67AE85
+_PHILOX_ROUND_A, _PHILOX_ROUND_B = 0xD2511F53, 0xCD9E8D57
+
+
+def philox4x32(counter, key, rounds=10):
+    """counter: 4 arrays of uint32; key: (k0, k1) ints.  Returns the 4 output arrays (uint32)."""
+    c0, c1, c2, c3 = (np.asarray(c, dtype=np.uint64) for c in counter)
+    k0, k1 = int(key[0]) & 0xffffffff, int(key[1]) & 0xffffffff
+    mask = np.uint64(0xffffffff)
+    for _ in range(rounds):
+        pb = np.uint64(_PHILOX_ROUND_B) * c2
+        pa = np.uint64(_PHILOX_ROUND_A) * c0
+        c0, c2 = (pb >> np.uint64(32)) ^ c1 ^ np.uint64(k0), (pa >> np.uint64(32)) ^ c3 ^ np.uint64(k1)
+        c1, c3 = pb & mask, pa & mask
+        k0, k1 = (k0 + _PHILOX_KEY_A) & 0xffffffff, (k1 + _PHILOX_KEY_B) & 0xffffffff
+    return tuple(c.astype(np.uint32) for c in (c0, c1, c2, c3))
+
+
+def triton_rand(seed, offsets):
+    """tl.rand(seed, offsets) for int32 offsets, as float32."""
+    offs = np.asarray(offsets).astype(np.uint32)
+    zero = np.zeros_like(offs)
+    word = philox4x32((offs, zero, zero, zero), (seed & 0xffffffff, (seed >> 32) & 0xffffffff))[0]
+    x = word.view(np.int32).astype(np.int64)
+    x = np.where(x < 0, -x - 1, x)
+    return x.astype(np.float32) * np.float32(4.6566127342e-10)
+
+
+def stochastic_perturb(q, noise, fp8type):
+    """_stochastic_rounding (_division.py:129-150) in fp32: |q| plus noise * (one step of the format at q's
+    exponent), clamped to q's binade (to [2^-9, 2^-6] resp. [2^-16, 2^-14] below the normal range, so zeros
+    become the smallest subnormal), with q's sign.  The caller's saturating RNE cast follows."""
+    fp8type = _dt(fp8type)
+    m_bit = 3 if fp8type == torch.float8_e4m3fn else 2
+    sub_min = np.float32(2.0 ** -9 if fp8type == torch.float8_e4m3fn else 2.0 ** -16)
+    q = np.asarray(q, dtype=np.float32)
+    e = np.maximum((q.view(np.uint32) & np.uint32(0x7F800000)).view(np.float32), sub_min)
+    sub = e == sub_min
+    step = np.where(sub, np.float32(1.0), np.float32(2.0 ** -m_bit)).astype(np.float32)
+    n = (e * np.asarray(noise, dtype=np.float32)) * step          # division by 2^m or 1: exact
+    a = np.abs(q) + n
+    hi = np.where(sub, np.float32(2.0 ** m_bit), np.float32(2.0)).astype(np.float32) * e
+    a = np.minimum(np.maximum(a, e), hi)
+    return np.where(np.signbit(q), -a, a).astype(np.float32)
+
+
+def fp8_division_stochastic(x, fp8type, s, ld=None):
+    """fp8_division(x, QB, fp8type, s, stochastic=True): noise offset of element (m, n) = m * ld + n with
+    ld = x's row stride in elements (seed 0, _division.py:107-110)."""
+    M, N = x.shape
+    ld = N if ld is None else ld
+    q = (x.float() / s.float()).numpy()
+    offs = (np.arange(M, dtype=np.int64)[:, None] * ld + np.arange(N, dtype=np.int64)[None, :]).astype(np.int32)
+    out = stochastic_perturb(q, triton_rand(0, offs), fp8type)
+    return cast_fp8(torch.from_numpy(out), fp8type)

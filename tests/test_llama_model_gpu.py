@@ -8,7 +8,7 @@ from types import SimpleNamespace
 import pytest
 import torch
 
-from coat_b200.fp8_trainer import build_coat_optimizer
+from coat_b200.fp8_trainer import MasterWeights, build_coat_optimizer
 from coat_b200.models import CoatLlamaConfig, CoatLlamaForCausalLM
 from coat_b200.utils._fp8manager import FP8Manager
 
@@ -39,7 +39,8 @@ def test_training_loss_and_gradients_against_unquantised_model():
     ref.eval()   # evaluation mode = the plain torch operators; autograd still works
     ref_loss = ref(input_ids=ids, labels=ids).loss
     ref_loss.backward()
-    assert abs(float(loss) - float(ref_loss)) <= 0.01 * float(ref_loss), (float(loss), float(ref_loss))
+    loss, ref_loss = float(loss.detach()), float(ref_loss.detach())
+    assert abs(loss - ref_loss) <= 0.01 * ref_loss, (loss, ref_loss)
     for n, p in ref.named_parameters():
         t, r = grads[n].double().flatten(), p.grad.double().flatten()
         rel = float((t - r).norm() / r.norm())
@@ -52,17 +53,21 @@ def test_short_training_run_reduces_the_loss():
     model.train()
     args = SimpleNamespace(learning_rate=2e-3, adam_beta1=0.9, adam_beta2=0.95, adam_epsilon=1e-8, weight_decay=0.0)
     decay = [n for n, p in model.named_parameters() if p.dim() == 2]
-    opt = build_coat_optimizer(model, args, decay)
+    masters = MasterWeights(model)   # fp32 masters: the optimizer steps them and writes the bf16 weights itself
+    opt = build_coat_optimizer(masters, args, decay)
+    masters.attach(opt)
     losses = []
     for _ in range(12):
         FP8Manager.is_first_microbatch = True
         loss = model(input_ids=ids, labels=ids).loss
         loss.backward()
+        masters.copy_grads()
         opt.step()
-        opt.zero_grad(set_to_none=True)
-        losses.append(float(loss))
+        losses.append(float(loss.detach()))
     assert all(l == l for l in losses), losses
     assert losses[-1] < 0.6 * losses[0], losses
+    for m, p in zip(masters.masters, masters.model_params):   # the fused bf16 copy is the rounded master
+        assert torch.equal(p.detach(), m.detach().to(torch.bfloat16))
 
 
 def test_stock_checkpoint_names_load():
