@@ -12,6 +12,8 @@ from ._quantize_pertensor_transpose import fp8_quantize_pertensor_transpose  # n
 from ._transpose import fp8_transpose  # noqa: F401
 from .add_bwd import fp8_add_Ifp_Ifp_Ofp_Opt  # noqa: F401
 from .add_fwd import fp8_add_Ifp_Ifp_Ofp_Og16  # noqa: F401
+from .func_layernorm_noparam import fp8_layernorm_noparam_backward, fp8_layernorm_noparam_forward  # noqa: F401
+from .func_layernorm_param import fp8_layernorm_param_backward, fp8_layernorm_param_forward  # noqa: F401
 from .func_rmsnorm import fp8_rmsnorm_backward, fp8_rmsnorm_forward  # noqa: F401
 from .gelu_bwd import fp8_gelu_backward  # noqa: F401
 from .gelu_fwd import fp8_gelu_forward  # noqa: F401

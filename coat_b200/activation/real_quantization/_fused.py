@@ -36,14 +36,14 @@ def _amax_word(device):
 
 
 def _divide(y_bf16, fp8type, amax, want_transposed, flags, scale_dtype=torch.bfloat16, stochastic=False):
-    """Per-tensor quantize of a bf16 intermediate with the scale derived from the amax word."""
+    """Per-tensor quantize of a bf16 (LayerNorm: fp32) intermediate with the scale derived from the amax word."""
     M, N = y_bf16.shape
     dev = y_bf16.device
     q = torch.empty((M, N), dtype=fp8type, device=dev)
     q_t = torch.empty((N, M), dtype=fp8type, device=dev) if want_transposed else None
     s_max = torch.empty((), dtype=scale_dtype, device=dev)
     _call("coat_fp8_division", y_bf16.data_ptr(), q.data_ptr(), None if q_t is None else q_t.data_ptr(), None,
-          s_max.data_ptr(), amax.data_ptr(), M, N, N, _lib.fp8_format(fp8type)[0], _lib.BF16,
+          s_max.data_ptr(), amax.data_ptr(), M, N, N, _lib.fp8_format(fp8type)[0], _lib.float_dtype(y_bf16),
           _lib.float_dtype(scale_dtype), _flags(flags) | (_lib.QUANT_STOCHASTIC if stochastic else 0),
           _lib.stream_ptr(dev))
     return q, s_max, q_t
@@ -210,3 +210,68 @@ def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps):
               dx.data_ptr(), partial.data_ptr(), n_partials, dw.data_ptr(), M, N, QB, _lib.fp8_enum_of(x2),
               _lib.float_dtype(s2), _lib.float_dtype(g2), _lib.float_dtype(w), _lib.stream_ptr(dev))
     return _unflat(dx, bs), dw
+
+
+def _layernorm_forward(x, s_x, w, b, QB, eps, transpose_output_2d, flags):
+    (x2, s2), bs = _flat(x, s_x)
+    M, N = x2.shape
+    dev = x.device
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)   # fp32, as in the reference
+    s_y = torch.empty((M,), dtype=torch.bfloat16, device=dev)
+    mean = torch.empty((M,), dtype=torch.float32, device=dev)
+    rstd = torch.empty((M,), dtype=torch.float32, device=dev)
+    amax = _amax_word(dev)
+    if w is not None:
+        w, b = w.contiguous(), b.contiguous()
+        assert w.dtype == b.dtype and w.numel() == N and b.numel() == N
+    with torch.cuda.device(dev):
+        _call("coat_fp8_layernorm_forward", x2.data_ptr(), s2.data_ptr(), None if w is None else w.data_ptr(),
+              None if b is None else b.data_ptr(), y.data_ptr(), s_y.data_ptr(), mean.data_ptr(), rstd.data_ptr(),
+              amax.data_ptr(), M, N, QB, float(eps), _lib.fp8_enum_of(x2), _lib.float_dtype(s2),
+              _lib.BF16 if w is None else _lib.float_dtype(w), _flags(flags), _lib.stream_ptr(dev))
+        qy, s_max, qy_t = _divide(y, x2.dtype, amax, True, flags)
+    if bs is not None and not transpose_output_2d:
+        qy_t = qy_t.reshape(bs, -1, N)
+    return _unflat(qy, bs), s_max, qy_t, mean, rstd
+
+
+def fp8_layernorm_noparam_forward(x, s_x, QB, eps, transpose_output_2d=False, *, flags=None):
+    qy, s_max, qy_t, mean, rstd = _layernorm_forward(x, s_x, None, None, QB, eps, transpose_output_2d, flags)
+    return qy, s_max, qy_t, (mean, rstd, 8)   # 8 = num_warps of the reference, kept in the context tuple
+
+
+def fp8_layernorm_param_forward(x, s_x, w, b, QB, eps, transpose_output_2d=False, *, flags=None):
+    qy, s_max, qy_t, mean, rstd = _layernorm_forward(x, s_x, w, b, QB, eps, transpose_output_2d, flags)
+    return qy, s_max, qy_t, (w, b, mean, rstd, 8)
+
+
+def _layernorm_backward(x, s_x, g, QB, w, m, v):
+    (x2, s2, g2), bs = _flat(x, s_x, g)
+    M, N = g2.shape
+    dev = x.device
+    dx = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    dw = db = partial = None
+    n_partials = 0
+    if w is not None:
+        w = w.contiguous()
+        dw = torch.empty((N,), dtype=w.dtype, device=dev)
+        db = torch.empty((N,), dtype=w.dtype, device=dev)
+        n_partials = min(M, 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+        partial = torch.empty((n_partials, 2, N), dtype=torch.float32, device=dev)
+    P = lambda t: None if t is None else t.data_ptr()
+    with torch.cuda.device(dev):
+        _call("coat_fp8_layernorm_backward", x2.data_ptr(), s2.data_ptr(), g2.data_ptr(), P(w), m.data_ptr(),
+              v.data_ptr(), dx.data_ptr(), P(partial), n_partials, P(dw), P(db), M, N, QB, _lib.fp8_enum_of(x2),
+              _lib.float_dtype(s2), _lib.float_dtype(g2), _lib.BF16 if w is None else _lib.float_dtype(w),
+              _lib.stream_ptr(dev))
+    return _unflat(dx, bs), dw, db
+
+
+def fp8_layernorm_noparam_backward(x, s_x, g, QB, m, v, num_warps, stochastic=False):
+    if stochastic:   # the reference's branch refers to names that do not exist in its kernel and cannot run
+        raise NotImplementedError("stochastic rounding of the LayerNorm input gradient is not provided")
+    return _layernorm_backward(x, s_x, g, QB, None, m, v)[0]
+
+
+def fp8_layernorm_param_backward(x, s_x, g, QB, w, b, m, v, num_warps):
+    return _layernorm_backward(x, s_x, g, QB, w, m, v)

@@ -335,6 +335,179 @@ rmsnorm_dw_reduce_kernel(const float* __restrict__ partial_dw, int n_partials, v
 }
 
 // =================================================================================================
+// LayerNorm on a 1xQB-quantised input, with or without weight and bias (func_layernorm_noparam.py:54-186,
+// func_layernorm_param.py:54-230; used by the OLMo blocks)
+// =================================================================================================
+// Same row layout and fixed-order reductions as the RMSNorm kernels above.  As in the reference, the mean is
+// taken first and the variance is the mean of squared deviations from it (two sums over registers, not
+// E[x^2] - mean^2), the normalised row leaves in FP32 (the per-tensor division that follows reads fp32), and the
+// per-row scale is stored in bf16.
+template <int FMT, int S, bool IEEE, bool AFFINE>
+__global__ void __launch_bounds__(kNormThreads)
+layernorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, int in_scale_dtype,
+                     const void* __restrict__ w, const void* __restrict__ b, int wb_dtype, float* __restrict__ y,
+                     __nv_bfloat16* __restrict__ s_y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                     unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int QB, float eps, int fp8_fmt_out) {
+    __shared__ float red[kNormThreads / 32];
+    const int64_t row = blockIdx.x;
+    const int64_t segs = N >> 4;
+    float v[S][16];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+            load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), v[k]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum += v[k][i];
+        }
+    }
+    const float mean = qdiv<IEEE>(block_sum(sum, red), (float)N);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[k][i] -= mean;
+                ss += v[k][i] * v[k][i];
+            }
+        }
+    }
+    const float var = qdiv<IEEE>(block_sum(ss, red), (float)N);
+    const float rstd = qdiv<IEEE>(1.0f, sqrt_approx(var + eps));
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        if (c16 < segs) {
+            float wv[16], bv[16];
+            if (AFFINE) {
+                load_float16(w, wb_dtype, c16 * 16, wv);
+                load_float16(b, wb_dtype, c16 * 16, bv);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[k][i] *= rstd;
+                if (AFFINE) v[k][i] = v[k][i] * wv[i] + bv[i];
+                amax = fmaxf(amax, fabsf(v[k][i]));
+            }
+            float4* dst = reinterpret_cast<float4*>(y + row * N + c16 * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                dst[i] = make_float4(v[k][4 * i], v[k][4 * i + 1], v[k][4 * i + 2], v[k][4 * i + 3]);
+        }
+    }
+    amax = block_max(amax, red);
+    if (threadIdx.x == 0) {
+        const float fmax = fp8_fmt_out == COAT_E4M3 ? 448.0f : 57344.0f;
+        s_y[row] = __float2bfloat16_rn(qdiv<IEEE>(amax + kScaleMinThres, fmax));
+        mean_out[row] = mean;
+        rstd_out[row] = rstd;
+        if (amax_bits) atomicMax(amax_bits, __float_as_uint(amax));
+    }
+}
+
+// Backward: dx = (w*dy - (xhat * mean(xhat * w*dy) + mean(w*dy))) * rstd per row; with AFFINE also the per-CTA
+// partial sums of dW = sum dy * xhat and dB = sum dy, written to partial[cta][2][N] and summed in order by
+// rmsnorm_dw_reduce_kernel (deterministic; the reference serialises its partial sums behind a spin lock).
+template <int FMT, int S, bool AFFINE>
+__global__ void __launch_bounds__(kNormThreads)
+layernorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, int in_scale_dtype,
+                     const void* __restrict__ dy, int dy_dtype, const void* __restrict__ w, int w_dtype,
+                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                     __nv_bfloat16* __restrict__ dx, float* __restrict__ partial, int64_t M, int64_t N, int QB) {
+    __shared__ float red[kNormThreads / 32];
+    const int64_t segs = N >> 4;
+    float acc_w[AFFINE ? S : 1][16], acc_b[AFFINE ? S : 1][16], wv[AFFINE ? S : 1][16];
+    if (AFFINE) {
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) { acc_w[k][i] = 0.f; acc_b[k][i] = 0.f; wv[k][i] = 0.f; }
+            if (c16 < segs) load_float16(w, w_dtype, c16 * 16, wv[k]);
+        }
+    }
+    for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+        const float mean = mean_in[row], rstd = rstd_in[row];
+        float xhat[S][16], wdy[S][16];
+        float dot = 0.f, tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+            if (c16 < segs) {
+                load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), xhat[k]);
+                load_float16(dy, dy_dtype, row * N + c16 * 16, wdy[k]);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    xhat[k][i] = (xhat[k][i] - mean) * rstd;
+                    if (AFFINE) {
+                        acc_w[k][i] += wdy[k][i] * xhat[k][i];
+                        acc_b[k][i] += wdy[k][i];
+                        wdy[k][i] *= wv[k][i];
+                    }
+                    dot += xhat[k][i] * wdy[k][i];
+                    tot += wdy[k][i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { xhat[k][i] = 0.f; wdy[k][i] = 0.f; }
+            }
+        }
+        const float c1 = block_sum(dot, red) / (float)N;
+        const float c2 = block_sum(tot, red) / (float)N;
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+            if (c16 < segs) {
+                float o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = (wdy[k][i] - (xhat[k][i] * c1 + c2)) * rstd;
+                store_bf16x16(dx + row * N + c16 * 16, o);
+            }
+        }
+    }
+    if (AFFINE) {
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+            const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+            if (c16 < segs) {
+                float4* dw = reinterpret_cast<float4*>(partial + ((int64_t)blockIdx.x * 2) * N + c16 * 16);
+                float4* db = reinterpret_cast<float4*>(partial + ((int64_t)blockIdx.x * 2 + 1) * N + c16 * 16);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    dw[i] = make_float4(acc_w[k][4 * i], acc_w[k][4 * i + 1], acc_w[k][4 * i + 2], acc_w[k][4 * i + 3]);
+                    db[i] = make_float4(acc_b[k][4 * i], acc_b[k][4 * i + 1], acc_b[k][4 * i + 2], acc_b[k][4 * i + 3]);
+                }
+            }
+        }
+    }
+}
+
+// sums partial[p][which][col] over p (the two-row layout of layernorm_bwd_kernel)
+__global__ void __launch_bounds__(256)
+layernorm_dwdb_reduce_kernel(const float* __restrict__ partial, int n_partials, void* __restrict__ dw,
+                             void* __restrict__ db, int w_dtype, int64_t N) {
+    const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= N) return;
+    float sw = 0.f, sb = 0.f;
+    for (int p = 0; p < n_partials; ++p) {
+        sw += partial[((int64_t)p * 2) * N + col];
+        sb += partial[((int64_t)p * 2 + 1) * N + col];
+    }
+    if (w_dtype == COAT_F32) { reinterpret_cast<float*>(dw)[col] = sw; reinterpret_cast<float*>(db)[col] = sb; }
+    else if (w_dtype == COAT_BF16) {
+        reinterpret_cast<__nv_bfloat16*>(dw)[col] = __float2bfloat16_rn(sw);
+        reinterpret_cast<__nv_bfloat16*>(db)[col] = __float2bfloat16_rn(sb);
+    } else {
+        reinterpret_cast<__half*>(dw)[col] = __float2half_rn(sw);
+        reinterpret_cast<__half*>(db)[col] = __float2half_rn(sb);
+    }
+}
+
+// =================================================================================================
 // host side
 // =================================================================================================
 bool fmt_ok(int f) { return f == COAT_E4M3 || f == COAT_E5M2; }
@@ -500,5 +673,57 @@ extern "C" int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, cons
     else { if (S == 1) COAT_RMSB(COAT_E5M2, 1); else if (S == 2) COAT_RMSB(COAT_E5M2, 2); else COAT_RMSB(COAT_E5M2, 4); }
 #undef COAT_RMSB
     rmsnorm_dw_reduce_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(partial_dw, (int)grid, dw, w_dtype, N);
+    return coat_launch_status();
+}
+
+extern "C" int coat_fp8_layernorm_forward(const uint8_t* x, const void* s_x, const void* w, const void* b, float* y_f32,
+                                          void* s_y_rows_bf16, float* mean, float* rstd, unsigned int* amax_bits,
+                                          int64_t M, int64_t N, int QB, float eps, int fmt, int in_scale_dtype,
+                                          int wb_dtype, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (amax_bits && cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !s_x || !y_f32 || !s_y_rows_bf16 || !mean || !rstd || ((w == nullptr) != (b == nullptr))) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(in_scale_dtype) || (w && !fdt_ok(wb_dtype))) return COAT_E_BADARG;
+    if (N > 16384) return COAT_E_TOOBIG;
+    const int S = N <= 4096 ? 1 : (N <= 8192 ? 2 : 4);
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+    __nv_bfloat16* sy = reinterpret_cast<__nv_bfloat16*>(s_y_rows_bf16);
+#define COAT_LN3(F, SS, I, A) layernorm_fwd_kernel<F, SS, I, A><<<(unsigned)M, kNormThreads, 0, st>>>( \
+        x, s_x, in_scale_dtype, w, b, wb_dtype, y_f32, sy, mean, rstd, amax_bits, M, N, QB, eps, fmt)
+#define COAT_LN2(F, SS) do { if (ieee) { if (w) COAT_LN3(F, SS, true, true); else COAT_LN3(F, SS, true, false); } \
+                             else { if (w) COAT_LN3(F, SS, false, true); else COAT_LN3(F, SS, false, false); } } while (0)
+    if (fmt == COAT_E4M3) { if (S == 1) COAT_LN2(COAT_E4M3, 1); else if (S == 2) COAT_LN2(COAT_E4M3, 2); else COAT_LN2(COAT_E4M3, 4); }
+    else { if (S == 1) COAT_LN2(COAT_E5M2, 1); else if (S == 2) COAT_LN2(COAT_E5M2, 2); else COAT_LN2(COAT_E5M2, 4); }
+#undef COAT_LN2
+#undef COAT_LN3
+    return coat_launch_status();
+}
+
+extern "C" int coat_fp8_layernorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
+                                           const float* mean, const float* rstd, void* dx_bf16, float* partial,
+                                           int n_partials, void* dw, void* db, int64_t M, int64_t N, int QB, int fmt,
+                                           int in_scale_dtype, int dy_dtype, int w_dtype, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !s_x || !dy || !mean || !rstd || !dx_bf16) return COAT_E_BADARG;
+    if (w && (!partial || !dw || !db || n_partials < 1 || !fdt_ok(w_dtype))) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(in_scale_dtype) || !fdt_ok(dy_dtype)) return COAT_E_BADARG;
+    // with weight and bias a thread also carries the dW / dB partial sums of its columns: rows up to 8192
+    if (N > (w ? 8192 : 16384)) return COAT_E_TOOBIG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = N <= 4096 ? 1 : (N <= 8192 ? 2 : 4);
+    const int64_t want = w ? (int64_t)n_partials : (int64_t)4 * coat_sm_count();
+    const unsigned grid = (unsigned)(want < M ? want : M);
+    __nv_bfloat16* dx = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
+#define COAT_LNB3(F, SS, A) layernorm_bwd_kernel<F, SS, A><<<grid, kNormThreads, 0, st>>>( \
+        x, s_x, in_scale_dtype, dy, dy_dtype, w, w_dtype, mean, rstd, dx, partial, M, N, QB)
+#define COAT_LNB2(F, SS) do { if (w) COAT_LNB3(F, SS, true); else COAT_LNB3(F, SS, false); } while (0)
+    if (fmt == COAT_E4M3) { if (S == 1) COAT_LNB2(COAT_E4M3, 1); else if (S == 2) COAT_LNB2(COAT_E4M3, 2); else COAT_LNB3(COAT_E4M3, 4, false); }
+    else { if (S == 1) COAT_LNB2(COAT_E5M2, 1); else if (S == 2) COAT_LNB2(COAT_E5M2, 2); else COAT_LNB3(COAT_E5M2, 4, false); }
+#undef COAT_LNB2
+#undef COAT_LNB3
+    if (w) layernorm_dwdb_reduce_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(partial, (int)grid, dw, db, w_dtype, N);
     return coat_launch_status();
 }

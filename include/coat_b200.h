@@ -288,6 +288,29 @@ int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy,
                               void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
                               int dy_dtype, int w_dtype, void* stream);
 
+/* LayerNorm of a 1xQB-quantised input, without (w == b == NULL) or with weight and bias: per row
+ * mean = sum(x) / N, rstd = 1 / sqrt(sum((x - mean)^2) / N + eps), y = (x - mean) * rstd (* w + b), written in
+ * FP32 as the reference does (its per-tensor division then reads fp32); one bf16 scale per row
+ * ((max|y| + 1e-10) / fp8_max), mean and rstd (fp32) per row, tensor amax.  N <= 16384.  Replaces the kernels
+ * of fp8_layernorm_noparam_forward (func_layernorm_noparam.py:188-245, kernel :54-110) and
+ * fp8_layernorm_param_forward (func_layernorm_param.py:204-263, kernel :54-113). */
+int coat_fp8_layernorm_forward(const uint8_t* x, const void* s_x, const void* w, const void* b, float* y_f32,
+                               void* s_y_rows_bf16, float* mean, float* rstd, unsigned int* amax_bits,
+                               int64_t M, int64_t N, int QB, float eps, int fmt, int in_scale_dtype,
+                               int wb_dtype, int flags, void* stream);
+
+/* LayerNorm backward: dx (bf16) = (w*dy - (xhat * mean(xhat * w*dy) + mean(w*dy))) * rstd with
+ * xhat = (x - mean) * rstd; with w != NULL also dw = sum_rows dy * xhat and db = sum_rows dy (w_dtype), through
+ * caller-provided scratch `partial` of n_partials x 2 x N fp32 (deterministic two-stage sum, no locks), N <= 8192;
+ * with w == NULL partial, dw and db are unused and N <= 16384.  Replaces fp8_layernorm_noparam_backward
+ * (func_layernorm_noparam.py:248-297, kernel :123-185; its stochastic branch names variables that do not
+ * exist there and cannot run, so it has no counterpart here) and fp8_layernorm_param_backward
+ * (func_layernorm_param.py:266-367, kernels :124-200). */
+int coat_fp8_layernorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
+                                const float* mean, const float* rstd, void* dx_bf16, float* partial,
+                                int n_partials, void* dw, void* db, int64_t M, int64_t N, int QB, int fmt,
+                                int in_scale_dtype, int dy_dtype, int w_dtype, void* stream);
+
 /* =========================== FP8 GEMM ==========================================================
  * C[M,N] = (A[M,K] * B[N,K]^T) * (float(*scale_a) * float(*scale_b)) (+ bias[N]), A and B FP8 codes, both with
  * K contiguous (row pitch K bytes, K a multiple of 16, 16-byte aligned bases), formats fmt_a / fmt_b chosen per

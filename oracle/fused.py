@@ -94,3 +94,32 @@ def rmsnorm_backward(x, s_x, g, w, rstd, QB):
     dx = ((wdy - xhat * c1) * rstd.unsqueeze(1)).to(torch.bfloat16)
     dw = (g.float() * xhat).sum(dim=0)
     return dx, dw
+
+
+# ---- LayerNorm (func_layernorm_noparam.py:54-186, func_layernorm_param.py:54-200) ---------------------
+def layernorm_forward_value(x, s_x, w, b, QB, eps):
+    """-> (fp32 value before the per-tensor quantisation, mean, rstd).  w = b = None: no affine part."""
+    v = dequant(x, s_x, QB)
+    n = v.shape[1]
+    mean = v.sum(dim=1, keepdim=True) / n
+    d = v - mean
+    var = (d * d).sum(dim=1, keepdim=True) / n
+    rstd = 1 / torch.sqrt(var + eps)
+    y = d * rstd
+    if w is not None:
+        y = y * w.float() + b.float()
+    return y, mean.flatten(), rstd.flatten()
+
+
+def layernorm_backward(x, s_x, g, w, mean, rstd, QB):
+    """-> (dx bf16, dw, db); dw = db = None without weight."""
+    v = dequant(x, s_x, QB)
+    n = v.shape[1]
+    xhat = (v - mean.unsqueeze(1)) * rstd.unsqueeze(1)
+    wdy = g.float() if w is None else w.float() * g.float()
+    c1 = (xhat * wdy).sum(dim=1, keepdim=True) / n
+    c2 = wdy.sum(dim=1, keepdim=True) / n
+    dx = ((wdy - (xhat * c1 + c2)) * rstd.unsqueeze(1)).to(torch.bfloat16)
+    if w is None:
+        return dx, None, None
+    return dx, (g.float() * xhat).sum(dim=0), g.float().sum(dim=0)

@@ -185,3 +185,67 @@ def test_rmsnorm_forward_backward(N):
     # deterministic: a second run gives the same bits (the reference's lock-ordered sum does not)
     dx2, dw2 = r.fp8_rmsnorm_backward(q.cuda(), s.cuda(), g.cuda(), w.cuda(), rstd, QB, nw)
     assert torch.equal(dw, dw2) and torch.equal(dx, dx2)
+
+
+@pytest.mark.parametrize("N", [512, 4096, 5120])
+@pytest.mark.parametrize("affine", [False, True])
+def test_layernorm_forward_backward(N, affine):
+    """LayerNorm without and with weight/bias against the oracle and against torch's layer_norm autograd on the
+    dequantised input.  mean / rstd: summation order only (5e-7 relative resp. absolute on the mean's scale)."""
+    r = R()
+    M = 64
+    q, s = qinput(M, N, 21)
+    gen = torch.Generator().manual_seed(22)
+    w = (1 + 0.1 * torch.randn(N, generator=gen)).to(torch.bfloat16) if affine else None
+    b = (0.1 * torch.randn(N, generator=gen)).to(torch.bfloat16) if affine else None
+    value, emean, erstd = F.layernorm_forward_value(q, s, w, b, QB, 1e-5)
+    es_max = F.rmsnorm_row_scales(value, "E4M3").max()
+    eq = Q.fp8_division(value, "E4M3", es_max)
+    if affine:
+        qy, s_max, qy_t, (w_ctx, b_ctx, mean, rstd, nw) = r.fp8_layernorm_param_forward(
+            q.cuda(), s.cuda(), w.cuda(), b.cuda(), QB, 1e-5, flags=IEEE)
+    else:
+        qy, s_max, qy_t, (mean, rstd, nw) = r.fp8_layernorm_noparam_forward(q.cuda(), s.cuda(), QB, 1e-5, flags=IEEE)
+    v = F.dequant(q, s, QB)
+    assert torch.allclose(mean.cpu(), emean, rtol=0, atol=5e-7 * float(v.abs().max()))
+    assert torch.allclose(rstd.cpu(), erstd, rtol=1e-6, atol=0)
+    assert torch.equal(qy.view(torch.uint8).t(), qy_t.view(torch.uint8))
+    assert abs(s_max.float().item() - es_max.float().item()) <= es_max.float().item() * 2 ** -7
+    if s_max.float().item() == es_max.float().item():
+        assert frac_equal(qy, eq) >= 0.99 and code_steps(qy, eq).max() <= 1
+    g = grad(M, N, 23)
+    if affine:
+        dx, dw, db = r.fp8_layernorm_param_backward(q.cuda(), s.cuda(), g.cuda(), QB, w.cuda(), b.cuda(), mean, rstd, nw)
+    else:
+        dx = r.fp8_layernorm_noparam_backward(q.cuda(), s.cuda(), g.cuda(), QB, mean, rstd, nw)
+    edx, edw, edb = F.layernorm_backward(q, s, g, w, emean, erstd, QB)
+    assert dx.dtype == torch.bfloat16
+    assert frac_equal(dx, edx) >= 0.97 and (dx.cpu().float() - edx.float()).abs().max() <= 2 ** -7 * edx.float().abs().max()
+    # torch autograd of layer_norm on the dequantised input agrees with the oracle's formulas
+    vv = v.clone().requires_grad_(True)
+    ww = None if w is None else w.float().requires_grad_(True)
+    bb = None if b is None else b.float().requires_grad_(True)
+    torch.nn.functional.layer_norm(vv, (N,), ww, bb, 1e-5).backward(g.float())
+    assert torch.allclose(edx.float(), vv.grad, rtol=2e-2, atol=2e-2 * float(vv.grad.abs().max()))
+    if affine:
+        assert dw.dtype == w.dtype and dw.shape == (N,) and db.shape == (N,)
+        assert torch.allclose(dw.cpu().float(), edw, rtol=1e-2, atol=1e-3 * edw.abs().max().item())
+        assert torch.allclose(db.cpu().float(), edb, rtol=1e-2, atol=1e-3 * edb.abs().max().item())
+        assert torch.allclose(edw, ww.grad, rtol=1e-3, atol=1e-3 * float(ww.grad.abs().max()))
+        assert torch.allclose(edb, bb.grad, rtol=1e-3, atol=1e-3 * float(bb.grad.abs().max()))
+        dx2, dw2, db2 = r.fp8_layernorm_param_backward(q.cuda(), s.cuda(), g.cuda(), QB, w.cuda(), b.cuda(), mean, rstd, nw)
+        assert torch.equal(dw, dw2) and torch.equal(db, db2) and torch.equal(dx, dx2)
+
+
+def test_layernorm_batched_shapes_and_limits():
+    r = R()
+    q, s = qinput(64, 512, 24)
+    q3, s3 = q.view(4, 16, 512).cuda(), s.view(4, 16, -1).cuda()
+    qy, s_max, qy_t, (mean, rstd, nw) = r.fp8_layernorm_noparam_forward(q3, s3, QB, 1e-5)
+    assert qy.shape == (4, 16, 512) and qy_t.shape == (4, 128, 512) and mean.shape == (64,)
+    qy2, _, qy_t2, _ = r.fp8_layernorm_noparam_forward(q3, s3, QB, 1e-5, transpose_output_2d=True)
+    assert qy_t2.shape == (512, 64) and torch.equal(qy_t2.view(torch.uint8), qy.view(torch.uint8).view(64, 512).t())
+    dx = r.fp8_layernorm_noparam_backward(q3, s3, grad(64, 512, 25).view(4, 16, 512).cuda(), QB, mean, rstd, nw)
+    assert dx.shape == (4, 16, 512)
+    with pytest.raises(NotImplementedError):
+        r.fp8_layernorm_noparam_backward(q3, s3, dx, QB, mean, rstd, nw, stochastic=True)
