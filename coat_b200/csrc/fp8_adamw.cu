@@ -646,12 +646,13 @@ constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(
 // and sends them to this GPU's buffer and to every peer's with bulk stores of up to a whole tile.
 constexpr size_t kBcastStageBytes = kTile * kGroup * sizeof(__nv_bfloat16);
 constexpr size_t kTiledSmemBcast = kTiledSmem + kTiledWarps * kBcastStageBytes;
-constexpr int kTiledCtasPerSm = (int)((227 * 1024) / (kTiledSmemBcast + 1024));
+constexpr int tiled_ctas_per_sm(bool bcast) {
+    return (int)((227 * 1024) / ((bcast ? kTiledSmemBcast : kTiledSmem) + 1024));
+}
 static_assert(kTiledSmem % 16 == 0 && kBcastStageBytes % 16 == 0, "bulk copies need 16-byte aligned staging");
-static_assert(kTiledCtasPerSm * (kTiledSmemBcast + 1024) <= 227 * 1024, "tile does not fit the planned occupancy");
 
 template <typename scalar_t, bool MULTI, bool BCAST>
-__global__ void __launch_bounds__(kTiledThreads, kTiledCtasPerSm)
+__global__ void __launch_bounds__(kTiledThreads, tiled_ctas_per_sm(BCAST))
 fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
                               const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
                               AdamwHyper h, unsigned long long* dbg) {
@@ -1095,7 +1096,7 @@ int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_
                 return COAT_E_LAUNCH;
             const int64_t tiles = (total_groups + kTile - 1) / kTile;
             const int64_t ctas_needed = (tiles + kTiledWarps - 1) / kTiledWarps;
-            const int64_t cap = (int64_t)coat_sm_count() * kTiledCtasPerSm;
+            const int64_t cap = (int64_t)coat_sm_count() * tiled_ctas_per_sm(bcast);
             const int grid = (int)(ctas_needed < cap ? ctas_needed : cap);
             kern<<<grid, kTiledThreads, smem, st>>>(single, table, prefix, n_tensors, total_groups, h,
                                                           g_debug_counters);
