@@ -266,6 +266,7 @@ def quantizer_extras(torch, device, peak):
     s_y_t = torch.empty(N, M // 16, dtype=torch.bfloat16, device=device)
     s_max = torch.empty((), dtype=torch.bfloat16, device=device)
     amax = torch.empty(1, dtype=torch.int32, device=device)
+    sync_words = torch.zeros(4, dtype=torch.int32, device=device)   # the one-launch kernel's words: zero in, zero out
     E4M3, BF16 = _lib.E4M3, _lib.BF16
 
     def st():
@@ -280,6 +281,10 @@ def quantizer_extras(torch, device, peak):
         return rc or L.coat_fp8_division(x.data_ptr(), y.data_ptr(), y_t.data_ptr() if transposed else None, None,
                                          s_max.data_ptr(), amax.data_ptr(), M, N, N, E4M3, BF16, BF16, 0, st())
 
+    def pertensor_one_launch(x):
+        return L.coat_fp8_quantize_pertensor(x.data_ptr(), y.data_ptr(), s_y.data_ptr(), s_max.data_ptr(),
+                                             sync_words.data_ptr(), M, N, N, 16, E4M3, BF16, BF16, 0, st())
+
     def qt(x):
         return L.coat_fp8_quantize_transpose(x.data_ptr(), y.data_ptr(), s_y.data_ptr(), y_t.data_ptr(),
                                              s_y_t.data_ptr(), M, N, N, 16, E4M3, BF16, BF16, 0, st())
@@ -293,7 +298,8 @@ def quantizer_extras(torch, device, peak):
 
     cases = {
         "quantize_1x16": (group, 3.125, 1),
-        "quantize_pertensor": (lambda x: pertensor(x, False), 3.125, 2),
+        "quantize_pertensor": (pertensor_one_launch, 3.125, 1),   # what fp8_quantize_pertensor calls
+        "quantize_pertensor_two_launches": (lambda x: pertensor(x, False), 3.125, 2),
         "quantize_pertensor_transpose": (lambda x: pertensor(x, True), 4.0, 2),
         "quantize_transpose_1x16": (qt, 4.25, 1),
         # the two passes of the per-tensor quantizers on their own

@@ -71,12 +71,27 @@ def _flags_stochastic(flags, stochastic):
     return _flags(flags) | (_lib.QUANT_STOCHASTIC if stochastic else 0)
 
 
+_SYNC_WORDS = {}
+
+
+def _sync_words(dev):
+    """Three zero words per (device, stream) for the one-launch per-tensor kernel, which needs them zero on entry
+    and leaves them zero (allocated and cleared once; calls ordered on a stream share them)."""
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), _lib.stream_ptr(dev))
+    words = _SYNC_WORDS.get(key)
+    if words is None:
+        words = _SYNC_WORDS[key] = torch.zeros(4, dtype=torch.int32, device=dev)
+    return key, words
+
+
 def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_transposed, flags, stochastic=False):
-    """Pass 1 (tensor amax, optional group scales) + pass 2 (division by the one scale)."""
+    """Per-tensor quantize.  Without transposed copy (and without stochastic rounding): one cooperative launch
+    that re-reads x from L2.  Otherwise pass 1 (tensor amax, optional group scales) + pass 2 (division by the
+    one scale, straight and / or transposed)."""
     M, N = x.shape
     fmt = _lib.fp8_format(fp8type)[0]
     dev = x.device
-    amax = torch.empty(1, dtype=torch.int32, device=dev)   # 4-byte scratch word, zeroed by pass 1
+    sync = torch.empty(1, dtype=torch.int32, device=dev)   # amax word of the two-call form, zeroed by pass 1
     s_y = torch.empty((M, N // QB), dtype=scale_dtype, device=dev) if want_scales else None
     s_max = torch.empty((), dtype=scale_dtype, device=dev)
     y = torch.empty((M, N), dtype=fp8type, device=dev) if want_straight else None
@@ -84,9 +99,19 @@ def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_tra
     P = lambda t: None if t is None else t.data_ptr()
     with torch.cuda.device(dev):
         st = _lib.stream_ptr(dev)
-        _call("coat_fp8_group_scales_amax", x.data_ptr(), P(s_y), amax.data_ptr(), M, N, x.stride(0), QB, fmt,
+        if want_straight and not want_transposed and not stochastic:
+            key, words = _sync_words(dev)
+            try:
+                _call("coat_fp8_quantize_pertensor", x.data_ptr(), y.data_ptr(), P(s_y), s_max.data_ptr(),
+                      words.data_ptr(), M, N, x.stride(0), QB, fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype),
+                      _flags(flags), st)
+            except Exception:
+                _SYNC_WORDS.pop(key, None)   # do not reuse words a failed call may have left dirty
+                raise
+            return y, s_max, s_y, None
+        _call("coat_fp8_group_scales_amax", x.data_ptr(), P(s_y), sync.data_ptr(), M, N, x.stride(0), QB, fmt,
               _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
-        _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), None, s_max.data_ptr(), amax.data_ptr(), M, N,
+        _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), None, s_max.data_ptr(), sync.data_ptr(), M, N,
               x.stride(0), fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags_stochastic(flags, stochastic),
               st)
     return y, s_max, s_y, y_t

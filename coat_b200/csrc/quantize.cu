@@ -26,6 +26,7 @@
 
 namespace {
 
+__device__ int g_quant_device_status = 0;   // COAT_E_TIMEOUT if a bounded wait (a staging copy, the grid barrier) ran out
 
 // =================================================================================================
 // 1. per-1xQB-group quantize  (_quantize.py:37-118)  and pass 1 of the per-tensor quantize
@@ -187,6 +188,172 @@ division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __
 }
 
 // =================================================================================================
+// 2b. per-tensor quantize in ONE cooperative launch: pass 1 (tensor amax, optional group scales), a grid
+//     barrier, pass 2 (division by the one scale).  Every CTA owns one contiguous slice of the matrix and walks
+//     it forwards in pass 1 and BACKWARDS in pass 2, so that the second read of x finds the lines it touched
+//     last still in the L2 of its own die (two separate kernels re-read x from DRAM: the CTA-to-SM mapping
+//     changes, and a forward re-scan of 67 MB meets an LRU-like L2 at its oldest lines).  Outputs are stored
+//     with the streaming hint so that they do not push x out.
+// =================================================================================================
+#ifndef COAT_PT_FUSED_UNROLL
+#define COAT_PT_FUSED_UNROLL 4
+#endif
+constexpr int kFusedUnroll = COAT_PT_FUSED_UNROLL;
+constexpr int kBarrierLimit = 1 << 20;   // polls of ~0.1-1 us each: about a second, then COAT_E_TIMEOUT
+
+template <typename T> struct RawSeg;      // one 16-element segment as loaded
+template <> struct RawSeg<float> { uint4 q[4]; };
+template <> struct RawSeg<__nv_bfloat16> { uint4 q[2]; };
+template <> struct RawSeg<__half> { uint4 q[2]; };
+
+template <typename T, bool STREAM>
+__device__ __forceinline__ RawSeg<T> load_raw(const T* p) {
+    RawSeg<T> r;
+#pragma unroll
+    for (int i = 0; i < (int)(sizeof(T) * 16 / 16); ++i)
+        r.q[i] = STREAM ? __ldcs(reinterpret_cast<const uint4*>(p) + i) : __ldcg(reinterpret_cast<const uint4*>(p) + i);
+    return r;
+}
+__device__ __forceinline__ float raw_absmax(const RawSeg<__nv_bfloat16>& r) { return seg_absmax<__nv_bfloat16>(r.q[0], r.q[1]); }
+__device__ __forceinline__ float raw_absmax(const RawSeg<__half>& r) { return seg_absmax<__half>(r.q[0], r.q[1]); }
+__device__ __forceinline__ float raw_absmax(const RawSeg<float>& r) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        m = fmaxf(fmaxf(m, fmaxf(fabsf(__uint_as_float(r.q[i].x)), fabsf(__uint_as_float(r.q[i].y)))),
+                  fmaxf(fabsf(__uint_as_float(r.q[i].z)), fabsf(__uint_as_float(r.q[i].w))));
+    return m;
+}
+__device__ __forceinline__ void raw_to_float(const RawSeg<__nv_bfloat16>& r, float (&v)[16]) {
+    const uint32_t w[8] = {r.q[0].x, r.q[0].y, r.q[0].z, r.q[0].w, r.q[1].x, r.q[1].y, r.q[1].z, r.q[1].w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { v[2 * i] = __uint_as_float(w[i] << 16); v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u); }
+}
+__device__ __forceinline__ void raw_to_float(const RawSeg<__half>& r, float (&v)[16]) {
+    const uint32_t w[8] = {r.q[0].x, r.q[0].y, r.q[0].z, r.q[0].w, r.q[1].x, r.q[1].y, r.q[1].z, r.q[1].w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        v[2 * i] = f.x; v[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void raw_to_float(const RawSeg<float>& r, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[4 * i] = __uint_as_float(r.q[i].x); v[4 * i + 1] = __uint_as_float(r.q[i].y);
+        v[4 * i + 2] = __uint_as_float(r.q[i].z); v[4 * i + 3] = __uint_as_float(r.q[i].w);
+    }
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All CTAs of a cooperative launch meet here once.  Bounded: returns false (in every thread of the CTA) if the
+// others have not arrived after kBarrierLimit polls.  `word` receives *payload as of the barrier.
+__device__ __forceinline__ bool grid_barrier_once(unsigned int* counter, const unsigned int* payload, unsigned int* word) {
+    __shared__ unsigned int s_payload;
+    bool ok = true;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();            // this CTA's atomicMax on the payload is ordered before its arrival
+        atomicAdd(counter, 1u);
+        int tries = 0;
+        while (ld_acquire_u32(counter) < gridDim.x) {
+            if (++tries > kBarrierLimit) { ok = false; break; }
+            __nanosleep(100);
+        }
+        s_payload = ld_acquire_u32(payload);
+    }
+    ok = __syncthreads_and(ok);
+    *word = s_payload;
+    return ok;
+}
+
+#ifndef COAT_PT_FUSED_CTAS
+#define COAT_PT_FUSED_CTAS 4
+#endif
+template <typename T, int FMT, bool IEEE>
+__global__ void __launch_bounds__(kStraightThreads, COAT_PT_FUSED_CTAS)
+pertensor_fused_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* __restrict__ s_y, void* __restrict__ s_out,
+                       int scale_dtype, unsigned int* __restrict__ sync /*[0] amax bits, [1] arrivals, [2] departures*/,
+                       int64_t M, int64_t N, int64_t ldx, int QB, int64_t segs_per_cta) {
+    constexpr int kStep = kStraightThreads * kFusedUnroll;
+    const int64_t segs_per_row = N >> 4;
+    const int64_t total = M * segs_per_row;
+    const int lanes = QB >> 4, lane_shift = 31 - __clz(lanes);
+    const int64_t begin = (int64_t)blockIdx.x * segs_per_cta;          // a multiple of 8: groups stay inside a warp
+    const int64_t end = begin + segs_per_cta < total ? begin + segs_per_cta : total;
+    const GroupScale<FMT, IEEE> group_scale;
+    // ---- pass 1: forwards
+    float amax = 0.f;
+    for (int64_t base = begin; base < end; base += kStep) {
+        RawSeg<T> r[kFusedUnroll];
+#pragma unroll
+        for (int k = 0; k < kFusedUnroll; ++k) {
+            const int64_t seg = base + k * kStraightThreads + threadIdx.x;
+            if (seg < end) r[k] = load_raw<T, false>(x + seg_offset(seg, segs_per_row, ldx));
+        }
+#pragma unroll
+        for (int k = 0; k < kFusedUnroll; ++k) {
+            const int64_t seg = base + k * kStraightThreads + threadIdx.x;
+            float m = seg < end ? raw_absmax(r[k]) : 0.f;
+            amax = fmaxf(amax, m);
+            if (s_y) {   // uniform over the launch
+                m = subgroup_max(m, lanes);
+                if (seg < end && (seg & (lanes - 1)) == 0) store_scale(s_y, seg >> lane_shift, scale_dtype, group_scale(m));
+            }
+        }
+    }
+    amax = coat_warp_max(amax);
+    __shared__ float wmax[kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = wmax[0];
+#pragma unroll
+        for (int w = 1; w < kStraightThreads / 32; ++w) m = fmaxf(m, wmax[w]);
+        atomicMax(&sync[0], __float_as_uint(m));   // non-negative floats order like their bits
+    }
+    // ---- everyone's maximum is in
+    unsigned int amax_word;
+    if (!grid_barrier_once(&sync[1], &sync[0], &amax_word)) {
+        if (threadIdx.x == 0) g_quant_device_status = COAT_E_TIMEOUT;
+        return;
+    }
+    const float scale = tensor_scale_from_amax<FMT, IEEE>(&amax_word, scale_dtype);
+    if (s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scale);
+    const ScaleDivider<IEEE> divide(scale);
+    // ---- pass 2: backwards over the same slice
+    const int64_t last = begin + ((end - begin - 1) / kStep) * kStep;
+    for (int64_t base = last; base >= begin; base -= kStep) {
+        RawSeg<T> r[kFusedUnroll];
+#pragma unroll
+        for (int k = 0; k < kFusedUnroll; ++k) {
+            const int64_t seg = base + k * kStraightThreads + threadIdx.x;
+            if (seg < end) r[k] = load_raw<T, true>(x + seg_offset(seg, segs_per_row, ldx));
+        }
+#pragma unroll
+        for (int k = 0; k < kFusedUnroll; ++k) {
+            const int64_t seg = base + k * kStraightThreads + threadIdx.x;
+            if (seg < end) {
+                float v[16], q[16];
+                raw_to_float(r[k], v);
+                divide.apply(v, q);
+                __stcs(reinterpret_cast<uint4*>(y + seg * 16), pack16<FMT>(q));
+            }
+        }
+    }
+    // the three words go back to zero for the next call: the last CTA to leave clears them (everyone has passed
+    // the barrier and has taken its copy of the amax word by then)
+    if (threadIdx.x == 0 && atomicAdd(&sync[2], 1u) == gridDim.x - 1) {
+        sync[0] = 0u; sync[1] = 0u; sync[2] = 0u;
+    }
+}
+
+// =================================================================================================
 // 3. dequantize (_dequantize.py:44-116): y = bf16(code * group scale)
 // =================================================================================================
 template <int FMT>
@@ -345,7 +512,6 @@ transpose_quant_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, uint8_t
 constexpr int kWT = 128;
 constexpr int kTmaStages = 2;
 constexpr int kTmaWaitLimit = 1 << 22;
-__device__ int g_quant_device_status = 0;   // COAT_E_TIMEOUT if a bounded wait on a staging copy ran out
 
 // shared memory: input stages | two transposed tiles and two tiles of transposed scales | barriers
 constexpr size_t kTileTBytes = kWT * 32 * sizeof(uint32_t);
@@ -719,6 +885,44 @@ struct QuantTransposeArgs {
     }
 };
 
+struct PertensorFusedArgs {
+    const void* x; uint8_t* y; void* s_y; void* s_out; int scale_dtype; unsigned int* sync; int64_t M, N, ldx; int QB;
+    cudaStream_t st;
+    template <typename T, int FMT, bool IEEE> int run() const {
+        auto kern = pertensor_fused_kernel<T, FMT, IEEE>;
+        static int ctas_per_sm = 0;   // per instantiation; every B200 of a process gives the same answer
+        if (ctas_per_sm == 0) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kStraightThreads, 0) != cudaSuccess || n < 1)
+                return COAT_E_LAUNCH;
+            ctas_per_sm = n;
+        }
+        constexpr int64_t kStep = (int64_t)kStraightThreads * kFusedUnroll;
+        const int64_t total = M * (N / 16);
+        const int64_t resident = (int64_t)coat_sm_count() * ctas_per_sm;   // every SM gets the same number of CTAs
+        int64_t grid = (total + kStep - 1) / kStep;
+        if (grid > resident) grid = resident;
+        const int64_t segs_per_cta = ((total + grid - 1) / grid + 7) / 8 * 8;   // equal slices, group-aligned
+        grid = (total + segs_per_cta - 1) / segs_per_cta;
+        // cooperative: the launch fails instead of waiting at the barrier if the grid cannot be co-resident
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kStraightThreads);
+        cfg.stream = st;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeCooperative;
+        attr.val.cooperative = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const T*>(x), y, s_y, s_out, scale_dtype, sync, M, N, ldx, QB,
+                               segs_per_cta) != cudaSuccess) {
+            cudaGetLastError();
+            return COAT_E_LAUNCH;
+        }
+        return coat_launch_status();
+    }
+};
+
 int check_2d(const void* x, int64_t M, int64_t N, int64_t ldx, int in_dtype, int QB) {
     if (M < 0 || N < 0 || ldx < N) return COAT_E_BADARG;
     if (!qb_ok(QB) || N % QB != 0) return COAT_E_SHAPE;
@@ -762,6 +966,25 @@ extern "C" int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const 
     if (stochastic && !y) return COAT_E_BADARG;   // the transposed copy is made from y
     DivisionArgs a{x, y, y_t, s_in, s_out, scale_dtype, amax_bits, M, N, ldx, (cudaStream_t)stream, stochastic};
     return dispatch(in_dtype, fmt, flags, a);
+}
+
+extern "C" int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, void* s_y, void* s_out, unsigned int* sync_words,
+                                           int64_t M, int64_t N, int64_t ldx, int QB, int fmt, int in_dtype,
+                                           int scale_dtype, int flags, void* stream) {
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x || !y || !s_out || !sync_words || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (int rc = check_2d(x, M, N, ldx, in_dtype, QB)) return rc;
+    if (!coat_aligned(y, 16) || !coat_aligned(sync_words, 4)) return COAT_E_ALIGN;
+    PertensorFusedArgs a{x, y, s_y, s_out, scale_dtype, sync_words, M, N, ldx, QB, (cudaStream_t)stream};
+    return dispatch(in_dtype, fmt, flags, a);
+}
+
+// Synchronises, returns and clears the quantizers' device status word (COAT_E_TIMEOUT if a bounded wait ran out).
+extern "C" int coat_fp8_quantize_device_status(void) {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_quant_device_status, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    if (v != 0 && cudaMemcpyToSymbol(g_quant_device_status, &zero, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
+    return v;
 }
 
 extern "C" int coat_fp8_quantize_transpose(const void* x, uint8_t* y, void* s_y, uint8_t* y_t, void* s_y_t, int64_t M,

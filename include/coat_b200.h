@@ -183,6 +183,22 @@ int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const void* s_in,
                       const unsigned int* amax_bits, int64_t M, int64_t N, int64_t ldx, int fmt,
                       int in_dtype, int scale_dtype, int flags, void* stream);
 
+/* Per-tensor quantize without transposed copy in ONE cooperative launch: pass 1 (tensor amax, and the 1xQB group
+ * scales if s_y != NULL), a bounded grid barrier, pass 2 (q = x / s with s = round_to_scale_dtype((amax + 1e-10)
+ * / fp8_max), also written to *s_out).  Every CTA re-reads, backwards, the slice it read in pass 1, so the
+ * second read is served from L2.  Same results as coat_fp8_group_scales_amax + coat_fp8_division.   sync_words: 12 bytes of caller scratch that
+ * must be ZERO on entry and are zero again when the kernel ends (so one zero-initialised allocation serves all
+ * calls that are ordered on a stream; two calls that may overlap on the GPU need separate words; after
+ * COAT_E_TIMEOUT zero them again).  Replaces
+ * fp8_quantize_pertensor (_quantize_pertensor.py:106-147: kernel, s_y.max(), fp8_division). */
+int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, void* s_y, void* s_out, unsigned int* sync_words,
+                                int64_t M, int64_t N, int64_t ldx, int QB, int fmt, int in_dtype,
+                                int scale_dtype, int flags, void* stream);
+
+/* Synchronises, returns and clears the quantizers' device status word (COAT_E_TIMEOUT if a bounded wait on a
+ * staging copy or at the grid barrier ran out; never expected). */
+int coat_fp8_quantize_device_status(void);
+
 /* One pass: 1x16 groups along the rows -> (y, s_y[M, N/16]) and 1x16 groups of the transposed matrix
  * (16 consecutive rows of one column) -> (y_t[N, M], s_y_t[N, M/16]).  QB must be 16, M a multiple of 16.
  * Replaces fp8_quantize_transpose (_quantize_transpose.py:176-226, kernel :39-173). */

@@ -246,3 +246,37 @@ def test_block128_rejects_ragged_shapes():
         fp8_quantize_perblock(torch.zeros(128, 192, dtype=torch.bfloat16, device="cuda"), 128, "E4M3")
     with pytest.raises(RuntimeError):
         fp8_quantize_perblock(torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda"), 64, "E4M3")
+
+
+@pytest.mark.parametrize("QB", [16, 32, 128])
+@pytest.mark.parametrize("dtype,scale_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                               (torch.float16, torch.bfloat16)])
+def test_one_launch_pertensor_bit_exact(QB, dtype, scale_dtype):
+    """The cooperative one-launch per-tensor quantize (amax, grid barrier, division re-reading x backwards):
+    group sizes, input and scale dtypes, a row count that leaves the last CTA a ragged slice, a row stride."""
+    r, _ = ops()
+    from coat_b200 import _lib
+    M, N = 1000, 384
+    big = make_x(M, N + 128, seed=QB, dtype=dtype)
+    for x in (big[:, :N].contiguous(), big[:, :N]):          # contiguous, and with a row stride of N + 128
+        q, s_max, s_y = r.fp8_quantize_pertensor(x.cuda() if x.is_contiguous() else big.cuda()[:, :N], QB, "E4M3",
+                                                 scale_dtype=scale_dtype, flags=IEEE)
+        eq, es_max, es_y = Q.fp8_quantize_pertensor(x.contiguous(), QB, "E4M3", scale_dtype=scale_dtype)
+        same_bits(s_y, es_y)
+        same_bits(s_max, es_max)
+        same_bits(q, eq)
+    assert _lib.lib().coat_fp8_quantize_device_status() == 0
+
+
+def test_one_launch_pertensor_many_trips_equals_two_pass():
+    """A matrix large enough that every CTA walks its slice in several trips (persistent grid): the result
+    equals the two-launch path (group scales + amax, then division), 3-D input included."""
+    r, _ = ops()
+    x = make_x(4 * 4096, 2048, seed=77).cuda().view(4, 4096, 2048)
+    q, s_max, s_y = r.fp8_quantize_pertensor(x, 16, "E5M2")
+    q2, s_max2, q_t = r.fp8_quantize_pertensor_transpose(x, 16, "E5M2", transpose_output_2d=True)
+    assert q.shape == (4, 4096, 2048) and s_y.shape == (4, 4096, 128)
+    assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8)) and s_max == s_max2
+    assert torch.equal(q_t.view(torch.uint8), q.view(torch.uint8).view(-1, 2048).t())
+    _, s_ref = r.fp8_quantize(x, 16, "E5M2")
+    assert torch.equal(s_y, s_ref) and s_max == s_y.max()
