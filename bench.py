@@ -511,6 +511,97 @@ def layer_extras(torch, device, iters=5):
     return out
 
 
+def fused_extras(torch, device, peak):
+    """GB/s of the fused quantize-on-save operators, the norms and the optimizer step without expansion, through the
+    python operator API (the calls the decoder layer makes, with its arguments), on BASELINE.json's shapes:
+    8192 tokens x 11008 for the MLP operators, x 4096 for the residual adds and the norms; 4096 x 4096 fp32 for the
+    optimizer.  Device time of 10 calls replayed from one CUDA graph (two input sets rotate; every operator moves
+    more than L2 holds), median of 7 replays after a quarter of a second of warm-up replays.  Algorithmic bytes = compulsory reads + writes of the operator's
+    inputs and outputs (FP8 codes 1 B, 1x16 bf16 scales 0.125 B/elem, bf16 2 B); the implementations move more
+    where the reference's data flow forces a bf16 intermediate before a per-tensor scale is known."""
+    import coat_b200.activation.real_quantization as r
+    from coat_b200.optimizer import qoptim_cuda
+    T, I, H = 8192, 11008, 4096
+    gen = torch.Generator(device=device).manual_seed(4)
+
+    def q16(M, N, scale=1.0):
+        x = (torch.randn(M, N, generator=gen, device=device) * scale).to(torch.bfloat16)
+        return r.fp8_quantize(x, 16, "E4M3")
+
+    def bf(M, N, scale=1.0):
+        return (torch.randn(M, N, generator=gen, device=device) * scale).to(torch.bfloat16)
+
+    sets = []
+    for _ in range(2):
+        d = {"gate": q16(T, I), "up": q16(T, I), "g_i": bf(T, I, 1e-2), "h": q16(T, H), "a": bf(T, H), "b": bf(T, H),
+             "g_h": bf(T, H, 1e-2)}
+        d["w"] = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).to(torch.bfloat16)
+        _, _, _, ctx = r.fp8_rmsnorm_forward(*d["h"], d["w"], 16, 1e-5)
+        d["rstd"] = ctx[1]
+        _, _, _, (d["mean"], d["ln_rstd"], _) = r.fp8_layernorm_noparam_forward(*d["h"], 16, 1e-5)
+        sets.append(d)
+    cases = {
+        # name: (call on one input set, elements, algorithmic bytes per element)
+        "silu_forward": (lambda d: r.fp8_silu_forward(*d["gate"], 16), T * I, 2.25),
+        "mul_forward_pertensor_transposed": (lambda d: r.fp8_mul_forward(*d["gate"], *d["up"], 16, transpose_output_2d=True), T * I, 4.25),
+        "mul_backward_pertensor_transposed": (lambda d: r.fp8_mul_backward(*d["gate"], *d["up"], d["g_i"], 16, "E5M2", output_quantized_transpose=True), T * I, 8.25),
+        "silu_backward_pertensor_transposed": (lambda d: r.fp8_silu_backward(*d["gate"], d["g_i"], 16, "E5M2", output_quantized_transpose=True), T * I, 5.125),
+        "gelu_forward_pertensor_transposed": (lambda d: r.fp8_gelu_forward(*d["gate"], 16, transpose_output_2d=True), T * I, 3.125),
+        "add_fwd_bf16_and_1x16": (lambda d: r.fp8_add_Ifp_Ifp_Ofp_Og16(d["a"], d["b"], torch.float8_e4m3fn, 16), T * H, 7.125),
+        "add_bwd_bf16_and_pertensor": (lambda d: r.fp8_add_Ifp_Ifp_Ofp_Opt(d["a"], d["g_h"], 16, "E5M2"), T * H, 7.125),
+        "rmsnorm_forward_pertensor_transposed": (lambda d: r.fp8_rmsnorm_forward(*d["h"], d["w"], 16, 1e-5, transpose_output_2d=True), T * H, 3.125),
+        "rmsnorm_backward": (lambda d: r.fp8_rmsnorm_backward(*d["h"], d["g_h"], d["w"], d["rstd"], 16, 8), T * H, 5.125),
+        "layernorm_noparam_forward_pertensor_transposed": (lambda d: r.fp8_layernorm_noparam_forward(*d["h"], 16, 1e-5, transpose_output_2d=True), T * H, 3.125),
+        "layernorm_noparam_backward": (lambda d: r.fp8_layernorm_noparam_backward(*d["h"], d["g_h"], 16, d["mean"], d["ln_rstd"], 8), T * H, 5.125),
+    }
+    # the optimizer step WITHOUT expansion (fp8_adamw_cuda_kernel.cu:21-125): 16.125 B per parameter
+    n = 4096 * 4096
+    opt_sets = []
+    for _ in range(4):
+        o = {"p": torch.randn(n, generator=gen, device=device) * 0.02, "g": torch.randn(n, generator=gen, device=device) * 1e-3,
+             "m": torch.zeros(n, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+             "v": torch.zeros(n, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+             "s_m": torch.zeros(n // 128, device=device), "s_v": torch.zeros(n // 128, device=device)}
+        qoptim_cuda.fp8_adamw_step(o["p"], o["g"], o["m"], o["s_m"], o["v"], o["s_v"], 0.9, 0.95, 1e-4, 0.1, 1e-8, 1, 128)
+        opt_sets.append(o)
+    step_no = [2]
+
+    def plain_step(o):
+        qoptim_cuda.fp8_adamw_step(o["p"], o["g"], o["m"], o["s_m"], o["v"], o["s_v"], 0.9, 0.95, 1e-4, 0.1, 1e-8,
+                                   step_no[0], 128)
+
+    out = {}
+    iters = 10
+    for name, (fn, elems, bpe) in list(cases.items()) + [("fp8_adamw_step_no_expansion", (plain_step, n, 16.125))]:
+        data = opt_sets if fn is plain_step else sets
+        for d in data:
+            fn(d)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(iters):
+                fn(data[i % len(data)])
+        t_warm = time.time()
+        while time.time() - t_warm < 0.25:   # warm-up until the clocks have ramped up (a cold process reads 2-3x slow)
+            graph.replay()
+            torch.cuda.synchronize(device)
+        times = []
+        for _ in range(7):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            times.append(e0.elapsed_time(e1) / iters)
+        del graph
+        ms = sorted(times)[len(times) // 2]
+        gbs = elems * bpe / (ms / 1e3) / 1e9
+        out[name] = {"us": ms * 1e3, "GB/s": gbs, "frac_of_measured_hbm": gbs / peak, "algorithmic_bytes_per_elem": bpe}
+        if fn is plain_step:
+            out[name]["params_per_s"] = n / (ms / 1e3)
+    return out
+
+
 def run_kernel_workload(args):
     """`--workload quantizers|gemm`: only those kernels, for profiling captures and quick checks."""
     import torch
@@ -519,6 +610,8 @@ def run_kernel_workload(args):
     peak, kind = measured_peaks()
     if args.workload == "quantizers":
         extras = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak)}
+    elif args.workload == "fused":
+        extras = {"fused_operators_8192_tokens": fused_extras(torch, device, peak)}
     elif args.workload == "blockscaled":
         extras = {"deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
     elif args.workload == "layer":
@@ -660,6 +753,7 @@ def run_gpu_arm(args):
             del opt, grads
             torch.cuda.empty_cache()
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
+                              "fused_operators_8192_tokens": fused_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
                               "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device),
                               "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
@@ -679,7 +773,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "gemm", "layer", "blockscaled"],
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
@@ -688,7 +782,7 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
-    elif args.workload in ("quantizers", "gemm", "layer", "blockscaled"):
+    elif args.workload in ("quantizers", "fused", "gemm", "layer", "blockscaled"):
         run_kernel_workload(args)
     else:
         run_gpu_arm(args)
