@@ -281,8 +281,9 @@ def quantizer_extras(torch, device, peak):
         return rc or L.coat_fp8_division(x.data_ptr(), y.data_ptr(), y_t.data_ptr() if transposed else None, None,
                                          s_max.data_ptr(), amax.data_ptr(), M, N, N, E4M3, BF16, BF16, 0, st())
 
-    def pertensor_one_launch(x):
-        return L.coat_fp8_quantize_pertensor(x.data_ptr(), y.data_ptr(), s_y.data_ptr(), s_max.data_ptr(),
+    def pertensor_one_launch(x, transposed=False):
+        return L.coat_fp8_quantize_pertensor(x.data_ptr(), y.data_ptr(), y_t.data_ptr() if transposed else None,
+                                             None if transposed else s_y.data_ptr(), s_max.data_ptr(),
                                              sync_words.data_ptr(), M, N, N, 16, E4M3, BF16, BF16, 0, st())
 
     def qt(x):
@@ -300,7 +301,8 @@ def quantizer_extras(torch, device, peak):
         "quantize_1x16": (group, 3.125, 1),
         "quantize_pertensor": (pertensor_one_launch, 3.125, 1),   # what fp8_quantize_pertensor calls
         "quantize_pertensor_two_launches": (lambda x: pertensor(x, False), 3.125, 2),
-        "quantize_pertensor_transpose": (lambda x: pertensor(x, True), 4.0, 2),
+        "quantize_pertensor_transpose": (lambda x: pertensor_one_launch(x, True), 4.0, 1),   # what the operator calls
+        "quantize_pertensor_transpose_two_launches": (lambda x: pertensor(x, True), 4.0, 2),
         "quantize_transpose_1x16": (qt, 4.25, 1),
         # the two passes of the per-tensor quantizers on their own
         "pass1_tensor_amax": (amax_pass, 2.0, 1),

@@ -85,9 +85,9 @@ def _sync_words(dev):
 
 
 def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_transposed, flags, stochastic=False):
-    """Per-tensor quantize.  Without transposed copy (and without stochastic rounding): one cooperative launch
-    that re-reads x from L2.  Otherwise pass 1 (tensor amax, optional group scales) + pass 2 (division by the
-    one scale, straight and / or transposed)."""
+    """Per-tensor quantize.  Normally one cooperative launch that re-reads x from L2; with stochastic rounding, or
+    a transposed copy of a matrix whose row count is not a multiple of 16, pass 1 (tensor amax, optional group
+    scales) + pass 2 (division by the one scale, straight and / or transposed)."""
     M, N = x.shape
     fmt = _lib.fp8_format(fp8type)[0]
     dev = x.device
@@ -99,16 +99,18 @@ def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_tra
     P = lambda t: None if t is None else t.data_ptr()
     with torch.cuda.device(dev):
         st = _lib.stream_ptr(dev)
-        if want_straight and not want_transposed and not stochastic:
+        # the transposing form of the one-launch kernel walks 128 x 128 tiles: no group scales, M % 16 == 0
+        one_launch = not stochastic and (not want_transposed or (not want_scales and M % 16 == 0))
+        if one_launch:
             key, words = _sync_words(dev)
             try:
-                _call("coat_fp8_quantize_pertensor", x.data_ptr(), y.data_ptr(), P(s_y), s_max.data_ptr(),
+                _call("coat_fp8_quantize_pertensor", x.data_ptr(), P(y), P(y_t), P(s_y), s_max.data_ptr(),
                       words.data_ptr(), M, N, x.stride(0), QB, fmt, _lib.float_dtype(x), _lib.float_dtype(scale_dtype),
                       _flags(flags), st)
             except Exception:
                 _SYNC_WORDS.pop(key, None)   # do not reuse words a failed call may have left dirty
                 raise
-            return y, s_max, s_y, None
+            return y, s_max, s_y, y_t
         _call("coat_fp8_group_scales_amax", x.data_ptr(), P(s_y), sync.data_ptr(), M, N, x.stride(0), QB, fmt,
               _lib.float_dtype(x), _lib.float_dtype(scale_dtype), _flags(flags), st)
         _call("coat_fp8_division", x.data_ptr(), P(y), P(y_t), None, s_max.data_ptr(), sync.data_ptr(), M, N,

@@ -81,8 +81,11 @@ __device__ __forceinline__ float sigmoid_ref(float x) { return qdiv<IEEE>(1.0f, 
 __device__ __forceinline__ float sqrt_approx(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ float ex2_approx(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 
+#ifndef COAT_FUSED_MIN_CTAS
+#define COAT_FUSED_MIN_CTAS 1
+#endif
 template <int OP, int FMT_IN, int FMT_OUT, bool IEEE>
-__global__ void __launch_bounds__(kStraightThreads)
+__global__ void __launch_bounds__(kStraightThreads, COAT_FUSED_MIN_CTAS)
 fused_elementwise_kernel(FusedArgs a) {
     // one 16-element segment per thread, one trip; every operand has contiguous rows, so no index division
     const int64_t total = a.M * (a.N >> 4);

@@ -576,12 +576,17 @@ struct DivFullDivider {   // the division instruction itself, out of line (scale
     __device__ __forceinline__ float operator()(float x) const { return div_full_outlined(x, s); }
 };
 
-template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT, int C>
+// FUSED (scalar-scale variant only): the kernel also finds the tensor's amax itself.  Launched cooperatively, every
+// CTA first walks its tiles forwards through the same staging ring taking maxima, all CTAs meet at a bounded grid
+// barrier, and the quantising pass then walks the same tiles BACKWARDS, so that its reads are served from L2
+// (see pertensor_fused_kernel).  `sync` = three words, zero on entry, zero again at exit.
+template <typename T, int FMT, bool IEEE, bool GROUPS, bool STRAIGHT, int C, bool FUSED = false>
 __global__ void __launch_bounds__(TmaShape<C>::kThreads, sizeof(T) == 4 ? 1 : 2)
 transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* __restrict__ y,
                            uint8_t* __restrict__ y_t, void* __restrict__ s_y, void* __restrict__ s_y_t,
                            const void* __restrict__ s_in, void* __restrict__ s_out, int scale_dtype,
-                           const unsigned int* __restrict__ amax_bits, int M, int N, int tiles_m, int tiles_n) {
+                           const unsigned int* __restrict__ amax_bits, int M, int N, int tiles_m, int tiles_n,
+                           unsigned int* __restrict__ sync) {
     constexpr int kThreads = TmaShape<C>::kThreads;
     const int n_tiles = tiles_m * tiles_n;
     extern __shared__ unsigned char smem_dyn[];
@@ -598,11 +603,35 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
     const int word = ((m_loc >> 2) + 4 * (n_loc / C)) & 31;
     const GroupScale<FMT, IEEE> group_scale;
     float scalar = 1.f;
-    if (!GROUPS) {
+    if (!GROUPS && !FUSED) {
         scalar = amax_bits ? tensor_scale_from_amax<FMT, IEEE>(amax_bits, scale_dtype) : load_scale(s_in, 0, scale_dtype);
         if (amax_bits && s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scalar);
     }
-    const ScaleDivider<IEEE> by_scalar(scalar);
+    // Uses of the staging ring are numbered k = 0, 1, ...: stage k % kTmaStages, barrier parity (k / kTmaStages) & 1.
+    // Plain: use k is tile blockIdx.x + k * gridDim.x.  FUSED: the first n_mine uses are the amax pass over the
+    // same tiles, the next n_mine the quantising pass over them in reverse order.
+    const int n_mine = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int k_end = FUSED ? 2 * n_mine : n_mine;
+    auto tile_of = [&](int use) -> int {
+        const int i = (FUSED && use >= n_mine) ? 2 * n_mine - 1 - use : use;
+        return (int)blockIdx.x + i * (int)gridDim.x;
+    };
+    auto issue = [&](int use) {   // thread 0 only
+        const int st = use % kTmaStages;
+        int tm, tn;
+        tile_coords(tile_of(use), tiles_n, tm, tn);
+        coat_tma::mbar_expect_tx(&full[st], kStageBytes);
+        coat_tma::load_2d(base + (size_t)st * kStageBytes, &map_x, tn * kWT, tm * kWT, &full[st]);
+    };
+    auto give_up = [&](int use) {   // a wait ran out (never expected): leave only after our copies in flight have landed
+        if (threadIdx.x == 0) {
+            g_quant_device_status = COAT_E_TIMEOUT;
+            for (int q = 0; q < kTmaStages; ++q)
+                if (use + q < k_end)
+                    coat_tma::mbar_wait(&full[(use + q) % kTmaStages], (uint32_t)((use + q) / kTmaStages) & 1u, kTmaWaitLimit);
+        }
+        __syncthreads();
+    };
     if (threadIdx.x == 0) {
 #pragma unroll
         for (int s = 0; s < kTmaStages; ++s) coat_tma::mbar_init(&full[s], 1);
@@ -611,18 +640,41 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
     __syncthreads();
     if (threadIdx.x == 0) {
 #pragma unroll
-        for (int s = 0; s < kTmaStages; ++s) {
-            const int t = blockIdx.x + s * gridDim.x;
-            if (t < n_tiles) {
-                int tm, tn;
-                tile_coords(t, tiles_n, tm, tn);
-                coat_tma::mbar_expect_tx(&full[s], kStageBytes);
-                coat_tma::load_2d(base + (size_t)s * kStageBytes, &map_x, tn * kWT, tm * kWT, &full[s]);
-            }
-        }
+        for (int s = 0; s < kTmaStages; ++s)
+            if (s < k_end) issue(s);
     }
     int k = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++k) {
+    if (FUSED) {
+        float amax = 0.f;
+        for (; k < n_mine; ++k) {
+            const int s = k % kTmaStages;
+            const T* stage = reinterpret_cast<const T*>(base + (size_t)s * kStageBytes);
+            const bool arrived = coat_tma::mbar_wait(&full[s], (uint32_t)(k / kTmaStages) & 1u, kTmaWaitLimit);
+            float v[4][C];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) load_cols<T, C>(stage + (m_loc + j) * kWT + n_loc, v[j]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) amax = fmaxf(amax, absmax_cols<C>(v[j]));   // parts outside the matrix are zero-filled
+            if (!__syncthreads_and(arrived)) { give_up(k); return; }
+            if (threadIdx.x == 0 && k + kTmaStages < k_end) issue(k + kTmaStages);
+        }
+        amax = coat_warp_max(amax);
+        float* wmax = reinterpret_cast<float*>(after_stages);   // the transposed-tile buffer is free until the second pass
+        if (lane == 0) wmax[warp] = amax;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = wmax[0];
+            for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, wmax[w]);
+            atomicMax(&sync[0], __float_as_uint(m));
+        }
+        unsigned int amax_word;
+        if (!grid_barrier_once(&sync[1], &sync[0], &amax_word)) { give_up(k); return; }
+        scalar = tensor_scale_from_amax<FMT, IEEE>(&amax_word, scale_dtype);
+        if (s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scalar);
+    }
+    const ScaleDivider<IEEE> by_scalar(scalar);
+    for (; k < k_end; ++k) {
+        const int t = tile_of(k);
         const int s = k % kTmaStages;
         const T* stage = reinterpret_cast<const T*>(base + (size_t)s * kStageBytes);
         uint32_t (*tile_t)[32] = reinterpret_cast<uint32_t (*)[32]>(after_stages + (size_t)(k & 1) * kTileTBytes);
@@ -684,27 +736,8 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
         // transposed codes and scales are complete.  Tile k+1 writes the other pair of buffers, and nobody
         // passes the barrier of tile k+1 (after which this pair is written again) before every thread has
         // finished the readout of tile k below.
-        if (!__syncthreads_and(arrived)) {
-            if (threadIdx.x == 0) {   // never expected; leave only after our copies in flight have landed (bounded)
-                g_quant_device_status = COAT_E_TIMEOUT;
-                for (int q = 0; q < kTmaStages; ++q) {
-                    const int kq = k + q;
-                    if (blockIdx.x + (int64_t)kq * gridDim.x < n_tiles)
-                        coat_tma::mbar_wait(&full[kq % kTmaStages], (uint32_t)(kq / kTmaStages) & 1u, kTmaWaitLimit);
-                }
-            }
-            __syncthreads();
-            return;
-        }
-        if (threadIdx.x == 0) {
-            const int64_t t2 = (int64_t)t + (int64_t)kTmaStages * gridDim.x;
-            if (t2 < n_tiles) {
-                int tm2, tn2;
-                tile_coords((int)t2, tiles_n, tm2, tn2);
-                coat_tma::mbar_expect_tx(&full[s], kStageBytes);
-                coat_tma::load_2d(base + (size_t)s * kStageBytes, &map_x, tn2 * kWT, tm2 * kWT, &full[s]);
-            }
-        }
+        if (!__syncthreads_and(arrived)) { give_up(k); return; }
+        if (threadIdx.x == 0 && k + kTmaStages < k_end) issue(k + kTmaStages);
         // transposed rows leave in 16-byte pieces: one warp instruction = 4 rows x 128 contiguous bytes
 #pragma unroll
         for (int it = 0; it < kWT * 8 / kThreads; ++it) {
@@ -739,6 +772,9 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
             }
         }
     }
+    if (FUSED && threadIdx.x == 0 && atomicAdd(&sync[2], 1u) == gridDim.x - 1) {   // last CTA out clears the words
+        sync[0] = 0u; sync[1] = 0u; sync[2] = 0u;
+    }
 }
 
 inline bool tma_tiles_fit(int64_t M, int64_t N) {   // tile counts and coordinates are 32-bit in the kernel
@@ -761,7 +797,47 @@ int launch_transpose_tma(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, voi
     const int64_t cap = (int64_t)coat_sm_count() * (sizeof(T) == 4 ? 1 : 2);
     const int grid = (int)(n_tiles < cap ? n_tiles : cap);
     kern<<<grid, TmaShape<C>::kThreads, smem, st>>>(map, y, y_t, s_y, s_y_t, s_in, s_out, scale_dtype, amax, (int)M, (int)N,
-                                           (int)tiles_m, (int)tiles_n);
+                                           (int)tiles_m, (int)tiles_n, nullptr);
+    return coat_launch_status();
+}
+
+// The FUSED form of the scalar-scale variant (amax pass + barrier + quantising pass), launched cooperatively.
+template <typename T, int FMT, bool IEEE, bool STRAIGHT>
+int launch_transpose_tma_fused(const void* x, uint8_t* y, uint8_t* y_t, void* s_out, int scale_dtype, unsigned int* sync,
+                               int64_t M, int64_t N, int64_t ldx, cudaStream_t st) {
+    CUtensorMap map;
+    if (!coat_tma::make_map_2d(&map, x, (int)sizeof(T), M, N, ldx * (int64_t)sizeof(T), kWT, kWT)) return COAT_E_DEVICE;
+    constexpr int C = 8;
+    auto kern = transpose_quant_tma_kernel<T, FMT, IEEE, false, STRAIGHT, C, true>;
+    constexpr size_t smem = tma_quant_smem<T>();
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return COAT_E_LAUNCH;
+    static int ctas_per_sm = 0;   // per instantiation
+    if (ctas_per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, TmaShape<C>::kThreads, smem) != cudaSuccess || n < 1)
+            return COAT_E_LAUNCH;
+        ctas_per_sm = n;
+    }
+    const int64_t tiles_n = (N + kWT - 1) / kWT, tiles_m = (M + kWT - 1) / kWT;
+    const int64_t n_tiles = tiles_n * tiles_m;
+    const int64_t cap = (int64_t)coat_sm_count() * ctas_per_sm;
+    const int grid = (int)(n_tiles < cap ? n_tiles : cap);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(TmaShape<C>::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeCooperative;
+    attr.val.cooperative = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, map, y, y_t, (void*)nullptr, (void*)nullptr, (const void*)nullptr, s_out, scale_dtype,
+                           (const unsigned int*)nullptr, (int)M, (int)N, (int)tiles_m, (int)tiles_n, sync) != cudaSuccess) {
+        cudaGetLastError();
+        return COAT_E_LAUNCH;
+    }
     return coat_launch_status();
 }
 
@@ -886,9 +962,13 @@ struct QuantTransposeArgs {
 };
 
 struct PertensorFusedArgs {
-    const void* x; uint8_t* y; void* s_y; void* s_out; int scale_dtype; unsigned int* sync; int64_t M, N, ldx; int QB;
-    cudaStream_t st;
+    const void* x; uint8_t* y; uint8_t* y_t; void* s_y; void* s_out; int scale_dtype; unsigned int* sync; int64_t M, N, ldx;
+    int QB; cudaStream_t st;
     template <typename T, int FMT, bool IEEE> int run() const {
+        if (y_t) {
+            if (y) return launch_transpose_tma_fused<T, FMT, IEEE, true>(x, y, y_t, s_out, scale_dtype, sync, M, N, ldx, st);
+            return launch_transpose_tma_fused<T, FMT, IEEE, false>(x, nullptr, y_t, s_out, scale_dtype, sync, M, N, ldx, st);
+        }
         auto kern = pertensor_fused_kernel<T, FMT, IEEE>;
         static int ctas_per_sm = 0;   // per instantiation; every B200 of a process gives the same answer
         if (ctas_per_sm == 0) {
@@ -968,14 +1048,19 @@ extern "C" int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const 
     return dispatch(in_dtype, fmt, flags, a);
 }
 
-extern "C" int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, void* s_y, void* s_out, unsigned int* sync_words,
-                                           int64_t M, int64_t N, int64_t ldx, int QB, int fmt, int in_dtype,
-                                           int scale_dtype, int flags, void* stream) {
+extern "C" int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, void* s_out,
+                                           unsigned int* sync_words, int64_t M, int64_t N, int64_t ldx, int QB, int fmt,
+                                           int in_dtype, int scale_dtype, int flags, void* stream) {
     if (M == 0 || N == 0) return COAT_OK;
-    if (!x || !y || !s_out || !sync_words || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
+    if (!x || (!y && !y_t) || !s_out || !sync_words || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
     if (int rc = check_2d(x, M, N, ldx, in_dtype, QB)) return rc;
-    if (!coat_aligned(y, 16) || !coat_aligned(sync_words, 4)) return COAT_E_ALIGN;
-    PertensorFusedArgs a{x, y, s_y, s_out, scale_dtype, sync_words, M, N, ldx, QB, (cudaStream_t)stream};
+    if ((y && !coat_aligned(y, 16)) || !coat_aligned(sync_words, 4)) return COAT_E_ALIGN;
+    if (y_t) {   // the tile kernel: no group scales, 16-row granularity, 16-byte aligned transposed rows
+        if (s_y) return COAT_E_BADARG;
+        if (M % 16 != 0 || !tma_tiles_fit(M, N)) return COAT_E_SHAPE;
+        if (!coat_aligned(y_t, 16)) return COAT_E_ALIGN;
+    }
+    PertensorFusedArgs a{x, y, y_t, s_y, s_out, scale_dtype, sync_words, M, N, ldx, QB, (cudaStream_t)stream};
     return dispatch(in_dtype, fmt, flags, a);
 }
 

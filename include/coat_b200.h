@@ -183,17 +183,19 @@ int coat_fp8_division(const void* x, uint8_t* y, uint8_t* y_t, const void* s_in,
                       const unsigned int* amax_bits, int64_t M, int64_t N, int64_t ldx, int fmt,
                       int in_dtype, int scale_dtype, int flags, void* stream);
 
-/* Per-tensor quantize without transposed copy in ONE cooperative launch: pass 1 (tensor amax, and the 1xQB group
- * scales if s_y != NULL), a bounded grid barrier, pass 2 (q = x / s with s = round_to_scale_dtype((amax + 1e-10)
- * / fp8_max), also written to *s_out).  Every CTA re-reads, backwards, the slice it read in pass 1, so the
- * second read is served from L2.  Same results as coat_fp8_group_scales_amax + coat_fp8_division.   sync_words: 12 bytes of caller scratch that
+/* Per-tensor quantize in ONE cooperative launch: pass 1 (tensor amax, and the 1xQB group scales if s_y != NULL), a
+ * bounded grid barrier, pass 2 (q = x / s with s = round_to_scale_dtype((amax + 1e-10) / fp8_max), also written
+ * to *s_out).  Every CTA re-reads, backwards, the part of x it read in pass 1, so the second read is served from
+ * L2.  Same results as coat_fp8_group_scales_amax + coat_fp8_division.  Outputs: y (M x N) and / or the
+ * transposed copy y_t (N x M); with y_t the tile kernel runs: s_y must be NULL, M a multiple of 16
+ * (COAT_E_SHAPE otherwise: use the two calls), y_t 16-byte aligned.  sync_words: 12 bytes of caller scratch that
  * must be ZERO on entry and are zero again when the kernel ends (so one zero-initialised allocation serves all
  * calls that are ordered on a stream; two calls that may overlap on the GPU need separate words; after
- * COAT_E_TIMEOUT zero them again).  Replaces
- * fp8_quantize_pertensor (_quantize_pertensor.py:106-147: kernel, s_y.max(), fp8_division). */
-int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, void* s_y, void* s_out, unsigned int* sync_words,
-                                int64_t M, int64_t N, int64_t ldx, int QB, int fmt, int in_dtype,
-                                int scale_dtype, int flags, void* stream);
+ * COAT_E_TIMEOUT zero them again).  Replaces fp8_quantize_pertensor (_quantize_pertensor.py:106-147: kernel,
+ * s_y.max(), fp8_division) and fp8_quantize_pertensor_transpose (_quantize_pertensor_transpose.py:106-150). */
+int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, uint8_t* y_t, void* s_y, void* s_out,
+                                unsigned int* sync_words, int64_t M, int64_t N, int64_t ldx, int QB, int fmt,
+                                int in_dtype, int scale_dtype, int flags, void* stream);
 
 /* Synchronises, returns and clears the quantizers' device status word (COAT_E_TIMEOUT if a bounded wait on a
  * staging copy or at the grid barrier ran out; never expected). */

@@ -280,3 +280,18 @@ def test_one_launch_pertensor_many_trips_equals_two_pass():
     assert torch.equal(q_t.view(torch.uint8), q.view(torch.uint8).view(-1, 2048).t())
     _, s_ref = r.fp8_quantize(x, 16, "E5M2")
     assert torch.equal(s_y, s_ref) and s_max == s_y.max()
+    # both one-launch kernels against the plain division kernel with the same scale
+    q3, _ = r.fp8_division(x, 16, "E5M2", s_max)
+    assert torch.equal(q.view(torch.uint8), q3.view(torch.uint8))
+    from coat_b200 import _lib
+    assert _lib.lib().coat_fp8_quantize_device_status() == 0
+
+
+def test_one_launch_transposed_falls_back_for_ragged_row_counts():
+    """M not a multiple of 16: the operator takes the two-call path; results agree with the straight one-launch kernel."""
+    r, _ = ops()
+    x = make_x(1004, 256, seed=78).cuda()
+    q, s_max, q_t = r.fp8_quantize_pertensor_transpose(x, 16, "E4M3")
+    q2, s_max2, _ = r.fp8_quantize_pertensor(x, 16, "E4M3")
+    assert s_max == s_max2 and torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
+    assert torch.equal(q_t.view(torch.uint8), q.view(torch.uint8).t())
