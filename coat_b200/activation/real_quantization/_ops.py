@@ -78,6 +78,9 @@ def _sync_words(dev):
     """Three zero words per (device, stream) for the one-launch per-tensor kernel, which needs them zero on entry
     and leaves them zero (allocated and cleared once; calls ordered on a stream share them)."""
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), _lib.stream_ptr(dev))
+    if torch.cuda.is_current_stream_capturing():
+        # memory allocated during a capture belongs to the graph's pool: use fresh words (their memset is captured)
+        return None, torch.zeros(4, dtype=torch.int32, device=dev)
     words = _SYNC_WORDS.get(key)
     if words is None:
         words = _SYNC_WORDS[key] = torch.zeros(4, dtype=torch.int32, device=dev)

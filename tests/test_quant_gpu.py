@@ -295,3 +295,25 @@ def test_one_launch_transposed_falls_back_for_ragged_row_counts():
     q2, s_max2, _ = r.fp8_quantize_pertensor(x, 16, "E4M3")
     assert s_max == s_max2 and torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
     assert torch.equal(q_t.view(torch.uint8), q.view(torch.uint8).t())
+
+
+def test_one_launch_pertensor_replays_from_a_cuda_graph():
+    """Cooperative launches inside a captured graph: replays (with the input changed in place between them) equal
+    the eager results, so the sync words really are zero again after every launch."""
+    r, _ = ops()
+    x = make_x(2048, 1024, seed=90).cuda()
+    x2 = make_x(2048, 1024, seed=91).cuda()
+    buf = x.clone()
+    r.fp8_quantize_pertensor(buf, 16, "E4M3")               # first use outside the capture
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        q, s_max, s_y = r.fp8_quantize_pertensor(buf, 16, "E4M3")
+        qa, sa, qa_t = r.fp8_quantize_pertensor_transpose(buf, 16, "E4M3")
+    for src in (x, x2, x):
+        buf.copy_(src)
+        g.replay()
+        torch.cuda.synchronize()
+        eq, es_max, es_y = r.fp8_quantize_pertensor(src, 16, "E4M3")
+        assert torch.equal(q.view(torch.uint8), eq.view(torch.uint8)) and s_max == es_max and torch.equal(s_y, es_y)
+        assert torch.equal(qa.view(torch.uint8), eq.view(torch.uint8)) and sa == es_max
+        assert torch.equal(qa_t.view(torch.uint8), eq.view(torch.uint8).t())
