@@ -646,8 +646,12 @@ constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(
 // and sends them to this GPU's buffer and to every peer's with bulk stores of up to a whole tile.
 constexpr size_t kBcastStageBytes = kTile * kGroup * sizeof(__nv_bfloat16);
 constexpr size_t kTiledSmemBcast = kTiledSmem + kTiledWarps * kBcastStageBytes;
+// A table launch also keeps the tensors' group offsets in (static) shared memory: the binary search that maps a
+// tile to its tensor is a chain of dependent loads, 9 deep for the 291 tensors of Llama-2-7B, and from L2 that
+// chain was most of the latency of a tile's set-up.
+constexpr int kPrefixCap = 512;
 constexpr int tiled_ctas_per_sm(bool bcast) {
-    return (int)((227 * 1024) / ((bcast ? kTiledSmemBcast : kTiledSmem) + 1024));
+    return (int)((227 * 1024) / ((bcast ? kTiledSmemBcast : kTiledSmem) + 1024 + kPrefixCap * sizeof(int)));
 }
 static_assert(kTiledSmem % 16 == 0 && kBcastStageBytes % 16 == 0, "bulk copies need 16-byte aligned staging");
 
@@ -676,6 +680,12 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     const int64_t n_tiles = (total_groups + kTile - 1) / kTile;
     const int64_t warps_total = (int64_t)gridDim.x * kTiledWarps;
     unsigned long long n_fast = 0, n_exact = 0, n_cand_total = 0, n_pend_total = 0;
+    __shared__ int s_prefix[MULTI ? kPrefixCap : 1];
+    const bool prefix_cached = MULTI && n_tensors <= kPrefixCap && total_groups < (1ll << 31);
+    if (prefix_cached) {
+        for (int i = threadIdx.x; i < n_tensors; i += kTiledThreads) s_prefix[i] = (int)group_prefix[i];
+        __syncthreads();
+    }
     if (lane == 0) {
         w.n_pend = 0;
         w.n_cand = 0;
@@ -701,12 +711,20 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             int64_t group = gi;
             if (MULTI) {
                 int lo = 0, hi = n_tensors - 1;
-                while (lo < hi) {
-                    int mid = (lo + hi + 1) >> 1;
-                    if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                if (prefix_cached) {
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if ((int64_t)s_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                    }
+                    group = gi - s_prefix[lo];
+                } else {
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                    }
+                    group = gi - group_prefix[lo];
                 }
                 ti = lo;
-                group = gi - group_prefix[ti];
             }
             const TensorDesc& t = MULTI ? table[ti] : single;
             const int64_t e0 = group * kGroup;
