@@ -157,7 +157,7 @@ def test_add_bit_exact():
     same(qy2, eq)
 
 
-@pytest.mark.parametrize("N", [512, 4096, 5120])
+@pytest.mark.parametrize("N", [512, 2048, 4096, 5120, 10240])   # 1, 2 and 4 segments per thread
 def test_rmsnorm_forward_backward(N):
     r = R()
     M = 64
