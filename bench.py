@@ -374,6 +374,15 @@ def gemm_extras(torch, device, iters=10):
                                    M, N, K, _lib.fp8_enum_of(a), _lib.fp8_enum_of(bm), _lib.BF16, _lib.BF16, 0, 16, 0,
                                    _lib.stream_ptr(device))
         calls[name] = (call, M, N, K)
+    # the forward GEMM with the fused 1x16 quantising epilogue (FP8 codes + bf16 group scales instead of bf16), as the
+    # gate / up projections of the decoder layer use it
+    cq = torch.empty(T, I, dtype=torch.uint8, device=device)
+    sq = torch.empty(T, I // 16, dtype=torch.bfloat16, device=device)
+
+    def call_q():
+        return L.coat_fp8_gemm(x.data_ptr(), w.data_ptr(), cq.data_ptr(), sq.data_ptr(), s.data_ptr(), s.data_ptr(), None,
+                               T, I, H, _lib.E4M3, _lib.E4M3, _lib.BF16, _lib.BF16, 1, 16, 0, _lib.stream_ptr(device))
+    calls["forward_e4m3xe4m3_quantising_epilogue_1x16"] = (call_q, T, I, H)
 
     def timed(call, n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -208,34 +208,70 @@ __device__ __forceinline__ float ld_scalar(const void* p, int dtype, int64_t i =
     return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// 32 consecutive columns of one row -> FP8 codes and 32 / QBV group scales.  A lane owns its row, so its stores
+// never coalesce with its neighbours': the 32 codes leave as two 16-byte stores and the scales as one store
+// (4-byte stores of the codes, eight per lane, made the quantising GEMM a third slower than the bf16 one).
 template <int FMT_C, int QBV>
 __device__ __forceinline__ void quantize_groups(const GemmEpilogue& e, int row, int col0, const float (&v)[32]) {
     const float fmax = CoatFp8Max<FMT_C>::value;
     uint8_t* dst = reinterpret_cast<uint8_t*>(e.c) + (int64_t)row * e.N + col0;
     __nv_bfloat16* sdst = reinterpret_cast<__nv_bfloat16*>(e.scale_c) + (int64_t)row * (e.N / QBV) + col0 / QBV;
+    uint32_t words[8];
+    uint16_t sbits[32 / QBV];
+    const bool whole = col0 + 32 <= e.N;
 #pragma unroll
     for (int gi = 0; gi < 32 / QBV; ++gi) {
-        if (col0 + gi * QBV >= e.N) break;
-        float amax = 0.f;
+        float m[QBV / 2];   // balanced tree: the epilogue warp has nobody to hide a 16-deep chain behind
 #pragma unroll
-        for (int i = 0; i < QBV; ++i) amax = fmaxf(amax, fabsf(v[gi * QBV + i]));
+        for (int i = 0; i < QBV / 2; ++i) m[i] = fmaxf(fabsf(v[gi * QBV + 2 * i]), fabsf(v[gi * QBV + 2 * i + 1]));
+#pragma unroll
+        for (int wdt = QBV / 4; wdt >= 1; wdt >>= 1)
+#pragma unroll
+            for (int i = 0; i < wdt; ++i) m[i] = fmaxf(m[2 * i], m[2 * i + 1]);
+        const float amax = m[0];
         const float num = amax + 1e-10f;
         const float scale = e.ieee_div ? __fdiv_rn(num, fmax) : coat_div_full(num, fmax);
-        sdst[gi] = __float2bfloat16_rn(scale);
+        sbits[gi] = coat_float_to_bf16_bits(scale);
         // div.full.f32(x, s) == x * rcp.approx.f32(s) bit for bit while |s| is in [2^-120, 2^120]
         float r;
         asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(scale));
         const bool fast = !e.ieee_div && scale >= 7.5231638e-37f && scale <= 1.3292280e36f;
+        // one branch per group, not a three-way select per element: with the select the compiler evaluated the
+        // reciprocal product, div.full and the IEEE division for every element (22 instructions per element, and the
+        // epilogue warps, one per scheduler and latency-bound, took longer per tile than the tensor cores)
+        if (fast) {
 #pragma unroll
-        for (int i = 0; i < QBV; i += 4) {
-            float q[4];
+            for (int i = 0; i < QBV; i += 4)
+                words[(gi * QBV + i) >> 2] = coat_float4_to_fp8x4<FMT_C>(v[gi * QBV + i] * r, v[gi * QBV + i + 1] * r,
+                                                                         v[gi * QBV + i + 2] * r, v[gi * QBV + i + 3] * r);
+        } else if (e.ieee_div) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float x = v[gi * QBV + i + j];
-                q[j] = fast ? x * r : (e.ieee_div ? __fdiv_rn(x, scale) : coat_div_full(x, scale));
-            }
-            *reinterpret_cast<uint32_t*>(dst + gi * QBV + i) = coat_float4_to_fp8x4<FMT_C>(q[0], q[1], q[2], q[3]);
+            for (int i = 0; i < QBV; i += 4)
+                words[(gi * QBV + i) >> 2] = coat_float4_to_fp8x4<FMT_C>(
+                    __fdiv_rn(v[gi * QBV + i], scale), __fdiv_rn(v[gi * QBV + i + 1], scale),
+                    __fdiv_rn(v[gi * QBV + i + 2], scale), __fdiv_rn(v[gi * QBV + i + 3], scale));
+        } else {
+#pragma unroll
+            for (int i = 0; i < QBV; i += 4)
+                words[(gi * QBV + i) >> 2] = coat_float4_to_fp8x4<FMT_C>(
+                    coat_div_full(v[gi * QBV + i], scale), coat_div_full(v[gi * QBV + i + 1], scale),
+                    coat_div_full(v[gi * QBV + i + 2], scale), coat_div_full(v[gi * QBV + i + 3], scale));
         }
+    }
+    if (whole && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(words[0], words[1], words[2], words[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (col0 + 4 * k < e.N) *reinterpret_cast<uint32_t*>(dst + 4 * k) = words[k];   // N is a multiple of QBV >= 16
+    }
+    if (QBV == 16 && whole && (reinterpret_cast<uintptr_t>(sdst) & 3) == 0) {
+        *reinterpret_cast<uint32_t*>(sdst) = (uint32_t)sbits[0] | ((uint32_t)sbits[32 / QBV - 1] << 16);
+    } else {
+#pragma unroll
+        for (int gi = 0; gi < 32 / QBV; ++gi)
+            if (col0 + gi * QBV < e.N) sdst[gi] = __ushort_as_bfloat16(sbits[gi]);
     }
 }
 
@@ -255,7 +291,9 @@ __device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, int row, i
             for (int i = 0; i < 4; ++i)
                 reinterpret_cast<uint4*>(dst)[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
         } else {
-            for (int i = 0; i < 32 && col0 + i < e.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)   // static indices: a run-time index would put v[] in local memory
+                if (col0 + i < e.N) dst[i] = __float2bfloat16_rn(v[i]);
         }
     } else {
         // fused 1xQB quantisation (linear.py:139-164): QB is 16 or 32, N a multiple of QB, so groups never
