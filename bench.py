@@ -458,7 +458,8 @@ def layer_extras(torch, device, iters=5):
     """Forward + backward of ONE Llama-2-7B decoder layer (hidden 4096, 32 heads, MLP 11008) on 4 x 2048 tokens
     through the FP8 layer of this package, and, beside it, the same layer in plain bf16 torch (cuBLAS GEMMs,
     SDPA, eager elementwise ops) as a yardstick on the same GPU.  Weights N(0, 0.02), input N(0, 1) * 0.5,
-    upstream gradient N(0, 1e-2); memory-efficient weight mode, first micro-batch (weight scales recomputed)."""
+    upstream gradient N(0, 1e-2); memory-efficient weight mode, first micro-batch (weight scales recomputed); gradients
+    are reset to None before every step in both legs (no accumulation adds)."""
     import torch.nn.functional as F
     from coat_b200.activation.real_quantization.func_quantize import Coat_quantize_bgn, Coat_quantize_end
     from coat_b200.models.coat_llama import CoatLlamaConfig, CoatLlamaDecoderLayer
@@ -480,6 +481,9 @@ def layer_extras(torch, device, iters=5):
     FP8Manager.is_first_microbatch = True
 
     def fp8_step():
+        for p in layer.parameters():   # zero_grad(set_to_none=True), as a training step does: autograd then stores each
+            p.grad = None              # gradient instead of adding it to last step's (a host-side reset, no kernel)
+        x.grad = None
         (h, qh, sh), = layer(*bgn(x))
         end(h, qh, sh).backward(up)
 
@@ -500,6 +504,9 @@ def layer_extras(torch, device, iters=5):
         h = rms(y, w["post_attention_layernorm.weight"])
         y = y + F.linear(F.silu(F.linear(h, w["MLPResidual.gate_proj.weight"])) *
                          F.linear(h, w["MLPResidual.up_proj.weight"]), w["MLPResidual.down_proj.weight"])
+        for t in w.values():
+            t.grad = None
+        x.grad = None
         y.backward(up)
 
     from coat_b200.models.coat_llama import llama_rotary_embeddings
