@@ -196,9 +196,14 @@ def fp8_rmsnorm_forward(x, s_x, w, QB, eps, transpose_output_2d=False, *, flags=
     return _unflat(qy, bs), s_max, qy_t, (w, rstd, num_warps)
 
 
-def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps):
+def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps, *, more_g=()):
+    """`more_g`: up to two further bf16 addends of the upstream gradient; the result is that of calling with
+    `g + more_g[0] + more_g[1]` (bf16 sums, left to right), without the add kernels."""
+    more = [t.reshape(-1, t.shape[-1]) for t in more_g]
+    assert len(more) <= 2 and all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in more)
     (x2, s2, g2), bs = _flat(x, s_x, g)
     M, N = g2.shape
+    assert all(t.shape == g2.shape for t in more) and (not more or g2.dtype == torch.bfloat16)
     dev = x.device
     dx = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     dw = torch.empty((N,), dtype=w.dtype, device=dev)
@@ -206,9 +211,11 @@ def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps):
     partial = torch.empty((n_partials, N), dtype=torch.float32, device=dev)
     w = w.contiguous()
     with torch.cuda.device(dev):
-        _call("coat_fp8_rmsnorm_backward", x2.data_ptr(), s2.data_ptr(), g2.data_ptr(), w.data_ptr(), v.data_ptr(),
-              dx.data_ptr(), partial.data_ptr(), n_partials, dw.data_ptr(), M, N, QB, _lib.fp8_enum_of(x2),
-              _lib.float_dtype(s2), _lib.float_dtype(g2), _lib.float_dtype(w), _lib.stream_ptr(dev))
+        _call("coat_fp8_rmsnorm_backward", x2.data_ptr(), s2.data_ptr(), g2.data_ptr(),
+              more[0].data_ptr() if len(more) > 0 else None, more[1].data_ptr() if len(more) > 1 else None,
+              w.data_ptr(), v.data_ptr(), dx.data_ptr(), partial.data_ptr(), n_partials, dw.data_ptr(), M, N, QB,
+              _lib.fp8_enum_of(x2), _lib.float_dtype(s2), _lib.float_dtype(g2), _lib.float_dtype(w),
+              _lib.stream_ptr(dev))
     return _unflat(dx, bs), dw
 
 

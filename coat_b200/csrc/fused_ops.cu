@@ -284,7 +284,8 @@ rmsnorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
 template <int FMT, int S>
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, int in_scale_dtype,
-                   const void* __restrict__ dy, int dy_dtype, const void* __restrict__ w, int w_dtype,
+                   const void* __restrict__ dy, const void* __restrict__ dy2, const void* __restrict__ dy3,
+                   int dy_dtype, const void* __restrict__ w, int w_dtype,
                    const float* __restrict__ rstd_in, __nv_bfloat16* __restrict__ dx, float* __restrict__ partial_dw,
                    int64_t M, int64_t N, int QB) {
     __shared__ float red[kNormThreads / 32];
@@ -310,6 +311,20 @@ rmsnorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
                 float g[16];
                 load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), xhat[k]);
                 load_float16(dy, dy_dtype, row * N + c16 * 16, g);
+                // optional further addends of the upstream gradient (the dgrads of the projections that read the
+                // norm's output), added left to right with a rounding to bf16 after each sum, as torch's bf16
+                // `a + b + c` gives it: saves the separate add kernels and their round trips through memory
+                if (dy2) {
+                    float t[16];
+                    load_float16(dy2, dy_dtype, row * N + c16 * 16, t);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) g[i] = __bfloat162float(__float2bfloat16_rn(g[i] + t[i]));
+                    if (dy3) {
+                        load_float16(dy3, dy_dtype, row * N + c16 * 16, t);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) g[i] = __bfloat162float(__float2bfloat16_rn(g[i] + t[i]));
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     xhat[k][i] *= rstd;
@@ -702,20 +717,23 @@ extern "C" int coat_fp8_rmsnorm_forward(const uint8_t* x, const void* s_x, const
     return coat_launch_status();
 }
 
-extern "C" int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
-                                         const float* rstd, void* dx_bf16, float* partial_dw, int n_partials,
+extern "C" int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* dy2,
+                                         const void* dy3, const void* w, const float* rstd, void* dx_bf16,
+                                         float* partial_dw, int n_partials,
                                          void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
                                          int dy_dtype, int w_dtype, void* stream) {
     if (int rc = check_shape(M, N, QB)) return rc;
     if (M == 0 || N == 0) return COAT_OK;
     if (!x || !s_x || !dy || !w || !rstd || !dx_bf16 || !partial_dw || !dw || n_partials < 1) return COAT_E_BADARG;
+    if (dy3 && !dy2) return COAT_E_BADARG;
+    if ((dy2 || dy3) && dy_dtype != COAT_BF16) return COAT_E_BADARG;   // the sums are rounded to bf16
     if (!fmt_ok(fmt) || !fdt_ok(in_scale_dtype) || !fdt_ok(dy_dtype) || !fdt_ok(w_dtype)) return COAT_E_BADARG;
     if (N > 16384) return COAT_E_TOOBIG;
     cudaStream_t st = (cudaStream_t)stream;
     const int S = N <= 4096 ? 1 : (N <= 8192 ? 2 : 4);
     const unsigned grid = (unsigned)(n_partials < M ? n_partials : M);
     __nv_bfloat16* dx = reinterpret_cast<__nv_bfloat16*>(dx_bf16);
-#define COAT_RMSB(F, SS) rmsnorm_bwd_kernel<F, SS><<<grid, kNormThreads, 0, st>>>(x, s_x, in_scale_dtype, dy, dy_dtype, w, w_dtype, rstd, dx, partial_dw, M, N, QB)
+#define COAT_RMSB(F, SS) rmsnorm_bwd_kernel<F, SS><<<grid, kNormThreads, 0, st>>>(x, s_x, in_scale_dtype, dy, dy2, dy3, dy_dtype, w, w_dtype, rstd, dx, partial_dw, M, N, QB)
     if (fmt == COAT_E4M3) { if (S == 1) COAT_RMSB(COAT_E4M3, 1); else if (S == 2) COAT_RMSB(COAT_E4M3, 2); else COAT_RMSB(COAT_E4M3, 4); }
     else { if (S == 1) COAT_RMSB(COAT_E5M2, 1); else if (S == 2) COAT_RMSB(COAT_E5M2, 2); else COAT_RMSB(COAT_E5M2, 4); }
 #undef COAT_RMSB

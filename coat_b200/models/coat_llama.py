@@ -151,9 +151,10 @@ class _CoatLlamaBeforeAttentionResidual(torch.autograd.Function):
             dx, dw = fp8_linear_backward(ln_x_t, ln_s, qg, qg_s, qg_t, w_t, s_w, group_size)
             dgrads.append(dx)
             wgrads.append(dw)
-        fc1_g = dgrads[0] + dgrads[1] + dgrads[2]
-
-        in_g, rms_weight_grad = fp8_rmsnorm_backward(in_x, in_s, fc1_g, rms_weight, rstd, group_size, num_warps)
+        # the three input gradients are summed (in bf16, left to right, as `a + b + c` would) inside the norm's
+        # backward kernel
+        in_g, rms_weight_grad = fp8_rmsnorm_backward(in_x, in_s, dgrads[0], rms_weight, rstd, group_size, num_warps,
+                                                     more_g=(dgrads[1], dgrads[2]))
         # residual gradient + norm gradient, and the per-tensor FP8 copy for the block below
         re_g, (in_g, in_sg, in_sg_g16) = fp8_add_Ifp_Ifp_Ofp_Opt(fp_grad, in_g, group_size, fwobits["babit"],
                                                                  stochastic=False)
@@ -337,9 +338,8 @@ class _CoatLlamaMLPResidual(torch.autograd.Function):
                                                   group_size)
         fc2_g, weight2_grad = fp8_linear_backward(ln_x_t, ln_s, mul_g2, mul_gs2, mul_g2_t, w_up_t, weight2_s,
                                                   group_size)
-        fc_g = fc1_g + fc2_g
-
-        in_g, rms_weight_grad = fp8_rmsnorm_backward(in_x, in_s, fc_g, rms_weight, rstd, group_size, num_warps)
+        in_g, rms_weight_grad = fp8_rmsnorm_backward(in_x, in_s, fc1_g, rms_weight, rstd, group_size, num_warps,
+                                                     more_g=(fc2_g,))   # fc1_g + fc2_g, summed in the kernel
         re_g, (in_g, in_sg, in_sg_g16) = fp8_add_Ifp_Ifp_Ofp_Opt(fp_grad, in_g, group_size, fwobits["babit"],
                                                                  stochastic=False)
         return (re_g, _as_e4m3(in_g), in_sg_g16,

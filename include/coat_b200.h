@@ -300,9 +300,12 @@ int coat_fp8_rmsnorm_forward(const uint8_t* x, const void* s_x, const void* w, v
 
 /* RMSNorm backward: dx (bf16) and dw (w_dtype).  partial_dw is caller-provided scratch of n_partials x N
  * fp32 (n_partials CTAs each sum their rows in registers, a second kernel adds the partials in order:
- * deterministic, no locks).  Replaces fp8_rmsnorm_backward (func_rmsnorm.py:281-335, kernels :121-220). */
-int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* w,
-                              const float* rstd, void* dx_bf16, float* partial_dw, int n_partials,
+ * deterministic, no locks).  dy2 / dy3 (NULL, or bf16 like dy): further addends of the upstream gradient; the
+ * kernel uses bf16(bf16(dy + dy2) + dy3), what a bf16 `dy + dy2 + dy3` in torch gives, without the add kernels
+ * (an extension: the reference sums the projections' input gradients in torch before this call).  Replaces
+ * fp8_rmsnorm_backward (func_rmsnorm.py:281-335, kernels :121-220). */
+int coat_fp8_rmsnorm_backward(const uint8_t* x, const void* s_x, const void* dy, const void* dy2, const void* dy3,
+                              const void* w, const float* rstd, void* dx_bf16, float* partial_dw, int n_partials,
                               void* dw, int64_t M, int64_t N, int QB, int fmt, int in_scale_dtype,
                               int dy_dtype, int w_dtype, void* stream);
 

@@ -249,3 +249,20 @@ def test_layernorm_batched_shapes_and_limits():
     assert dx.shape == (4, 16, 512)
     with pytest.raises(NotImplementedError):
         r.fp8_layernorm_noparam_backward(q3, s3, dx, QB, mean, rstd, nw, stochastic=True)
+
+
+@pytest.mark.parametrize("n_more", [1, 2])
+def test_rmsnorm_backward_sums_its_upstream_gradients(n_more):
+    """`more_g`: the kernel's bf16 left-to-right sum of the addends gives the bits of passing torch's `a + b (+ c)`."""
+    import torch
+    r = R()
+    M, N = 96, 4096
+    q, s = qinput(M, N, 41)
+    w = (1 + 0.1 * torch.randn(N, generator=torch.Generator().manual_seed(42))).to(torch.bfloat16).cuda()
+    q, s = q.cuda(), s.cuda()
+    _, _, _, (_, rstd, nw) = r.fp8_rmsnorm_forward(q, s, w, QB, 1e-5)
+    gs = [grad(M, N, 43 + i).cuda() for i in range(1 + n_more)]
+    total = gs[0] + gs[1] if n_more == 1 else gs[0] + gs[1] + gs[2]
+    dx_ref, dw_ref = r.fp8_rmsnorm_backward(q, s, total, w, rstd, QB, nw)
+    dx, dw = r.fp8_rmsnorm_backward(q, s, gs[0], w, rstd, QB, nw, more_g=tuple(gs[1:]))
+    assert torch.equal(dx, dx_ref) and torch.equal(dw, dw_ref)
