@@ -146,6 +146,34 @@ def fp8_mul_backward(x1, s_x1, x2, s_x2, g, QB, fp8type, stochastic=False, outpu
     return _unflat(y1, bs), (_unflat(qy2, bs), s_max, qy2_t)
 
 
+def fp8_mul_silu_backward(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type, *, flags=None):
+    """Backward of `silu(gate) * up` in one elementwise kernel (no counterpart in the reference, which calls
+    fp8_mul_backward and fp8_silu_backward one after the other; same bits):
+        (d_up, s, d_up_t), (d_gate, s, d_gate_t) = per-tensor FP8 codes, scale and transposed codes of the
+        gradients towards the up and the gate projections, i.e.
+        fp8_mul_backward(silu_x, silu_s, up_x, up_s, g, QB, fp8type, output_quantized_transpose=True)[1] and
+        fp8_silu_backward(gate_x, gate_s, <first output of that call>, QB, fp8type, output_quantized_transpose=True)."""
+    (a, sa, b, sb, c, sc, g2), bs = _flat(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g)
+    assert a.shape == b.shape == c.shape == g2.shape and sa.shape == sb.shape == sc.shape
+    assert a.dtype == b.dtype == c.dtype and sa.dtype == sb.dtype == sc.dtype
+    M, N = a.shape
+    fp8type = _fp8_dtype(fp8type)
+    dev = a.device
+    y_up = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    y_gate = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    s_up = torch.empty(sa.shape, dtype=torch.bfloat16, device=dev)
+    s_gate = torch.empty(sa.shape, dtype=torch.bfloat16, device=dev)
+    amax_up, amax_gate = _amax_word(dev), _amax_word(dev)
+    with torch.cuda.device(dev):
+        _call("coat_fp8_mul_silu_backward", a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(), c.data_ptr(),
+              sc.data_ptr(), g2.data_ptr(), y_up.data_ptr(), s_up.data_ptr(), amax_up.data_ptr(), y_gate.data_ptr(),
+              s_gate.data_ptr(), amax_gate.data_ptr(), M, N, QB, _lib.fp8_enum_of(a), _lib.float_dtype(sa),
+              _lib.float_dtype(g2), _lib.fp8_format(fp8type)[0], _flags(flags), _lib.stream_ptr(dev))
+        q_up, smax_up, q_up_t = _divide(y_up, fp8type, amax_up, True, flags)
+        q_gate, smax_gate, q_gate_t = _divide(y_gate, fp8type, amax_gate, True, flags)
+    return (_unflat(q_up, bs), smax_up, q_up_t), (_unflat(q_gate, bs), smax_gate, q_gate_t)
+
+
 def _add(x1, x2, QB, fp8type, want_codes, want_amax, flags):
     (a, b), bs = _flat(x1, x2)
     assert a.shape == b.shape

@@ -177,6 +177,77 @@ fused_elementwise_kernel(FusedArgs a) {
 }
 
 // =================================================================================================
+// Gated-MLP backward in one kernel: fp8_mul_backward (mul_bwd.py:117-152) followed by fp8_silu_backward
+// (silu_bwd.py:112-137) without the bf16 round trip of the gradient that goes from one to the other.
+//   d_up   = g * silu_x                                  -> bf16 + 1xQB scales + tensor amax  (mul backward's 2nd output)
+//   t      = bf16(g * up)                                 (mul backward's 1st output, as the reference rounds it)
+//   d_gate = (sig + gate * sig * (1 - sig)) * t           -> bf16 + 1xQB scales + tensor amax  (silu backward)
+// Same bits as the two kernels one after the other; the memory-latency-bound product and the instruction-bound
+// sigmoid overlap inside one kernel, and 4 bytes per element less go through memory.
+// =================================================================================================
+struct MulSiluBwdArgs {
+    const uint8_t* x_silu; const void* s_silu;
+    const uint8_t* x_up; const void* s_up;
+    const uint8_t* x_gate; const void* s_gate;
+    const void* g; int g_dtype;
+    __nv_bfloat16* y_up; void* sy_up; unsigned int* amax_up;
+    __nv_bfloat16* y_gate; void* sy_gate; unsigned int* amax_gate;
+    int64_t M, N;
+    int QB, in_scale_dtype;
+    float fp8_max;
+};
+
+template <int FMT_IN, bool IEEE>
+__global__ void __launch_bounds__(kStraightThreads)
+mul_silu_backward_kernel(MulSiluBwdArgs a) {
+    const int64_t total = a.M * (a.N >> 4);
+    const int lanes = a.QB >> 4;
+    const int lane_shift = 31 - __clz(lanes);
+    const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
+    const bool live = seg < total;
+    const int64_t off = seg * 16;
+    float d_up[16], d_gate[16];
+    float amax_up = 0.f, amax_gate = 0.f;
+    if (live) {
+        float xs[16], xu[16], xg[16], gr[16];
+        load_dequant16<FMT_IN>(a.x_silu, a.s_silu, a.in_scale_dtype, seg, lane_shift, xs);
+        load_dequant16<FMT_IN>(a.x_up, a.s_up, a.in_scale_dtype, seg, lane_shift, xu);
+        load_dequant16<FMT_IN>(a.x_gate, a.s_gate, a.in_scale_dtype, seg, lane_shift, xg);
+        load_float16(a.g, a.g_dtype, off, gr);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            d_up[i] = gr[i] * xs[i];
+            const float t = __bfloat162float(__float2bfloat16_rn(gr[i] * xu[i]));
+            const float sg = sigmoid_ref<IEEE>(xg[i]);
+            d_gate[i] = __fmaf_rn(xg[i] * sg, 1.0f - sg, sg) * t;
+            amax_up = fmaxf(amax_up, fabsf(d_up[i]));
+            amax_gate = fmaxf(amax_gate, fabsf(d_gate[i]));
+        }
+    }
+    amax_up = subgroup_max(amax_up, lanes);     // whole warps: the grid is rounded up to blocks of 256 threads
+    amax_gate = subgroup_max(amax_gate, lanes);
+    if (live) {
+        store_bf16x16(a.y_up + off, d_up);
+        store_bf16x16(a.y_gate + off, d_gate);
+        if ((seg & (lanes - 1)) == 0) {
+            store_scale(a.sy_up, seg >> lane_shift, COAT_BF16, qdiv<IEEE>(amax_up + kScaleMinThres, a.fp8_max));
+            store_scale(a.sy_gate, seg >> lane_shift, COAT_BF16, qdiv<IEEE>(amax_gate + kScaleMinThres, a.fp8_max));
+        }
+    }
+    amax_up = coat_warp_max(live ? amax_up : 0.f);
+    amax_gate = coat_warp_max(live ? amax_gate : 0.f);
+    __shared__ float wmax[2][kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) { wmax[0][threadIdx.x >> 5] = amax_up; wmax[1][threadIdx.x >> 5] = amax_gate; }
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        const int which = threadIdx.x >> 5, l = threadIdx.x & 31;
+        float m = l < kStraightThreads / 32 ? wmax[which][l] : 0.f;
+        m = coat_warp_max(m);
+        if (l == 0) atomicMax(which ? a.amax_gate : a.amax_up, __float_as_uint(m));
+    }
+}
+
+// =================================================================================================
 // RMSNorm on a 1xQB-quantised input (func_rmsnorm.py:54-111 forward, :121-220 backward)
 // =================================================================================================
 // One CTA of 256 threads per row; thread t owns the 16-element segments t, t+256, ... (S of them, in
@@ -675,6 +746,36 @@ extern "C" int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const 
     a.y1_bf16 = reinterpret_cast<__nv_bfloat16*>(y1_bf16); a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y2_bf16);
     a.s_y = s_y2; a.amax_bits = amax_bits;
     return launch_fused<OP_MUL_BWD>(a, fmt_in, fmt_out, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_mul_silu_backward(const uint8_t* x_silu, const void* s_silu, const uint8_t* x_up, const void* s_up,
+                                          const uint8_t* x_gate, const void* s_gate, const void* g, void* y_up_bf16,
+                                          void* s_y_up, unsigned int* amax_up, void* y_gate_bf16, void* s_y_gate,
+                                          unsigned int* amax_gate, int64_t M, int64_t N, int QB, int fmt_in,
+                                          int in_scale_dtype, int g_dtype, int fmt_out, int flags, void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!amax_up || !amax_gate) return COAT_E_BADARG;
+    if (cudaMemsetAsync(amax_up, 0, sizeof(unsigned int), st) != cudaSuccess ||
+        cudaMemsetAsync(amax_gate, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x_silu || !s_silu || !x_up || !s_up || !x_gate || !s_gate || !g || !y_up_bf16 || !s_y_up || !y_gate_bf16 ||
+        !s_y_gate) return COAT_E_BADARG;
+    if (!fmt_ok(fmt_in) || !fmt_ok(fmt_out) || !fdt_ok(in_scale_dtype) || !fdt_ok(g_dtype)) return COAT_E_BADARG;
+    MulSiluBwdArgs a = {x_silu, s_silu, x_up, s_up, x_gate, s_gate, g, g_dtype,
+                        reinterpret_cast<__nv_bfloat16*>(y_up_bf16), s_y_up, amax_up,
+                        reinterpret_cast<__nv_bfloat16*>(y_gate_bf16), s_y_gate, amax_gate, M, N, QB, in_scale_dtype,
+                        fmt_max(fmt_out)};
+    const unsigned grid = straight_grid(M * (N / 16));
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+    if (fmt_in == COAT_E4M3) {
+        if (ieee) mul_silu_backward_kernel<COAT_E4M3, true><<<grid, kStraightThreads, 0, st>>>(a);
+        else mul_silu_backward_kernel<COAT_E4M3, false><<<grid, kStraightThreads, 0, st>>>(a);
+    } else {
+        if (ieee) mul_silu_backward_kernel<COAT_E5M2, true><<<grid, kStraightThreads, 0, st>>>(a);
+        else mul_silu_backward_kernel<COAT_E5M2, false><<<grid, kStraightThreads, 0, st>>>(a);
+    }
+    return coat_launch_status();
 }
 
 extern "C" int coat_fp8_add(const void* x1, const void* x2, void* y_bf16, uint8_t* y_q, void* s_y,

@@ -33,13 +33,12 @@ from ..activation.real_quantization import (
     fp8_division_transpose,
     fp8_linear_backward,
     fp8_linear_forward,
-    fp8_mul_backward,
+    fp8_mul_silu_backward,
     fp8_mul_forward,
     fp8_quantize_pertensor,
     fp8_quantize_pertensor_transpose,
     fp8_rmsnorm_backward,
     fp8_rmsnorm_forward,
-    fp8_silu_backward,
     fp8_silu_forward,
     fp8_transpose,
 )
@@ -326,10 +325,9 @@ class _CoatLlamaMLPResidual(torch.autograd.Function):
         del out_g, out_g_t, w_down_t
 
         # Mul (1: towards the gate branch, bf16; 2: towards up, per-tensor FP8 + transposed copy), then SiLU
-        mul_g1, (mul_g2, mul_gs2, mul_g2_t) = fp8_mul_backward(silu_x, silu_s, up_x, up_s, fc3_g, group_size,
-                                                               fwobits["babit"], output_quantized_transpose=True)
-        silu_g, silu_gs, silu_g_t = fp8_silu_backward(gate_x, gate_s, mul_g1, group_size, fwobits["babit"],
-                                                      output_quantized_transpose=True)
+        # (one kernel for fp8_mul_backward followed by fp8_silu_backward: same bits, no bf16 round trip between them)
+        (mul_g2, mul_gs2, mul_g2_t), (silu_g, silu_gs, silu_g_t) = fp8_mul_silu_backward(
+            silu_x, silu_s, up_x, up_s, gate_x, gate_s, fc3_g, group_size, fwobits["babit"])
 
         # gate / up projections
         w_gate_t = _backward_weight_t(saved_gate, weight1_s, qargs, fwobits["fwbit"])

@@ -283,6 +283,18 @@ int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const uint8_t* x2
                           int64_t M, int64_t N, int QB, int fmt_in, int in_scale_dtype, int g_dtype,
                           int fmt_out, int flags, void* stream);
 
+/* Backward of the gated MLP product in one kernel: coat_fp8_mul_backward(x_silu, x_up, g) followed by
+ * coat_fp8_act_backward(SiLU, x_gate, its first output) without the bf16 round trip between them:
+ *   y_up   = bf16(g * x_silu),                              group scales s_y_up (bf16),   tensor amax *amax_up
+ *   y_gate = bf16(silu'(x_gate) * bf16(g * x_up)),          group scales s_y_gate (bf16), tensor amax *amax_gate
+ * bit for bit what the two calls give (an extension: the reference calls fp8_mul_backward, mul_bwd.py:221-315, and
+ * fp8_silu_backward, silu_bwd.py:170-238, one after the other).  fmt_out: the FP8 format the scales are for. */
+int coat_fp8_mul_silu_backward(const uint8_t* x_silu, const void* s_silu, const uint8_t* x_up, const void* s_up,
+                               const uint8_t* x_gate, const void* s_gate, const void* g, void* y_up_bf16,
+                               void* s_y_up, unsigned int* amax_up, void* y_gate_bf16, void* s_y_gate,
+                               unsigned int* amax_gate, int64_t M, int64_t N, int QB, int fmt_in,
+                               int in_scale_dtype, int g_dtype, int fmt_out, int flags, void* stream);
+
 /* y = bf16(x1 + x2); if y_q != NULL also its 1xQB FP8 copy; group scales (bf16); optional tensor amax.
  * Replaces fp8_add_Ifp_Ifp_Ofp_Og16 (add_fwd.py:162-213, kernel :46-159) and the kernel of
  * fp8_add_Ifp_Ifp_Ofp_Opt (add_bwd.py:147-200, kernel :48-144). */

@@ -266,3 +266,32 @@ def test_rmsnorm_backward_sums_its_upstream_gradients(n_more):
     dx_ref, dw_ref = r.fp8_rmsnorm_backward(q, s, total, w, rstd, QB, nw)
     dx, dw = r.fp8_rmsnorm_backward(q, s, gs[0], w, rstd, QB, nw, more_g=tuple(gs[1:]))
     assert torch.equal(dx, dx_ref) and torch.equal(dw, dw_ref)
+
+
+@pytest.mark.parametrize("flags", [None, IEEE])
+def test_mul_silu_backward_equals_the_two_operators(flags):
+    """The one-kernel backward of silu(gate) * up gives, bit for bit, what fp8_mul_backward followed by
+    fp8_silu_backward give (codes, transposed codes and per-tensor scales of both gradients)."""
+    import torch
+    r = R()
+    M, N = 272, 1408
+    silu_q, silu_s = qinput(M, N, 51)
+    up_q, up_s = qinput(M, N, 52)
+    gate_q, gate_s = qinput(M, N, 53, scale=2.0)
+    g = grad(M, N, 54).cuda()
+    args = [t.cuda() for t in (silu_q, silu_s, up_q, up_s)]
+    gate_q, gate_s = gate_q.cuda(), gate_s.cuda()
+    g1, (q_up, s_up, q_up_t) = r.fp8_mul_backward(*args, g, QB, "E5M2", output_quantized_transpose=True, flags=flags)
+    q_gate, s_gate, q_gate_t = r.fp8_silu_backward(gate_q, gate_s, g1, QB, "E5M2", output_quantized_transpose=True,
+                                                   flags=flags)
+    (f_up, fs_up, f_up_t), (f_gate, fs_gate, f_gate_t) = r.fp8_mul_silu_backward(*args, gate_q, gate_s, g, QB, "E5M2",
+                                                                                   flags=flags)
+    u8 = lambda t: t.view(torch.uint8)
+    assert fs_up == s_up and fs_gate == s_gate
+    assert torch.equal(u8(f_up), u8(q_up)) and torch.equal(u8(f_up_t), u8(q_up_t))
+    assert torch.equal(u8(f_gate), u8(q_gate)) and torch.equal(u8(f_gate_t), u8(q_gate_t))
+    # batched input keeps the leading dimension on the straight codes
+    b = lambda t: t.view(2, M // 2, -1)
+    (b_up, _, b_up_t), _ = r.fp8_mul_silu_backward(b(args[0]), b(args[1]), b(args[2]), b(args[3]), b(gate_q), b(gate_s),
+                                                   b(g), QB, "E5M2", flags=flags)
+    assert b_up.shape == (2, M // 2, N) and torch.equal(u8(b_up).view(M, N), u8(q_up)) and b_up_t.shape == (N, M)
