@@ -564,6 +564,7 @@ def fused_extras(torch, device, peak):
         "mul_forward_pertensor_transposed": (lambda d: r.fp8_mul_forward(*d["gate"], *d["up"], 16, transpose_output_2d=True), T * I, 4.25),
         "mul_backward_pertensor_transposed": (lambda d: r.fp8_mul_backward(*d["gate"], *d["up"], d["g_i"], 16, "E5M2", output_quantized_transpose=True), T * I, 8.25),
         "silu_backward_pertensor_transposed": (lambda d: r.fp8_silu_backward(*d["gate"], d["g_i"], 16, "E5M2", output_quantized_transpose=True), T * I, 5.125),
+        "silu_mul_forward_one_kernel": (lambda d: r.fp8_silu_mul_forward(*d["gate"], *d["up"], 16, transpose_output_2d=True), T * I, 5.375),
         "mul_silu_backward_one_kernel": (lambda d: r.fp8_mul_silu_backward(*d["gate"], *d["up"], *d["gate"], d["g_i"], 16, "E5M2"), T * I, 9.375),
         "gelu_forward_pertensor_transposed": (lambda d: r.fp8_gelu_forward(*d["gate"], 16, transpose_output_2d=True), T * I, 3.125),
         "add_fwd_bf16_and_1x16": (lambda d: r.fp8_add_Ifp_Ifp_Ofp_Og16(d["a"], d["b"], torch.float8_e4m3fn, 16), T * H, 7.125),

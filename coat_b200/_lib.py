@@ -55,6 +55,7 @@ SIGNATURES = {
     "coat_fp8_mul_forward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_mul_backward": [_vp] * 9 + [_i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_add": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
+    "coat_fp8_silu_mul_forward": [_vp] * 9 + [_i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_mul_silu_backward": [_vp] * 13 + [_i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_rmsnorm_forward": [_vp] * 7 + [_i64, _i64, _i, _f, _i, _i, _i, _i, _vp],
     "coat_fp8_rmsnorm_backward": [_vp] * 9 + [_i, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],

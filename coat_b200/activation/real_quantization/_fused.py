@@ -146,6 +146,29 @@ def fp8_mul_backward(x1, s_x1, x2, s_x2, g, QB, fp8type, stochastic=False, outpu
     return _unflat(y1, bs), (_unflat(qy2, bs), s_max, qy2_t)
 
 
+def fp8_silu_mul_forward(gate_x, gate_s, up_x, up_s, QB, transpose_output_2d=False, *, flags=None):
+    """Forward of `silu(gate) * up` in one elementwise kernel (no counterpart in the reference, which calls
+    fp8_silu_forward and fp8_mul_forward one after the other; same bits):
+        (silu_x, silu_s), (mul_x, s_max, mul_x_t) = fp8_silu_forward(gate_x, gate_s, QB) and
+        fp8_mul_forward(silu_x, silu_s, up_x, up_s, QB, transpose_output_2d)."""
+    (a, sa, b, sb), bs = _flat(gate_x, gate_s, up_x, up_s)
+    assert a.shape == b.shape and sa.shape == sb.shape and a.dtype == b.dtype and sa.dtype == sb.dtype
+    M, N = a.shape
+    dev = a.device
+    q_silu = torch.empty_like(a)
+    s_silu = torch.empty_like(sa)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    amax = _amax_word(dev)
+    with torch.cuda.device(dev):
+        _call("coat_fp8_silu_mul_forward", a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(), q_silu.data_ptr(),
+              s_silu.data_ptr(), y.data_ptr(), None, amax.data_ptr(), M, N, QB, _lib.fp8_enum_of(a),
+              _lib.float_dtype(sa), _flags(flags), _lib.stream_ptr(dev))
+        qy, s_max, qy_t = _divide(y, b.dtype, amax, True, flags, scale_dtype=sa.dtype)
+    if bs is not None and not transpose_output_2d:
+        qy_t = qy_t.reshape(bs, -1, qy.shape[-1])
+    return (_unflat(q_silu, bs), _unflat(s_silu, bs)), (_unflat(qy, bs), s_max, qy_t)
+
+
 def fp8_mul_silu_backward(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type, *, flags=None):
     """Backward of `silu(gate) * up` in one elementwise kernel (no counterpart in the reference, which calls
     fp8_mul_backward and fp8_silu_backward one after the other; same bits):

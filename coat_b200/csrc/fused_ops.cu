@@ -248,6 +248,82 @@ mul_silu_backward_kernel(MulSiluBwdArgs a) {
 }
 
 // =================================================================================================
+// Gated-MLP forward in one kernel: fp8_silu_forward (silu_fwd.py:100-118) followed by fp8_mul_forward's kernel
+// (mul_fwd.py:101-127).  silu(gate) is quantised in 1xQB groups (codes and scales are outputs: the backward pass
+// needs them) and the product is formed from those codes times the ROUNDED scale, which is what the second
+// operator would read back from memory; the product leaves as bf16 with its group scales and the tensor amax.
+// =================================================================================================
+struct SiluMulFwdArgs {
+    const uint8_t* x_gate; const void* s_gate;
+    const uint8_t* x_up; const void* s_up;
+    uint8_t* q_silu; void* s_silu;
+    __nv_bfloat16* y; void* s_y; unsigned int* amax;
+    int64_t M, N;
+    int QB, scale_dtype;
+    float fp8_max;
+};
+
+template <int FMT, bool IEEE>
+__global__ void __launch_bounds__(kStraightThreads)
+silu_mul_forward_kernel(SiluMulFwdArgs a) {
+    const int64_t total = a.M * (a.N >> 4);
+    const int lanes = a.QB >> 4;
+    const int lane_shift = 31 - __clz(lanes);
+    const int64_t seg = (int64_t)blockIdx.x * kStraightThreads + threadIdx.x;
+    const bool live = seg < total;
+    const int64_t off = seg * 16;
+    float v[16], xu[16];
+    float amax = 0.f;
+    if (live) {
+        float xg[16];
+        load_dequant16<FMT>(a.x_gate, a.s_gate, a.scale_dtype, seg, lane_shift, xg);
+        load_dequant16<FMT>(a.x_up, a.s_up, a.scale_dtype, seg, lane_shift, xu);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            v[i] = sigmoid_ref<IEEE>(xg[i]) * xg[i];
+            amax = fmaxf(amax, fabsf(v[i]));
+        }
+    }
+    amax = subgroup_max(amax, lanes);   // whole warps: the grid is rounded up to blocks of 256 threads
+    float pmax = 0.f;
+    if (live) {
+        const float scale = qdiv<IEEE>(amax + kScaleMinThres, a.fp8_max);
+        float q[16];
+        ScaleDivider<IEEE>(scale).apply(v, q);
+        const uint4 codes = pack16<FMT>(q);
+        *reinterpret_cast<uint4*>(a.q_silu + off) = codes;
+        if ((seg & (lanes - 1)) == 0) store_scale(a.s_silu, seg >> lane_shift, a.scale_dtype, scale);
+        const float stored = round_to_dtype(scale, a.scale_dtype);   // what the product operator reads back
+        const uint32_t ww[4] = {codes.x, codes.y, codes.z, codes.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float f[4];
+            coat_fp8x4_to_float4<FMT>(ww[i], f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[4 * i + j] = (f[j] * stored) * xu[4 * i + j];
+                pmax = fmaxf(pmax, fabsf(v[4 * i + j]));
+            }
+        }
+    }
+    pmax = subgroup_max(pmax, lanes);
+    if (live) {
+        store_bf16x16(a.y + off, v);
+        if (a.s_y && (seg & (lanes - 1)) == 0)
+            store_scale(a.s_y, seg >> lane_shift, a.scale_dtype, qdiv<IEEE>(pmax + kScaleMinThres, a.fp8_max));
+    }
+    pmax = coat_warp_max(live ? pmax : 0.f);
+    __shared__ float wmax[kStraightThreads / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = pmax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < kStraightThreads / 32 ? wmax[threadIdx.x] : 0.f;
+        m = coat_warp_max(m);
+        if (threadIdx.x == 0) atomicMax(a.amax, __float_as_uint(m));
+    }
+}
+
+// =================================================================================================
 // RMSNorm on a 1xQB-quantised input (func_rmsnorm.py:54-111 forward, :121-220 backward)
 // =================================================================================================
 // One CTA of 256 threads per row; thread t owns the 16-element segments t, t+256, ... (S of them, in
@@ -746,6 +822,31 @@ extern "C" int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const 
     a.y1_bf16 = reinterpret_cast<__nv_bfloat16*>(y1_bf16); a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y2_bf16);
     a.s_y = s_y2; a.amax_bits = amax_bits;
     return launch_fused<OP_MUL_BWD>(a, fmt_in, fmt_out, flags, (cudaStream_t)stream);
+}
+
+extern "C" int coat_fp8_silu_mul_forward(const uint8_t* x_gate, const void* s_gate, const uint8_t* x_up, const void* s_up,
+                                         uint8_t* q_silu, void* s_silu, void* y_bf16, void* s_y, unsigned int* amax_bits,
+                                         int64_t M, int64_t N, int QB, int fmt, int scale_dtype, int flags,
+                                         void* stream) {
+    if (int rc = check_shape(M, N, QB)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!amax_bits) return COAT_E_BADARG;
+    if (cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return COAT_E_LAUNCH;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x_gate || !s_gate || !x_up || !s_up || !q_silu || !s_silu || !y_bf16) return COAT_E_BADARG;
+    if (!fmt_ok(fmt) || !fdt_ok(scale_dtype)) return COAT_E_BADARG;
+    SiluMulFwdArgs a = {x_gate, s_gate, x_up, s_up, q_silu, s_silu, reinterpret_cast<__nv_bfloat16*>(y_bf16), s_y,
+                        amax_bits, M, N, QB, scale_dtype, fmt_max(fmt)};
+    const unsigned grid = straight_grid(M * (N / 16));
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+    if (fmt == COAT_E4M3) {
+        if (ieee) silu_mul_forward_kernel<COAT_E4M3, true><<<grid, kStraightThreads, 0, st>>>(a);
+        else silu_mul_forward_kernel<COAT_E4M3, false><<<grid, kStraightThreads, 0, st>>>(a);
+    } else {
+        if (ieee) silu_mul_forward_kernel<COAT_E5M2, true><<<grid, kStraightThreads, 0, st>>>(a);
+        else silu_mul_forward_kernel<COAT_E5M2, false><<<grid, kStraightThreads, 0, st>>>(a);
+    }
+    return coat_launch_status();
 }
 
 extern "C" int coat_fp8_mul_silu_backward(const uint8_t* x_silu, const void* s_silu, const uint8_t* x_up, const void* s_up,

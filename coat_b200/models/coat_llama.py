@@ -34,12 +34,11 @@ from ..activation.real_quantization import (
     fp8_linear_backward,
     fp8_linear_forward,
     fp8_mul_silu_backward,
-    fp8_mul_forward,
     fp8_quantize_pertensor,
     fp8_quantize_pertensor_transpose,
     fp8_rmsnorm_backward,
     fp8_rmsnorm_forward,
-    fp8_silu_forward,
+    fp8_silu_mul_forward,
     fp8_transpose,
 )
 from ..utils._fp8_quantization_config import QuantizationConfig
@@ -289,8 +288,9 @@ class _CoatLlamaMLPResidual(torch.autograd.Function):
         # gate / up projections leave the GEMM already quantised in 1x16 groups
         gate_x, gate_s = fp8_linear_forward(ln_x, ln_s, w_gate, weight1_s, True, group_size)
         up_x, up_s = fp8_linear_forward(ln_x, ln_s, w_up, weight2_s, True, group_size)
-        silu_x, silu_s = fp8_silu_forward(gate_x, gate_s, group_size)
-        mul_x, mul_s, mul_x_t = fp8_mul_forward(silu_x, silu_s, up_x, up_s, group_size, transpose_output_2d=True)
+        # (one kernel for fp8_silu_forward followed by fp8_mul_forward: same bits)
+        (silu_x, silu_s), (mul_x, mul_s, mul_x_t) = fp8_silu_mul_forward(gate_x, gate_s, up_x, up_s, group_size,
+                                                                         transpose_output_2d=True)
         fc3_x = fp8_linear_forward(mul_x, mul_s, w_down, weight3_s, False, group_size)
         fp_x, (out_x, out_s) = fp8_add_Ifp_Ifp_Ofp_Og16(re_x, fc3_x, mul_x.dtype, group_size)
 

@@ -283,6 +283,15 @@ int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const uint8_t* x2
                           int64_t M, int64_t N, int QB, int fmt_in, int in_scale_dtype, int g_dtype,
                           int fmt_out, int flags, void* stream);
 
+/* Forward of the gated MLP product in one kernel: coat_fp8_silu_forward(x_gate) followed by
+ * coat_fp8_mul_forward(that result, x_up): q_silu / s_silu = 1xQB FP8 of silu(x_gate) (outputs, the backward pass
+ * reads them), y = bf16(dequantised silu * x_up) with group scales s_y (may be NULL) and the tensor amax, bit for bit
+ * what the two calls give (an extension: the reference calls fp8_silu_forward, silu_fwd.py:152-198, and
+ * fp8_mul_forward, mul_fwd.py:161-254, one after the other). */
+int coat_fp8_silu_mul_forward(const uint8_t* x_gate, const void* s_gate, const uint8_t* x_up, const void* s_up,
+                              uint8_t* q_silu, void* s_silu, void* y_bf16, void* s_y, unsigned int* amax_bits,
+                              int64_t M, int64_t N, int QB, int fmt, int scale_dtype, int flags, void* stream);
+
 /* Backward of the gated MLP product in one kernel: coat_fp8_mul_backward(x_silu, x_up, g) followed by
  * coat_fp8_act_backward(SiLU, x_gate, its first output) without the bf16 round trip between them:
  *   y_up   = bf16(g * x_silu),                              group scales s_y_up (bf16),   tensor amax *amax_up

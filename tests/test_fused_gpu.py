@@ -295,3 +295,22 @@ def test_mul_silu_backward_equals_the_two_operators(flags):
     (b_up, _, b_up_t), _ = r.fp8_mul_silu_backward(b(args[0]), b(args[1]), b(args[2]), b(args[3]), b(gate_q), b(gate_s),
                                                    b(g), QB, "E5M2", flags=flags)
     assert b_up.shape == (2, M // 2, N) and torch.equal(u8(b_up).view(M, N), u8(q_up)) and b_up_t.shape == (N, M)
+
+
+@pytest.mark.parametrize("flags", [None, IEEE])
+def test_silu_mul_forward_equals_the_two_operators(flags):
+    """The one-kernel forward of silu(gate) * up gives, bit for bit, what fp8_silu_forward followed by
+    fp8_mul_forward give (the saved silu codes and scales, the product's codes, transposed codes and scale)."""
+    import torch
+    r = R()
+    M, N = 272, 1408
+    gate_q, gate_s = qinput(M, N, 61, scale=2.0)
+    up_q, up_s = qinput(M, N, 62)
+    gate_q, gate_s, up_q, up_s = (t.cuda() for t in (gate_q, gate_s, up_q, up_s))
+    silu_q, silu_s = r.fp8_silu_forward(gate_q, gate_s, QB, flags=flags)
+    mul_q, mul_s, mul_t = r.fp8_mul_forward(silu_q, silu_s, up_q, up_s, QB, transpose_output_2d=True, flags=flags)
+    (f_silu_q, f_silu_s), (f_mul_q, f_mul_s, f_mul_t) = r.fp8_silu_mul_forward(gate_q, gate_s, up_q, up_s, QB,
+                                                                               transpose_output_2d=True, flags=flags)
+    u8 = lambda t: t.view(torch.uint8)
+    assert torch.equal(u8(f_silu_q), u8(silu_q)) and torch.equal(f_silu_s, silu_s)
+    assert f_mul_s == mul_s and torch.equal(u8(f_mul_q), u8(mul_q)) and torch.equal(u8(f_mul_t), u8(mul_t))
