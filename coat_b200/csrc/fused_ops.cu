@@ -368,7 +368,7 @@ __device__ __forceinline__ void prefetch_row(const uint8_t* x, const void* dy, i
     for (int k = 0; k < S; ++k) {
         const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
         if (c16 < segs) {
-            if ((threadIdx.x & 7) == 0) prefetch_l2(x + (row * segs + c16) * 16);   // 8 segments of codes per 128-byte line
+            if (x && (threadIdx.x & 7) == 0) prefetch_l2(x + (row * segs + c16) * 16);   // 8 segments of codes per 128-byte line
             const char* g = reinterpret_cast<const char*>(dy) + (row * N + c16 * 16) * dy_bytes;
             if (dy_bytes == 4 || (threadIdx.x & 3) == 0) prefetch_l2(g);          // 32 (64) bytes of gradient per segment
         }
@@ -448,6 +448,8 @@ rmsnorm_bwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
     }
     for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
         prefetch_row<S>(x, dy, dy_dtype, row + gridDim.x, M, N, segs);
+        if (dy2) prefetch_row<S>(nullptr, dy2, dy_dtype, row + gridDim.x, M, N, segs);
+        if (dy3) prefetch_row<S>(nullptr, dy3, dy_dtype, row + gridDim.x, M, N, segs);
         const float rstd = rstd_in[row];
         float xhat[S][16], wdy[S][16];
         float dot = 0.f;
