@@ -155,6 +155,14 @@ def _default_scale(x, fp8type, flags):
     return (amax.view(torch.float32)[0].to(x.dtype) + SCALE_MIN_THRES) / FP8_MAX_VALUE[fp8type]
 
 
+def fp8_pertensor_scale(x, fp8type, *, flags=None):
+    """The per-tensor scale alone, (x.abs().max() + 1e-10) / fp8_max in x's dtype: what `fp8_division(x, QB, fp8type)`
+    returns as its scale when none is passed (_division.py:178-179), without quantising anything.  For callers
+    that keep only the scale (the weight cache in memory-efficient mode)."""
+    x, _ = _prep(x)
+    return _default_scale(x, _fp8_dtype(fp8type), flags)
+
+
 def _division(x, fp8type, s_y, want_straight, want_transposed, flags, stochastic=False):
     M, N = x.shape
     want_straight = want_straight or stochastic   # the stochastic transposed copy is made from the straight one
