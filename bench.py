@@ -739,7 +739,7 @@ def run_gpu_arm(args):
         # profiles/fp8_adamw_expand_tiled_c1.md), scaled to this launch by its parameter count
         traffic = NCU_DRAM_BYTES_PER_PARAM * my_params
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_kernel<float,expand,table>",
+                    "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_expand_tiled_kernel<float,table>",
                     "kernel_ms": kernel_ms, "algorithmic_bytes_per_param": BYTES_PER_PARAM_BF16}
         if args.kernel_only or world > 1:  # profiling runs: nothing but the fused kernel; the CPU leg runs at N = 1
             cpu_v = cpu_steps = cpu_dt = cores = None
