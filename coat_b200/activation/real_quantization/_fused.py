@@ -258,7 +258,8 @@ def fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps, *, more_g=()):
     dev = x.device
     dx = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     dw = torch.empty((N,), dtype=w.dtype, device=dev)
-    n_partials = min(M, 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+    # one CTA per partial sum, all resident at once: 3 per SM for rows of up to 4096 elements, 2 beyond
+    n_partials = min(M, (3 if N <= 4096 else 2) * torch.cuda.get_device_properties(dev).multi_processor_count)
     partial = torch.empty((n_partials, N), dtype=torch.float32, device=dev)
     w = w.contiguous()
     with torch.cuda.device(dev):
