@@ -12,6 +12,8 @@ Reference wrappers mirrored here:
   fp8_dequantize                    _dequantize.py:119-156
 (paths under coat/activation/real_quantization/).
 """
+import os
+
 import torch
 
 from ... import _lib
@@ -72,6 +74,9 @@ def _flags_stochastic(flags, stochastic):
 
 
 _SYNC_WORDS = {}
+# COAT_PERTENSOR_ONE_LAUNCH=0: always take the two-call form (a cooperative launch needs every SM the library counts;
+# on a GPU partitioned by MPS limits or green contexts it is refused with a launch error)
+_ONE_LAUNCH = os.environ.get("COAT_PERTENSOR_ONE_LAUNCH", "1") != "0"
 
 
 def _sync_words(dev):
@@ -103,7 +108,8 @@ def _pertensor(x, QB, fp8type, scale_dtype, want_scales, want_straight, want_tra
     with torch.cuda.device(dev):
         st = _lib.stream_ptr(dev)
         # the transposing form of the one-launch kernel walks 128 x 128 tiles: no group scales, M % 16 == 0
-        one_launch = not stochastic and (not want_transposed or (not want_scales and M % 16 == 0))
+        one_launch = (_ONE_LAUNCH and not stochastic and
+                      (not want_transposed or (not want_scales and M % 16 == 0)))
         if one_launch:
             key, words = _sync_words(dev)
             try:
