@@ -79,7 +79,12 @@ template <bool IEEE>
 __device__ __forceinline__ float sigmoid_ref(float x) { return qdiv<IEEE>(1.0f, 1.0f + expf(-x)); }
 
 __device__ __forceinline__ float sqrt_approx(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
-__device__ __forceinline__ float ex2_approx(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float ex2_approx_noftz(float x) { float r; asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
+// `tl.math.sqrt(2.0)` and `tl.sqrt(2 * pi)` of the GELU kernels are folded by Triton's compiler into the correctly
+// rounded constants 0x3FB504F3 and 0x40206C99 (gelu_fwd.py:109, gelu_bwd.py:127-128); a run-time sqrt.approx of the
+// same arguments is one step off for the second, which flips a few codes per hundred thousand.
+__device__ constexpr float kSqrt2 = 1.41421353816986083984375f;     // 0x3FB504F3
+__device__ constexpr float kSqrt2Pi = 2.5066282749176025390625f;    // 0x40206C99
 
 // (no minimum number of CTAs per SM in the launch bounds: a minimum of 1 lets the compiler spend registers that cost
 // occupancy, SiLU backward 219 us instead of 178 us; minima of 6 and 8 measured no better than leaving it out)
@@ -119,17 +124,17 @@ fused_elementwise_kernel(FusedArgs a) {
                         v[i] = __fmaf_rn(x[i] * sg, 1.0f - sg, sg) * t[i];
                     }
                 } else if (OP == OP_GELU_FWD) {
-                    const float rt2 = sqrt_approx(2.0f);
+                    const float rt2 = kSqrt2;
 #pragma unroll
                     for (int i = 0; i < 16; ++i) v[i] = qdiv<IEEE>(1.0f + erff(qdiv<IEEE>(x[i], rt2)), 2.0f) * x[i];
                 } else if (OP == OP_GELU_BWD) {
                     load_float16(a.g, a.g_dtype, off, t);
-                    const float rt2 = sqrt_approx(2.0f), rt2pi = sqrt_approx(2.0f * 3.1415927410125732f);
+                    const float rt2 = kSqrt2, rt2pi = kSqrt2Pi;
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float cdf = qdiv<IEEE>(1.0f + erff(qdiv<IEEE>(x[i], rt2)), 2.0f);
-                        // tl.exp(u) is ex2.approx(u * log2 e)
-                        const float e = ex2_approx(qdiv<IEEE>(-powf(x[i], 2.0f), 2.0f) * 1.4426950408889634f);
+                        // libdevice.pow(x, 2) is x * x; tl.exp(u) is ex2.approx(u * log2 e) without flush-to-zero
+                        const float e = ex2_approx_noftz(qdiv<IEEE>(0.0f - __fmul_rn(x[i], x[i]), 2.0f) * 1.4426950408889634f);
                         v[i] = (cdf + qdiv<IEEE>(x[i] * e, rt2pi)) * t[i];
                     }
                 } else {   // OP_MUL_FWD, OP_MUL_BWD
@@ -327,24 +332,117 @@ silu_mul_forward_kernel(SiluMulFwdArgs a) {
 // =================================================================================================
 // RMSNorm on a 1xQB-quantised input (func_rmsnorm.py:54-111 forward, :121-220 backward)
 // =================================================================================================
-// One CTA of 256 threads per row; thread t owns the 16-element segments t, t+256, ... (S of them, in
-// registers), so a row of up to 16384 elements is read once.  Row sums are reduced in a fixed order
-// (sequential inside a thread, xor-shuffles inside a warp, then the 8 warp results in order), so the
-// result does not depend on scheduling.  The reference's sum order is whatever layout Triton picks, so
-// rstd agrees with it to rounding only, not bit for bit.
+// One CTA of 256 threads per row; thread t owns S 16-element segments (forward: S t ... S t + S - 1, the
+// reference's layout; backward: t, t+256, ...) in registers, so a row of up to 16384 elements is read once.  Row sums are reduced in a fixed order
+// (inside a thread, xor-shuffles inside a warp, then a tree over the 8 warp results), so the result does not
+// depend on scheduling; the forward kernels use the order of the reference's compiled kernels
+// (ref_order_row_sum), which makes rstd, and with it every output, bit-identical to the reference's.
 constexpr int kNormThreads = 256;
 
-__device__ __forceinline__ float block_sum(float v, float* smem /*[8]*/) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(COAT_FULL_MASK, v, o);
+// the eight warp sums combined as a butterfly over eight lanes does it (xor 4, 2, 1)
+__device__ __forceinline__ float block_sum_of_warp_sums(float v, float* smem /*[8]*/) {
     __syncthreads();   // protects smem reuse between consecutive reductions
     if ((threadIdx.x & 31) == 0) smem[threadIdx.x >> 5] = v;
     __syncthreads();
-    float r = 0.f;
-#pragma unroll
-    for (int w = 0; w < kNormThreads / 32; ++w) r += smem[w];
-    return r;
+    const float a0 = __fadd_rn(smem[0], smem[4]), a1 = __fadd_rn(smem[1], smem[5]);
+    const float a2 = __fadd_rn(smem[2], smem[6]), a3 = __fadd_rn(smem[3], smem[7]);
+    return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
 }
+__device__ __forceinline__ float block_sum(float v, float* smem /*[8]*/) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(COAT_FULL_MASK, v, o);
+    return block_sum_of_warp_sums(v, smem);
+}
+
+// Row sum of products a_i * b_i in the ORDER the reference's norm kernels use on this architecture, so that the
+// forward statistics (and with them every code) come out bit-identical to the reference's.  Its Triton kernels run
+// one program of 256 threads per row over the row padded with zeros to a power of two n2 (func_rmsnorm.py:82-95).
+// The layouts and the contractions below are read from that compiler's own output for sm_100 (its layout
+// attributes and PTX text), n2 = 256 ... 16384:
+//   * thread t holds the E = max(1, n2 / 256) consecutive elements E t ... E t + E - 1; its registers hold them in
+//     the order r = 0, 1, ...: element (r % G) * 16 + r / G with G = max(1, E / 16) (for E <= 16 simply in order;
+//     beyond, the thread's G groups of 16 interleaved);
+//   * E >= 2: p = a[r1] * b[r1]; p = fma(a[r0], b[r0], p); p = fma(a[r], b[r], p) for r = 2, 3, ... (every product
+//     contracted into the running sum), then p += shfl_xor(p, 16), 8, 4, 2, 1;
+//   * E == 1: p = fma(a, b, shfl_xor(a * b, 16)) (the product is contracted into the first exchange), then 8, 4, 2, 1;
+//   * the eight warp sums are combined as a butterfly over eight lanes (xor 4, 2, 1).
+// `f(k, i, A, B)` yields the factors of element i of this thread's k-th group of 16 (zeros in the padding).  With
+// n2 >= 4096 thread t of this kernel holds the same elements as the reference's thread t (groups S t ... S t + S - 1,
+// S = n2 / 4096); shorter rows go through shared memory, one slot per thread of the reference's layout.  Rows of
+// fewer than 32 elements are summed in this order too, which is not the reference's there.
+template <int E, class F>
+__device__ __forceinline__ void ref_order_partials(F f, float* part_a, float* part_b) {
+#pragma unroll
+    for (int j = 0; j < 16; j += E) {
+        float A, B;
+        const int slot = (threadIdx.x * 16 + j) / E;
+        if (E == 1) {
+            f(0, j, A, B);
+            part_a[slot] = A;
+            part_b[slot] = B;
+        } else {
+            f(0, j + 1, A, B);
+            float p = __fmul_rn(A, B);
+            f(0, j, A, B);
+            p = __fmaf_rn(A, B, p);
+#pragma unroll
+            for (int i = 2; i < E; ++i) {
+                f(0, j + i, A, B);
+                p = __fmaf_rn(A, B, p);
+            }
+            part_a[slot] = p;
+        }
+    }
+}
+
+template <int S, class F>
+__device__ __forceinline__ float ref_order_row_sum(F f, int n2, float* part /*[512]*/, float* red /*[8]*/) {
+    float p, A, B;
+    if (n2 >= 4096) {   // S == n2 / 4096; register r = element i = r / S of group k = r % S
+        f(1 % S, 1 / S, A, B);
+        p = __fmul_rn(A, B);
+        f(0, 0, A, B);
+        p = __fmaf_rn(A, B, p);
+#pragma unroll
+        for (int r = 2; r < 16 * S; ++r) {
+            f(r % S, r / S, A, B);
+            p = __fmaf_rn(A, B, p);
+        }
+        p += __shfl_xor_sync(COAT_FULL_MASK, p, 16);
+    } else {
+        const int e = n2 >= 256 ? n2 >> 8 : 1;
+        float* part_b = part + kNormThreads;
+        __syncthreads();
+        part[threadIdx.x] = 0.f;
+        part_b[threadIdx.x] = 0.f;
+        __syncthreads();
+        if ((int)threadIdx.x < (n2 >> 4)) {
+            if (e == 1) ref_order_partials<1>(f, part, part_b);
+            else if (e == 2) ref_order_partials<2>(f, part, part_b);
+            else if (e == 4) ref_order_partials<4>(f, part, part_b);
+            else ref_order_partials<8>(f, part, part_b);
+        }
+        __syncthreads();
+        if (e == 1) {
+            A = part[threadIdx.x];
+            B = part_b[threadIdx.x];
+            p = __fmaf_rn(A, B, __shfl_xor_sync(COAT_FULL_MASK, __fmul_rn(A, B), 16));
+        } else {
+            p = part[threadIdx.x];
+            p += __shfl_xor_sync(COAT_FULL_MASK, p, 16);
+        }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(COAT_FULL_MASK, p, o);
+    return block_sum_of_warp_sums(p, red);
+}
+
+__device__ __forceinline__ int next_pow2_at_least_16(int64_t n) {
+    int p = 16;
+    while (p < n) p <<= 1;
+    return p;
+}
+
 __device__ __forceinline__ float block_max(float v, float* smem /*[8]*/) {
     v = coat_warp_max(v);
     __syncthreads();
@@ -383,28 +481,28 @@ rmsnorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x, 
                    __nv_bfloat16* __restrict__ s_y, float* __restrict__ rstd_out, unsigned int* __restrict__ amax_bits,
                    int64_t M, int64_t N, int QB, float eps, int fp8_fmt_out) {
     __shared__ float red[kNormThreads / 32];
+    __shared__ float part[2 * kNormThreads];
     const int64_t row = blockIdx.x;
     const int64_t segs = N >> 4;
     float v[S][16];
-    float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        const int64_t c16 = (int64_t)threadIdx.x * S + k;   // the reference's layout: S consecutive groups per thread
         if (c16 < segs) {
             load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), v[k]);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) ss += v[k][i] * v[k][i];
         } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[k][i] = 0.f;
         }
     }
-    const float var = qdiv<IEEE>(block_sum(ss, red), (float)N);
+    const float ss = ref_order_row_sum<S>([&](int k, int i, float& A, float& B) { A = v[k][i]; B = v[k][i]; },
+                                          next_pow2_at_least_16(N), part, red);
+    const float var = qdiv<IEEE>(ss, (float)N);
     const float rstd = qdiv<IEEE>(1.0f, sqrt_approx(var + eps));
     float amax = 0.f;
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        const int64_t c16 = (int64_t)threadIdx.x * S + k;   // the reference's layout: S consecutive groups per thread
         if (c16 < segs) {
             float wv[16];
             load_float16(w, w_dtype, c16 * 16, wv);
@@ -569,38 +667,49 @@ layernorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x
                      __nv_bfloat16* __restrict__ s_y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
                      unsigned int* __restrict__ amax_bits, int64_t M, int64_t N, int QB, float eps, int fp8_fmt_out) {
     __shared__ float red[kNormThreads / 32];
+    __shared__ float part[2 * kNormThreads];
     const int64_t row = blockIdx.x;
     const int64_t segs = N >> 4;
-    float v[S][16];
-    float sum = 0.f;
+    const int n2 = next_pow2_at_least_16(N);
+    // raw codes as floats and the segment's scale: the reference's compiled kernel never rounds code * scale on
+    // its own in this operator, every use is contracted into a multiply-add (func_layernorm_noparam.py:86-96)
+    float c[S][16], sc[S];
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        const int64_t c16 = (int64_t)threadIdx.x * S + k;   // the reference's layout: S consecutive groups per thread
+        sc[k] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[k][i] = 0.f;
         if (c16 < segs) {
-            load_dequant16<FMT>(x, s_x, in_scale_dtype, row * segs + c16, 31 - __clz(QB >> 4), v[k]);
+            const int64_t seg = row * segs + c16;
+            const uint4 wq = *reinterpret_cast<const uint4*>(x + seg * 16);
+            sc[k] = load_scale(s_x, seg >> (31 - __clz(QB >> 4)), in_scale_dtype);
+            const uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sum += v[k][i];
-        }
-    }
-    const float mean = qdiv<IEEE>(block_sum(sum, red), (float)N);
-    float ss = 0.f;
+            for (int i = 0; i < 4; ++i) {
+                float f4[4];
+                coat_fp8x4_to_float4<FMT>(ww[i], f4);
 #pragma unroll
-    for (int k = 0; k < S; ++k) {
-        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
-        if (c16 < segs) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                v[k][i] -= mean;
-                ss += v[k][i] * v[k][i];
+                for (int j = 0; j < 4; ++j) c[k][4 * i + j] = f4[j];
             }
         }
     }
-    const float var = qdiv<IEEE>(block_sum(ss, red), (float)N);
+    const float sum = ref_order_row_sum<S>([&](int k, int i, float& A, float& B) { A = c[k][i]; B = sc[k]; }, n2, part, red);
+    const float mean = qdiv<IEEE>(sum, (float)N);
+    // deviations x - mean = fma(code, scale, -mean).  As in the reference the zero padding up to the next power of
+    // two is NOT masked out of the variance (each padded element adds mean^2, func_layernorm_noparam.py:92-94):
+    // rows whose length is a power of two, the only ones the OLMo models have, are unaffected.
+#pragma unroll
+    for (int k = 0; k < S; ++k)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[k][i] = __fmaf_rn(c[k][i], sc[k], -mean);
+    const float ss = ref_order_row_sum<S>([&](int k, int i, float& A, float& B) { A = c[k][i]; B = c[k][i]; }, n2, part, red);
+    const float var = qdiv<IEEE>(ss, (float)N);
     const float rstd = qdiv<IEEE>(1.0f, sqrt_approx(var + eps));
     float amax = 0.f;
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-        const int64_t c16 = threadIdx.x + (int64_t)k * kNormThreads;
+        const int64_t c16 = (int64_t)threadIdx.x * S + k;   // the reference's layout: S consecutive groups per thread
         if (c16 < segs) {
             float wv[16], bv[16];
             if (AFFINE) {
@@ -609,14 +718,14 @@ layernorm_fwd_kernel(const uint8_t* __restrict__ x, const void* __restrict__ s_x
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                v[k][i] *= rstd;
-                if (AFFINE) v[k][i] = v[k][i] * wv[i] + bv[i];
-                amax = fmaxf(amax, fabsf(v[k][i]));
+                c[k][i] = __fmul_rn(c[k][i], rstd);
+                if (AFFINE) c[k][i] = __fmaf_rn(c[k][i], wv[i], bv[i]);
+                amax = fmaxf(amax, fabsf(c[k][i]));
             }
             float4* dst = reinterpret_cast<float4*>(y + row * N + c16 * 16);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                dst[i] = make_float4(v[k][4 * i], v[k][4 * i + 1], v[k][4 * i + 2], v[k][4 * i + 3]);
+                dst[i] = make_float4(c[k][4 * i], c[k][4 * i + 1], c[k][4 * i + 2], c[k][4 * i + 3]);
         }
     }
     amax = block_max(amax, red);

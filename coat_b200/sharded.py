@@ -112,6 +112,7 @@ class _PeerBuffer:
     def __init__(self, lib_module, nbytes, device):
         import ctypes
         self._L = lib_module
+        self.device = device
         self.nbytes = int(nbytes)
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(lib_module.PEER_HANDLE_BYTES)
@@ -124,10 +125,10 @@ class _PeerBuffer:
         self.__cuda_array_interface__ = {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False),
                                          "version": 3, "strides": None}
 
-    def open_peer(self, rank, handle, device):
+    def open_peer(self, rank, handle):
         import ctypes
         ptr = ctypes.c_void_p()
-        with torch.cuda.device(device):
+        with torch.cuda.device(self.device):
             self._L.check(self._L.lib().coat_peer_buffer_open(handle, ctypes.byref(ptr)), "peer_buffer_open")
         self.peers[rank] = int(ptr.value)
 
@@ -142,6 +143,45 @@ class _PeerBuffer:
             self.ptr = 0
 
 
+def exchange_peer_buffers(make_buffer, rank, world_size, process_group=None):
+    """Create this rank's peer-mappable buffer with `make_buffer()`, swap handles over the process group and
+    map every peer's buffer (`buf.open_peer(rank, handle)`).  Returns the buffer.
+
+    A failure on ANY rank (allocation, or mapping one peer) is raised on EVERY rank, as a RuntimeError that
+    names the ranks that failed: the status travels with two object collectives that every rank takes part
+    in whatever happened to it, so no rank is left waiting in a collective for one that has already raised.
+    Callers may therefore fall back (e.g. to an NCCL exchange) on all ranks alike.  On failure whatever was
+    mapped is unmapped and, after a barrier, the rank's own buffer is freed."""
+    import torch.distributed as dist
+    err, buf = None, None
+    try:
+        buf = make_buffer()
+    except Exception as e:   # reported to every rank below
+        err = f"rank {rank}: {e}"
+    everyone = [None] * world_size
+    dist.all_gather_object(everyone, (err, buf.handle if buf is not None else None), group=process_group)
+    if not any(e for e, _ in everyone):
+        try:
+            for r in range(world_size):
+                if r != rank:
+                    buf.open_peer(r, everyone[r][1])
+        except Exception as e:
+            err = f"rank {rank}: {e}"
+    # second collective: every rank has mapped (or failed to map) every buffer before anyone steps
+    status = [None] * world_size
+    dist.all_gather_object(status, err, group=process_group)
+    failed = [e for e in status if e]
+    if failed:
+        if buf is not None:
+            buf.close()
+            dist.barrier(group=process_group)   # nobody maps this buffer any more
+            buf.free()
+        else:
+            dist.barrier(group=process_group)
+        raise RuntimeError("peer buffers could not be set up: " + "; ".join(failed))
+    return buf
+
+
 class ShardedCoatAdamW:
     """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
     weights everywhere.
@@ -216,147 +256,16 @@ class ShardedCoatAdamW:
         self.set_grad_buffer(self.grad)
 
     def _setup_peer_buffer(self, nbytes):
-        """Allocate this rank's gathered-weights buffer so that peers can map it, swap handles (a
-        collective over the process group) and map every peer's buffer.  A failure on any rank is
-        raised on every rank (the status travels with the collectives), so that callers can switch to
-        exchange="nccl" consistently."""
+        """Allocate this rank's gathered-weights buffer so that peers can map it, swap handles and map every
+        peer's buffer (exchange_peer_buffers: a failure on any rank is raised on every rank)."""
         import ctypes
-        import torch.distributed as dist
-        L = self._lib
-        err, buf = None, None
-        try:
-            buf = _PeerBuffer(L, nbytes, self.device)
-        except Exception as e:   # reported to every rank below
-            err = f"rank {self.rank}: {e}"
-        mine = (err, buf.handle if buf else None)
-        everyone = [None] * self.world_size
-        dist.all_gather_object(everyone, mine, group=self.process_group)
-        if not any(e for e, _ in everyone):
-            try:
-                for r in range(self.world_size):
-                    if r != self.rank:
-                        buf.open_peer(r, everyone[r][1], self.device)
-            except Exception as e:
-                err = f"rank {self.rank}: {e}"
-        status = [None] * self.world_size
-        # second collective: every rank has mapped (or failed to map) every buffer before anyone steps
-        dist.all_gather_object(status, err or everyone[self.rank][0], group=self.process_group)
-        failed = [e for e in status if e] or [e for e, _ in everyone if e]
-        if failed:
-            if buf:
-                buf.close()
-                dist.barrier(group=self.process_group)
-                buf.free()
-            raise RuntimeError("peer buffers could not be set up: " + "; ".join(failed))
+        buf = exchange_peer_buffers(lambda: _PeerBuffer(self._lib, nbytes, self.device), self.rank, self.world_size,
+                                    self.process_group)
         self._peer_buffer = buf
         self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
         deltas = [buf.peers[r] - buf.ptr for r in range(self.world_size) if r != self.rank]
         self._peer_deltas = (ctypes.c_int64 * len(deltas))(*deltas)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
-
-    def close(self):
-        for r, p in list(self.peers.items()):
-            self._L.lib().coat_peer_buffer_close(p)
-            del self.peers[r]
-
-    def free(self):
-        if self.ptr:
-            self._L.lib().coat_peer_buffer_free(self.ptr)
-            self.ptr = 0
-
-
-class ShardedCoatAdamW:
-    """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
-    weights everywhere.
-
-    exchange="p2p" (the default with more than one rank): ONE kernel per step does both the update and
-    the exchange; it stores its bf16 slice into every peer's copy of `self.gathered` over NVLink while
-    it computes (coat_fp8_adamw_multi_step_bcast), and a one-element all-reduce after it is the
-    barrier that tells every rank that all slices have landed.
-    exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
-    that the gather of bucket b runs under the step of bucket b+1.
-
-    With world_size 1 there is one bucket and no exchange.  Gradients are written by the caller
-    into `self.grad` (already reduce-scattered, as under ZeRO); the updated bf16 weights of ALL ranks
-    appear in `self.gathered` (bucket-major, see ShardPlan.gathered_offset) after step().  No rank may
-    start step k+1 while another still reads the weights of step k from `self.gathered`; in training
-    the gradient reduce-scatter between the two provides that order."""
-
-    def __init__(self, numels, rank=0, world_size=1, device="cuda", lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
-                 weight_decay=1e-2, expand_min=16, use_expansion=True, process_group=None, flags=0,
-                 n_buckets=None, exchange=None):
-        from . import _lib
-        self._lib = _lib
-        self.plan = ShardPlan(numels, world_size)
-        self.rank, self.world_size = rank, world_size
-        self.device = torch.device(device)
-        self.hyper = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, expand_min=expand_min)
-        self.use_expansion = use_expansion
-        self.process_group = process_group
-        self.flags = flags
-        self.step_count = 0
-        if exchange is None:
-            exchange = "p2p" if world_size > 1 else "none"
-        if exchange not in ("none", "p2p", "nccl") or (exchange == "none") != (world_size == 1):
-            raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
-        if exchange == "p2p" and world_size - 1 > _lib.MAX_PEERS:
-            raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
-        self.exchange = exchange
-        if n_buckets is None:
-            n_buckets = 8 if exchange == "nccl" else 1
-        self.bounds = self.plan.bucket_bounds(n_buckets)
-        self.n_buckets = len(self.bounds) - 1
-        self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
-        self.my_pieces = [pc for b in self.my_buckets for pc in b]
-        n, g = self.plan.shard_numel, self.plan.shard_groups
-        dev = self.device
-        self.param = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.grad = torch.zeros(n, dtype=torch.float32, device=dev)
-        self.exp_avg = torch.zeros(n, dtype=torch.uint8, device=dev)
-        self.exp_avg_sq = torch.zeros(n, dtype=torch.uint8, device=dev)
-        self.scale_exp_avg = torch.zeros(g, dtype=torch.float32, device=dev)
-        self.scale_exp_avg_sq = torch.zeros(g, dtype=torch.float32, device=dev)
-        self.expand_exp_avg = torch.ones(g, dtype=torch.float32, device=dev)
-        self.expand_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
-        self.sqrt_minmax_exp_avg = torch.ones(g, dtype=torch.float32, device=dev)
-        self.sqrt_minmax_exp_avg_sq = torch.ones(g, dtype=torch.float32, device=dev)
-        # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
-        self._peer_buffer = None
-        self._peer_deltas = None
-        if exchange == "p2p":
-            self._setup_peer_buffer(world_size * n * 2)
-        else:
-            self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
-        self._bucket_all, self._bucket_mine = [], []
-        for b in range(self.n_buckets):
-            lo, hi = int(self.bounds[b]) * GROUP, int(self.bounds[b + 1]) * GROUP
-            whole = self.gathered[lo * world_size: hi * world_size]
-            self._bucket_all.append(whole)
-            self._bucket_mine.append(whole[rank * (hi - lo):(rank + 1) * (hi - lo)])
-        self._comm = torch.cuda.Stream(device=dev) if exchange == "nccl" else None
-        self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if self._comm else []
-        self._table_cache = {}
-        self.set_grad_buffer(self.grad)
-
-    def _setup_peer_buffer(self, nbytes):
-        """Allocate this rank's gathered-weights buffer so that peers can map it, swap handles (a
-        collective over the process group) and map every peer's buffer."""
-        import ctypes
-        import torch.distributed as dist
-        L = self._lib
-        buf = _PeerBuffer(L, nbytes, self.device)
-        self._peer_buffer = buf
-        self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
-        handles = [None] * self.world_size
-        dist.all_gather_object(handles, buf.handle, group=self.process_group)
-        deltas = []
-        for r in range(self.world_size):
-            if r != self.rank:
-                buf.open_peer(r, handles[r], self.device)
-                deltas.append(buf.peers[r] - buf.ptr)
-        self._peer_deltas = (ctypes.c_int64 * len(deltas))(*deltas)
-        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
-        dist.barrier(group=self.process_group)   # every rank has mapped every buffer before anyone steps
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""

@@ -103,7 +103,11 @@ def layernorm_forward_value(x, s_x, w, b, QB, eps):
     n = v.shape[1]
     mean = v.sum(dim=1, keepdim=True) / n
     d = v - mean
-    var = (d * d).sum(dim=1, keepdim=True) / n
+    # the reference's kernels pad the row with zeros to the next power of two and do not mask the padding out of the
+    # squared deviations (func_layernorm_noparam.py:86-94, func_layernorm_param.py:86-94): each padded element adds
+    # mean^2.  Rows whose length is a power of two are unaffected.
+    n2 = 1 << max(4, (n - 1).bit_length())
+    var = ((d * d).sum(dim=1, keepdim=True) + (n2 - n) * mean * mean) / n
     rstd = 1 / torch.sqrt(var + eps)
     y = d * rstd
     if w is not None:

@@ -128,3 +128,62 @@ def test_gather_of_bf16_slices_world2_gloo():
     numels = [128 * 5, 77, 128 * 3 + 1, 4096, 1, 128 * 9]
     port = 29500 + os.getpid() % 2000
     mp.spawn(_gather_worker, args=(2, port, numels), nprocs=2, join=True)
+
+
+class _FakePeerBuffer:
+    """Stand-in for the CUDA IPC buffer: records what the set-up did to it."""
+
+    def __init__(self, rank, fail_create=False, fail_open=False):
+        if fail_create:
+            raise RuntimeError("out of memory (injected)")
+        self.handle = f"handle-of-{rank}".encode()
+        self.fail_open = fail_open
+        self.peers, self.closed, self.freed = {}, False, False
+
+    def open_peer(self, rank, handle):
+        if self.fail_open:
+            raise RuntimeError(f"cannot map the buffer of rank {rank} (injected)")
+        assert handle == f"handle-of-{rank}".encode()
+        self.peers[rank] = 1000 + rank
+
+    def close(self):
+        self.closed = True
+
+    def free(self):
+        self.freed = True
+
+
+def _peer_setup_worker(rank, world, port, failing_rank, how):
+    from coat_b200.sharded import exchange_peer_buffers
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        made = []
+
+        def make():
+            buf = _FakePeerBuffer(rank, fail_create=(how == "create" and rank == failing_rank),
+                                  fail_open=(how == "open" and rank == failing_rank))
+            made.append(buf)
+            return buf
+
+        if failing_rank is None:
+            buf = exchange_peer_buffers(make, rank, world)
+            assert sorted(buf.peers) == [r for r in range(world) if r != rank] and not buf.closed
+        else:
+            try:
+                exchange_peer_buffers(make, rank, world)
+            except RuntimeError as e:
+                # EVERY rank raises, and the message names the rank that failed
+                assert f"rank {failing_rank}" in str(e) and "injected" in str(e), str(e)
+            else:
+                raise AssertionError(f"rank {rank} did not see the failure of rank {failing_rank}")
+            assert all(b.closed and b.freed for b in made)
+        dist.barrier()   # no rank is stuck in a collective of the set-up
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("failing_rank,how", [(None, ""), (1, "open"), (0, "create")])
+def test_peer_buffer_setup_failure_reaches_every_rank_world2_gloo(failing_rank, how):
+    port = 33500 + os.getpid() % 2000 + (0 if failing_rank is None else 1 + failing_rank)
+    mp.spawn(_peer_setup_worker, args=(2, port, failing_rank, how), nprocs=2, join=True)
