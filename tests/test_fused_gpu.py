@@ -4,7 +4,8 @@
 Operators without a transcendental (gated product, residual add) must agree BIT FOR BIT under IEEE
 division.  SiLU / GELU evaluate exp / erf with libdevice on the GPU and libm on the CPU (last-place
 differences), and RMSNorm sums in a different order, so those are held to the tolerances written in
-each test; the exact lowering of the SiLU expressions is pinned separately against a Triton probe."""
+each test.  The same operators are compared with the reference's own Triton kernels, in the default mode and at
+the benchmark shapes, in test_vs_reference_triton_gpu.py."""
 import pytest
 import torch
 
