@@ -10,8 +10,9 @@ gradients, E4M3 moments in groups of 128), sharded ZeRO-style over the N GPUs on
 boundaries and followed by the all-gather of the updated bf16 weights.  Total work is fixed, so
 scaling is "strong".  Rank 0 prints ONE JSON line.
 
-`--impl reference` times the CPU restatement of the reference kernel (oracle/, OpenMP over groups) on
-the host cores, on a bounded sample of the same workload.
+`--impl reference` times the reference's optimizer step on the host cores, on a bounded sample of the same
+workload: the C restatement of its kernel (oracle/, OpenMP over groups, every core the process may use) as the
+line's value, and beside it the reference's pure-PyTorch path (oracle/adamw_torch.py).
 """
 import argparse
 import json
@@ -109,10 +110,21 @@ class ClockSampler:
 # CPU baseline / reference arm: the C restatement of the reference kernel on the host cores
 # ------------------------------------------------------------------------------------------------
 
+def host_cores():
+    """Cores this process may run on (not the machine's count: a container or a launcher may have cut it down)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_reference_steps(n_params, min_seconds, min_steps=2, seed=0):
-    """Time oracle.fp8_adamw_expand_step on `n_params` fp32 params; returns (params/s, steps, cores)."""
+    """Time oracle.fp8_adamw_expand_step on `n_params` fp32 params; returns (params/s, steps, seconds, threads).
+    The OpenMP thread count is set explicitly (torch.distributed.run exports OMP_NUM_THREADS=1) and the count in
+    effect is what is reported."""
     import torch
     from oracle import adamw as O
+    threads = O.set_num_threads(host_cores())
     gen = torch.Generator().manual_seed(seed)
     G = (n_params + 127) // 128
     p = torch.randn(n_params, generator=gen) * 0.02
@@ -131,7 +143,48 @@ def cpu_reference_steps(n_params, min_seconds, min_steps=2, seed=0):
         one(2 + steps)
         steps += 1
     dt = time.perf_counter() - t0
-    return n_params * steps / dt, steps, dt, os.cpu_count()
+    return n_params * steps / dt, steps, dt, threads
+
+
+def cpu_pure_pytorch_steps(n_params=4096 * 4096, warmup=1, steps=3, seed=0):
+    """The reference's pure-PyTorch FP8AdamW-expand path (its test's expectation, restated in oracle/adamw_torch.py
+    and pinned to the reference's own output by the CPU tests) on the host cores: 1 warm-up + 3 timed steps on a
+    4096 x 4096 tensor.  Returns {value, unit, cores, kind, sample}."""
+    import torch
+    from oracle import adamw_torch as T
+    threads = host_cores()
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(seed)
+    p = torch.randn(n_params, generator=gen) * 0.02
+    m = torch.randn(n_params, generator=gen) * 1e-3
+    v = (torch.randn(n_params, generator=gen) * 1e-3).square_() + 1e-12
+    grads = [torch.randn(n_params, generator=gen) * 1e-3 for _ in range(2)]
+    for i in range(warmup):
+        T.pure_pytorch_expand_step(p, grads[i & 1], m, v, HYPER["betas"][0], HYPER["betas"][1], HYPER["lr"],
+                                   HYPER["weight_decay"], HYPER["eps"], i)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        T.pure_pytorch_expand_step(p, grads[i & 1], m, v, HYPER["betas"][0], HYPER["betas"][1], HYPER["lr"],
+                                   HYPER["weight_decay"], HYPER["eps"], warmup + i)
+    dt = time.perf_counter() - t0
+    return {"value": n_params * steps / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{steps} steps of one 4096x4096 tensor in {dt:.1f} s after {warmup} warm-up: the reference's "
+                      "pure-PyTorch path (the expectation of its optimizer test, torch fake-quantizer), restated in "
+                      "oracle/adamw_torch.py"}
+
+
+def workload_config(world, exchange, workload="llama2-7b", note=""):
+    """The `config` object of the JSON line; both arms print the same one."""
+    what = ("FP8AdamW-expand step over the full Llama-2-7B parameter set (291 tensors, 6738415616 params)"
+            if workload == "llama2-7b" else "FP8AdamW-expand step over one 4096x4096 tensor (profiling case)")
+    how = {"p2p": " stored by the same kernel into every peer's buffer over NVLink (fused step + all-gather), "
+                  "one-element all-reduce as the closing barrier",
+           "nccl": " + bucketed NCCL all-gather on a side stream", None: ""}[exchange if world > 1 else None]
+    return {"workload": what + ", fp32 master weights, E4M3 moments group 128, bf16 weight copy" + how + note,
+            "parallelism": f"zero-shard x{world} on 128-element group boundaries",
+            "l2": "inputs larger than L2 (>= 10 GB per GPU per step)" if workload == "llama2-7b" else
+                  "inputs larger than L2 (308 MB per step)",
+            "hyper": {"lr": 1e-4, "betas": [0.9, 0.95], "wd": 0.1, "eps": 1e-8, "expand_min": 16}}
 
 
 def run_reference_arm(args):
@@ -142,23 +195,21 @@ def run_reference_arm(args):
     per_step = []
     for _ in range(max(0, args.warmup)):
         cpu_reference_steps(n, 0.0, min_steps=1)
-    t0 = time.perf_counter()
-    total_steps = 0
+    cores = 1
     for _ in range(max(1, args.steps)):
         rate, steps, dt, cores = cpu_reference_steps(n, 1.0, min_steps=1)
         per_step.append(dt / steps)
-        total_steps += steps
     ms = 1e3 * sum(per_step) / len(per_step)
     value = n / (ms / 1e3)
-    sample = (f"one 4096x4096 fp32 tensor (16 777 216 params) per step, C restatement of the reference kernel "
-              f"(oracle/fp8_adamw_oracle.c), OpenMP over groups")
+    sample = ("bounded sample of the workload: one 4096x4096 fp32 tensor (16 777 216 params) per step, C restatement "
+              f"of the reference kernel (oracle/fp8_adamw_oracle.c), OpenMP over groups, {cores} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
-        "config": {"workload": "FP8AdamW-expand step, Llama-2-7B parameter set (bounded CPU sample: one "
-                               "4096x4096 tensor per step)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": workload_config(args.gpus, args.exchange),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                         "pure_pytorch": cpu_pure_pytorch_steps()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
@@ -246,7 +297,7 @@ def e2e_public_api(torch, device, steps, warmup):
 
 
 def quantizer_extras(torch, device, peak):
-    """GB/s of the quantizers on BASELINE.json's activation configuration (8192 tokens x 4096 bf16,
+    """GB/s of the quantizers on the activation benchmark tensor (8192 tokens x 4096 bf16,
     0.1 % of the entries x100): algorithmic bytes / CUDA-event time of the C-ABI calls on preallocated
     outputs, 20 calls replayed from one CUDA graph so that host launch overhead (comparable to these
     15-30 us kernels) stays out of the device time.  The input (64 MB) is smaller than L2, so four
@@ -338,11 +389,12 @@ def quantizer_extras(torch, device, peak):
 
 
 def gemm_extras(torch, device, iters=10):
-    """TFLOP/s of the FP8 GEMM on BASELINE.json's Llama-2-7B MLP shape (8192 tokens, 4096 -> 11008): forward
+    """TFLOP/s of the FP8 GEMM on the Llama-2-7B MLP shape (8192 tokens, 4096 -> 11008): forward
     (E4M3 x E4M3), dgrad and wgrad (E5M2 x E4M3), 2*M*N*K flops each = 0.7388 TFLOP, CUDA-event time of the
     C-ABI call on preallocated outputs.  Operands (45-90 MB each, > 200 MB per GEMM with the output) exceed
-    L2 together.  Fractions are against 2x the measured bf16 GEMM peak of this pool (no FP8 peak was measured
-    by the driver) and against the nominal 4500 dense FP8 TFLOP/s."""
+    L2 together.  Fractions are against a dense FP8 rate measured in the same run (fp8_peak_yardstick: the library's
+    FP8 GEMM at 8192^3, burst and sustained), against 2x the measured bf16 GEMM peak of this pool and against the
+    nominal 4500 dense FP8 TFLOP/s."""
     from coat_b200 import _lib
     L = _lib.lib()
     T, H, I = 8192, 4096, 11008
@@ -364,6 +416,8 @@ def gemm_extras(torch, device, iters=10):
             bf16_sustained = float(peaks.get("bf16_tflops_sustained", bf16_sustained))
     out = {}
     calls = {}
+    yard = fp8_peak_yardstick(torch, device) if iters >= 10 else {"unavailable": "profiling run"}
+    time.sleep(0.5)   # let the clocks recover from the yardstick's sustained loop before the bursts
     for name, a, bm in (("forward_e4m3xe4m3", x, w), ("dgrad_e5m2xe4m3", g, w_t), ("wgrad_e5m2xe4m3", g_t, x_t)):
         M, K = a.shape
         N = bm.shape[0]
@@ -403,6 +457,8 @@ def gemm_extras(torch, device, iters=10):
         tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
         out[name] = {"M": M, "N": N, "K": K, "us": ms * 1e3, "TFLOP/s": tf, "frac_of_2x_measured_bf16": tf / (2 * bf16_peak),
                      "frac_of_nominal_fp8": tf / 4500.0}
+        if "burst_tflops" in yard:
+            out[name]["frac_of_measured_fp8_burst"] = tf / yard["burst_tflops"]
         time.sleep(0.05)
     for name, (call, M, N, K) in calls.items():
         if iters < 10:   # profiling runs ask for a few launches only
@@ -410,6 +466,9 @@ def gemm_extras(torch, device, iters=10):
         tf_sus = 2.0 * M * N * K / (timed(call, 600) / 1e3) / 1e12
         out[name]["TFLOP/s_sustained"] = tf_sus
         out[name]["frac_of_2x_measured_bf16_sustained"] = tf_sus / (2 * bf16_sustained)
+        if "sustained_tflops" in yard:
+            out[name]["frac_of_measured_fp8_sustained"] = tf_sus / yard["sustained_tflops"]
+    out["fp8_peak_yardstick"] = yard
     out["device_status"] = L.coat_fp8_gemm_device_status()
     return out
 
@@ -531,7 +590,7 @@ def layer_extras(torch, device, iters=5):
 
 def fused_extras(torch, device, peak):
     """GB/s of the fused quantize-on-save operators, the norms and the optimizer step without expansion, through the
-    python operator API (the calls the decoder layer makes, with its arguments), on BASELINE.json's shapes:
+    python operator API (the calls the decoder layer makes, with its arguments), on the benchmark shapes:
     8192 tokens x 11008 for the MLP operators, x 4096 for the residual adds and the norms; 4096 x 4096 fp32 for the
     optimizer.  Device time of 10 calls replayed from one CUDA graph (two input sets rotate; every operator moves
     more than L2 holds), median of 7 replays after a quarter of a second of warm-up replays.  Algorithmic bytes = compulsory reads + writes of the operator's
@@ -622,6 +681,138 @@ def fused_extras(torch, device, peak):
     return out
 
 
+def fp8_peak_yardstick(torch, device):
+    """A measured dense FP8 rate to quote the GEMM against: torch._scaled_mm (cuBLASLt) E4M3 x E4M3 -> bf16 at
+    8192^3, best of 10 single launches (burst) and 300 launches back to back (sustained, power-capped).  A library
+    GEMM used as a yardstick only; nothing in the product calls it."""
+    n = 8192
+    a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()   # column-major, as _scaled_mm wants
+    one = torch.tensor(1.0, device=device)
+    try:
+        def call():
+            return torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize(device)
+        best = 1e9
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            torch.cuda.synchronize(device)
+            best = min(best, e0.elapsed_time(e1))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(300):
+            call()
+        e1.record()
+        torch.cuda.synchronize(device)
+        sustained = e0.elapsed_time(e1) / 300
+    except Exception as exc:   # an image without an FP8 library GEMM: fall back to 2x the measured bf16 figures
+        return {"unavailable": str(exc)[:160]}
+    flop = 2.0 * n ** 3
+    return {"how": "torch._scaled_mm e4m3 x e4m3 -> bf16, 8192^3", "burst_tflops": flop / (best / 1e3) / 1e12,
+            "sustained_tflops": flop / (sustained / 1e3) / 1e12}
+
+
+def reference_on_this_gpu(torch, device, peak):
+    """The REFERENCE's own GPU kernels timed on this GPU beside this repository's, same inputs, same harness (python
+    wrappers called back to back, CUDA events, median of 5 rounds of 20 calls after warm-up, which also lets the
+    reference's autotuner settle): its compiled optimizer extension on the 4096 x 4096 tensor, its Triton quantizers
+    on the 8192 x 4096 activation and its Triton FP8 matmul on the Llama-2-7B MLP shapes.  Baseline figures only:
+    taken from the copies staged under oracle/_ref/ (absent -> the entry says so)."""
+    from oracle import ref_loader
+    import coat_b200.activation.real_quantization as mine
+    from coat_b200.optimizer import qoptim_cuda as my_opt
+    out = {}
+
+    def timed(fn, rounds=5, calls=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        times = []
+        for _ in range(rounds):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(calls):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            times.append(e0.elapsed_time(e1) / calls)
+        return sorted(times)[len(times) // 2] * 1e3   # us
+
+    def pair(name, ref_fn, my_fn, unit_work, unit):
+        try:
+            ref_us = timed(ref_fn)
+        except Exception as exc:
+            out[name] = {"reference": f"did not run: {str(exc)[:120]}"}
+            return
+        my_us = timed(my_fn)
+        out[name] = {"reference_us": ref_us, "ours_us": my_us, "speedup": ref_us / my_us,
+                     f"reference_{unit}": unit_work / ref_us, f"ours_{unit}": unit_work / my_us}
+
+    ref_opt = ref_loader.load_ref_qoptim()
+    if ref_opt is None:
+        out["fp8_adamw_expand_4096x4096"] = {"reference": "oracle/_ref/qoptim_cuda.so not built"}
+    else:
+        n = 4096 * 4096
+        gen = torch.Generator(device=device).manual_seed(0)
+
+        def state():
+            return dict(p=torch.randn(n, generator=gen, device=device) * 0.02,
+                        g=torch.randn(n, generator=gen, device=device) * 1e-3,
+                        m=torch.zeros(n, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+                        v=torch.zeros(n, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+                        vec=[torch.zeros(n // 128, device=device), torch.ones(n // 128, device=device),
+                             torch.ones(n // 128, device=device), torch.zeros(n // 128, device=device),
+                             torch.ones(n // 128, device=device), torch.ones(n // 128, device=device)])
+        sa, sb = state(), state()
+        step = [1]
+
+        def run(mod, st):
+            s_m, k_m, r_m, s_v, k_v, r_v = st["vec"]
+            step[0] += 1
+            mod.fp8_adamw_expand_step(st["p"], st["g"], st["m"], s_m, k_m, r_m, st["v"], s_v, k_v, r_v, 0.9, 0.95, 1e-4,
+                                      0.1, 1e-8, step[0], 128, 16)
+        pair("fp8_adamw_expand_4096x4096", lambda: run(ref_opt, sa), lambda: run(my_opt, sb), n / 1e3, "Gparams_per_s")
+
+    ref = ref_loader.load_ref_triton(one_config=False)
+    if ref is None:
+        out["triton_operators"] = {"reference": "oracle/_ref/coat_ref not staged"}
+        return out
+    M, N = 8192, 4096
+    gen = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(M, N, generator=gen, device=device)
+    x = torch.where(torch.rand(M, N, generator=gen, device=device) < 1e-3, x * 100, x).to(torch.bfloat16)
+    qt = ref_loader.ref_module("_quantize_transpose", one_config=False)
+    gb = lambda bytes_per_elem: M * N * bytes_per_elem / 1e3   # -> GB/s when divided by us
+    pair("fp8_quantize_1x16", lambda: ref.fp8_quantize(x, 16, "E4M3"), lambda: mine.fp8_quantize(x, 16, "E4M3"),
+         gb(3.125), "GBps")
+    pair("fp8_quantize_pertensor", lambda: ref.fp8_quantize_pertensor(x, 16, "E4M3"),
+         lambda: mine.fp8_quantize_pertensor(x, 16, "E4M3"), gb(3.125), "GBps")
+    pair("fp8_quantize_pertensor_transpose", lambda: ref.fp8_quantize_pertensor_transpose(x, 16, "E4M3"),
+         lambda: mine.fp8_quantize_pertensor_transpose(x, 16, "E4M3"), gb(4.0), "GBps")
+    pair("fp8_quantize_transpose_1x16", lambda: qt.fp8_quantize_transpose(x, 16, "E4M3"),
+         lambda: mine.fp8_quantize_transpose(x, 16, "E4M3"), gb(4.25), "GBps")
+    T, H, I = 8192, 4096, 11008
+    gen = torch.Generator(device=device).manual_seed(2)
+    X = torch.randn(T, H, generator=gen, device=device).to(torch.bfloat16)
+    W = (torch.randn(I, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    G = (torch.randn(T, I, generator=gen, device=device) * 1e-2).to(torch.bfloat16)
+    qx, sx, qx_t = mine.fp8_quantize_pertensor_transpose(X, 16, "E4M3")
+    qw, sw, qw_t = mine.fp8_quantize_pertensor_transpose(W, 16, "E4M3")
+    qg, sg, qg_t = mine.fp8_quantize_pertensor_transpose(G, 16, "E5M2")
+    tflop = 2.0 * T * H * I / 1e6   # -> TFLOP/s when divided by us
+    pair("fp8_linear_forward_8192x11008x4096", lambda: ref.fp8_linear_forward(qx, sx, qw, sw, False, 16),
+         lambda: mine.fp8_linear_forward(qx, sx, qw, sw, False, 16), tflop, "TFLOPs")
+    pair("fp8_linear_backward_dgrad_and_wgrad",
+         lambda: ref.fp8_linear_backward(qx_t, sx, qg, sg, qg_t, qw_t, sw, 16),
+         lambda: mine.fp8_linear_backward(qx_t, sx, qg, sg, qg_t, qw_t, sw, 16), 2 * tflop, "TFLOPs")
+    return out
+
+
 def run_kernel_workload(args):
     """`--workload quantizers|gemm`: only those kernels, for profiling captures and quick checks."""
     import torch
@@ -636,9 +827,41 @@ def run_kernel_workload(args):
         extras = {"deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
     elif args.workload == "layer":
         extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10)))}
+    elif args.workload == "reference-gpu":
+        extras = {"reference_on_this_gpu": reference_on_this_gpu(torch, device, peak),
+                  "fp8_peak_yardstick": fp8_peak_yardstick(torch, device)}
     else:
         extras = {"fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device, iters=max(1, args.steps))}
     print(json.dumps({"metric": "extras only", "config": {"workload": args.workload}, "extras": extras}), flush=True)
+
+
+def verify_gathered(opt, torch, dist):
+    """After a step at N > 1: does EVERY rank's gathered buffer hold EVERY rank's updated weights?  Each rank
+    checksums bf16(own fp32 shard) per bucket (a position-weighted sum of the bit patterns, int64) and the matching
+    slots of all ranks in its own gathered buffer; the own-shard checksums are all-gathered over NCCL and compared.
+    Returns True only if all slots on all ranks agree."""
+    dev = opt.device
+    W, rank = opt.world_size, opt.rank
+
+    def checksum(t_bf16):
+        bits = t_bf16.contiguous().view(torch.int16).to(torch.int64)
+        weight = (torch.arange(bits.numel(), device=dev, dtype=torch.int64) % 65521) + 1
+        return (bits * weight).sum()
+
+    own, seen = [], []
+    for b in range(opt.n_buckets):
+        lo, hi = int(opt.bounds[b]) * 128, int(opt.bounds[b + 1]) * 128
+        own.append(checksum(opt.param[lo:hi].to(torch.bfloat16)))
+        slots = opt._bucket_all[b].view(W, hi - lo)
+        seen.append(torch.stack([checksum(slots[r]) for r in range(W)]))
+    own = torch.stack(own)                         # [buckets]
+    seen = torch.stack(seen)                       # [buckets, W]
+    everyone = [torch.empty_like(own) for _ in range(W)]
+    dist.all_gather(everyone, own)
+    expected = torch.stack(everyone, dim=1)        # [buckets, W]
+    ok = torch.tensor([int(torch.equal(seen, expected))], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return bool(ok.item())
 
 
 def run_gpu_arm(args):
@@ -719,6 +942,11 @@ def run_gpu_arm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kernel_ms = t.tolist()
     n_launches = args.steps * opt.n_buckets
+    gather_verified = None
+    if world > 1:   # one more full step (the kernel-only steps above exchanged nothing), then compare the buffers
+        one_step()
+        barrier()
+        gather_verified = verify_gathered(opt, torch, dist)
     opt.close()   # collective: unmaps the peers' buffers
 
     # end to end through the public API with host buffers: every rank steps its own copy of one decoder layer
@@ -749,19 +977,15 @@ def run_gpu_arm(args):
             "metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
-            "config": {"workload": ("FP8AdamW-expand step over the full Llama-2-7B parameter set "
-                                    "(291 tensors, 6738415616 params)" if args.workload == "llama2-7b" else
-                                    "FP8AdamW-expand step over one 4096x4096 tensor (profiling case)") +
-                                   ", fp32 master weights, E4M3 moments group 128, "
-                                   "bf16 weight copy" + ({"p2p": " stored by the same kernel into every peer's buffer over NVLink "
-                                                                   "(fused step + all-gather), one-element all-reduce as "
-                                                                   "the closing barrier",
-                                                            "nccl": " + bucketed NCCL all-gather on a side stream",
-                                                            None: ""}[exchange]) + exchange_note,
-                       "parallelism": f"zero-shard x{world} on 128-element group boundaries",
-                       "l2": "inputs larger than L2 (>= 10 GB per GPU per step)" if args.workload == "llama2-7b" else
-                             "inputs larger than L2 (308 MB per step)",
-                       "hyper": {"lr": 1e-4, "betas": [0.9, 0.95], "wd": 0.1, "eps": 1e-8, "expand_min": 16}},
+            "config": workload_config(world, exchange, args.workload, exchange_note),
+            # the step alone (no exchange) and what the exchange adds, so that the scaling of the two can be told apart
+            "step_only": {"value": total / (kernel_ms / 1e3), "unit": UNIT, "ms_per_step": kernel_ms},
+            "exchange": None if world == 1 else {
+                "kind": exchange, "ms_beyond_step": ms - kernel_ms,
+                "bf16_bytes_received_per_gpu": 2 * opt.plan.shard_numel * (world - 1),
+                "link_bound_ms": 2 * opt.plan.shard_numel * (world - 1) / 770e9 * 1e3,
+                "link_rate_note": "770 GB/s per direction per GPU: the peer-copy rate measured on this pool",
+                "gather_verified": gather_verified},
             "roofline": roofline,
             "e2e": {"value": e2e_v, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "workload": f"CoatAdamW.step on one decoder layer ({e2e_n} params) per GPU, grads from pinned "
@@ -776,12 +1000,14 @@ def run_gpu_arm(args):
                               "fused_operators_8192_tokens": fused_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
                               "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device),
-                              "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
+                              "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak),
+                              "reference_on_this_gpu": reference_on_this_gpu(torch, device, peak)}
         if cpu_v is not None:
             line["cpu_baseline"] = {
                 "value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
                 "sample": f"{cpu_steps} steps of one 4096x4096 tensor in {cpu_dt:.1f} s, C restatement of the "
-                          "reference kernel with OpenMP over groups"}
+                          f"reference kernel with OpenMP over groups, {cores} threads",
+                "pure_pytorch": cpu_pure_pytorch_steps()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -793,7 +1019,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled"],
+    ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled", "reference-gpu"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
@@ -802,7 +1028,7 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
-    elif args.workload in ("quantizers", "fused", "gemm", "layer", "blockscaled"):
+    elif args.workload in ("quantizers", "fused", "gemm", "layer", "blockscaled", "reference-gpu"):
         run_kernel_workload(args)
     else:
         run_gpu_arm(args)

@@ -18,6 +18,7 @@ MAX_PEERS = 7            # COAT_MAX_PEERS
 PEER_HANDLE_BYTES = 64   # COAT_PEER_HANDLE_BYTES
 QUANT_IEEE_DIV = 1
 QUANT_STOCHASTIC = 2
+E_BADARG, E_TOOBIG, E_TIMEOUT = -1, -7, -8   # COAT_E_* codes that callers test for
 
 # Default flags of the quantizer entry points: 0 = the reference's (Triton's) division, QUANT_IEEE_DIV
 # = IEEE division.  Tests that compare with the CPU checker switch it.
@@ -61,6 +62,7 @@ SIGNATURES = {
     "coat_fp8_rmsnorm_backward": [_vp] * 9 + [_i, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_quantize_pertensor": [_vp] * 6 + [_i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_quantize_device_status": [],
+    "coat_fp8_quantize_set_barrier_limit": [_i],
     "coat_fp8_layernorm_forward": [_vp] * 9 + [_i64, _i64, _i, _f, _i, _i, _i, _i, _vp],
     "coat_fp8_layernorm_backward": [_vp] * 8 + [_i, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_gemm": [_vp] * 7 + [_i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _i, _vp],

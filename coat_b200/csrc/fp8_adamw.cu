@@ -1088,7 +1088,7 @@ fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
     }
 }
 
-unsigned long long* g_debug_counters = nullptr;
+thread_local unsigned long long* g_debug_counters = nullptr;   // per host thread: only the caller's own launches count
 
 int grid_for(int64_t total_groups) {
     int sms = coat_sm_count();
@@ -1221,7 +1221,7 @@ extern "C" int coat_fp8_adamw_multi_step_bcast(const CoatAdamwTensor* table, con
 
 // Debug aid: six device counters (groups on the fast path, groups on the exact path, iterations of
 // the max/min-candidate loop, iterations of the uncertain-rounding loop, uncertain elements, spare)
-// that later launches add to; pass NULL to switch counting off.  Not thread safe.
+// that later launches FROM THE CALLING HOST THREAD add to; pass NULL to switch counting off.
 extern "C" int coat_fp8_adamw_debug_counters(unsigned long long* device_counters) {
     g_debug_counters = device_counters;
     return COAT_OK;

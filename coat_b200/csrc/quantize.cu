@@ -199,7 +199,8 @@ division_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, const void* __
 #define COAT_PT_FUSED_UNROLL 4
 #endif
 constexpr int kFusedUnroll = COAT_PT_FUSED_UNROLL;
-constexpr int kBarrierLimit = 1 << 20;   // polls of ~0.1-1 us each: about a second, then COAT_E_TIMEOUT
+constexpr int kBarrierLimitDefault = 1 << 20;   // polls of ~0.1-1 us each: about a second, then COAT_E_TIMEOUT
+__device__ int g_barrier_limit = kBarrierLimitDefault;   // lowered only by coat_fp8_quantize_set_barrier_limit (tests)
 
 template <typename T> struct RawSeg;      // one 16-element segment as loaded
 template <> struct RawSeg<float> { uint4 q[4]; };
@@ -252,7 +253,7 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
 }
 
 // All CTAs of a cooperative launch meet here once.  Bounded: returns false (in every thread of the CTA) if the
-// others have not arrived after kBarrierLimit polls.  `word` receives *payload as of the barrier.
+// others have not arrived after g_barrier_limit polls.  `word` receives *payload as of the barrier.
 __device__ __forceinline__ bool grid_barrier_once(unsigned int* counter, const unsigned int* payload, unsigned int* word) {
     __shared__ unsigned int s_payload;
     bool ok = true;
@@ -261,8 +262,9 @@ __device__ __forceinline__ bool grid_barrier_once(unsigned int* counter, const u
         __threadfence();            // this CTA's atomicMax on the payload is ordered before its arrival
         atomicAdd(counter, 1u);
         int tries = 0;
+        const int limit = g_barrier_limit;
         while (ld_acquire_u32(counter) < gridDim.x) {
-            if (++tries > kBarrierLimit) { ok = false; break; }
+            if (++tries > limit) { ok = false; break; }
             __nanosleep(100);
         }
         s_payload = ld_acquire_u32(payload);
@@ -270,6 +272,15 @@ __device__ __forceinline__ bool grid_barrier_once(unsigned int* counter, const u
     ok = __syncthreads_and(ok);
     *word = s_payload;
     return ok;
+}
+
+// Every CTA of a one-launch per-tensor kernel leaves through here exactly once, whether it finished or gave up at a
+// bounded wait: the last one out puts the three sync words back to zero, so a call that timed out leaves the words
+// as clean as a call that did not and the next call on the same words starts from zero.
+__device__ __forceinline__ void pertensor_depart(unsigned int* sync) {
+    if (threadIdx.x == 0 && atomicAdd(&sync[2], 1u) == gridDim.x - 1) {
+        sync[0] = 0u; sync[1] = 0u; sync[2] = 0u;
+    }
 }
 
 #ifndef COAT_PT_FUSED_CTAS
@@ -321,6 +332,7 @@ pertensor_fused_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* _
     unsigned int amax_word;
     if (!grid_barrier_once(&sync[1], &sync[0], &amax_word)) {
         if (threadIdx.x == 0) g_quant_device_status = COAT_E_TIMEOUT;
+        pertensor_depart(sync);
         return;
     }
     const float scale = tensor_scale_from_amax<FMT, IEEE>(&amax_word, scale_dtype);
@@ -348,9 +360,7 @@ pertensor_fused_kernel(const T* __restrict__ x, uint8_t* __restrict__ y, void* _
     }
     // the three words go back to zero for the next call: the last CTA to leave clears them (everyone has passed
     // the barrier and has taken its copy of the amax word by then)
-    if (threadIdx.x == 0 && atomicAdd(&sync[2], 1u) == gridDim.x - 1) {
-        sync[0] = 0u; sync[1] = 0u; sync[2] = 0u;
-    }
+    pertensor_depart(sync);
 }
 
 // =================================================================================================
@@ -631,6 +641,7 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
                     coat_tma::mbar_wait(&full[(use + q) % kTmaStages], (uint32_t)((use + q) / kTmaStages) & 1u, kTmaWaitLimit);
         }
         __syncthreads();
+        if (FUSED) pertensor_depart(sync);
     };
     if (threadIdx.x == 0) {
 #pragma unroll
@@ -772,9 +783,7 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
             }
         }
     }
-    if (FUSED && threadIdx.x == 0 && atomicAdd(&sync[2], 1u) == gridDim.x - 1) {   // last CTA out clears the words
-        sync[0] = 0u; sync[1] = 0u; sync[2] = 0u;
-    }
+    if (FUSED) pertensor_depart(sync);   // last CTA out clears the words
 }
 
 inline bool tma_tiles_fit(int64_t M, int64_t N) {   // tile counts and coordinates are 32-bit in the kernel
@@ -1072,6 +1081,13 @@ extern "C" int coat_fp8_quantize_device_status(void) {
     return v;
 }
 
+// Diagnostic: number of polls a CTA spends at the grid barrier of the one-launch per-tensor kernels before it gives up
+// (on the current device; polls < 0 restores the default of about a second).
+extern "C" int coat_fp8_quantize_set_barrier_limit(int polls) {
+    const int v = polls < 0 ? kBarrierLimitDefault : polls;
+    return cudaMemcpyToSymbol(g_barrier_limit, &v, sizeof(int)) == cudaSuccess ? COAT_OK : COAT_E_LAUNCH;
+}
+
 extern "C" int coat_fp8_quantize_transpose(const void* x, uint8_t* y, void* s_y, uint8_t* y_t, void* s_y_t, int64_t M,
                                            int64_t N, int64_t ldx, int QB, int fmt, int in_dtype, int scale_dtype,
                                            int flags, void* stream) {
@@ -1226,6 +1242,7 @@ struct StaticAmaxArgs {
 extern "C" int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, void* s_out, int64_t M,
                                                   int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
                                                   int flags, void* stream) {
+    if (flags & COAT_QUANT_STOCHASTIC) return COAT_E_BADARG;   // round-to-nearest only: rejected, not ignored
     if (M == 0 || N == 0) return COAT_OK;
     if (!x || (!y && !y_t) || !s_out || !scale_dtype_ok(scale_dtype)) return COAT_E_BADARG;
     if (int rc = check_2d(x, M, N, ldx, in_dtype, 16)) return rc;

@@ -276,13 +276,27 @@ class CoatAdamW(Optimizer):
                              prefix=torch.from_numpy(prefix).to(device), total=int(prefix[-1]))
                 self._tables[key] = entry
             rows = entry["rows"]
+            changed = []
             for row, i in enumerate(idxs):
                 g = params[i].grad
                 if g.dtype != params[i].dtype or not g.is_contiguous():
                     raise RuntimeError("gradients must be contiguous and match the parameter dtype")
-                rows[row]["g"] = g.data_ptr()
-                rows[row]["p"] = params[i].data_ptr()
-            entry["dev"].copy_(entry["host"], non_blocking=True)
+                gp, pp = g.data_ptr(), params[i].data_ptr()
+                if rows[row]["g"] != gp or rows[row]["p"] != pp:
+                    changed.append((row, gp, pp))
+            if changed:
+                # The pinned table is the source of an asynchronous copy: it may be rewritten only once the copy
+                # queued by an earlier step has read it (the host can run a step ahead of the GPU, and with
+                # zero_grad(set_to_none=True) gradients come back at new addresses).  Unchanged pointers need no copy.
+                if entry.get("copied") is not None:
+                    entry["copied"].synchronize()
+                for row, gp, pp in changed:
+                    rows[row]["g"] = gp
+                    rows[row]["p"] = pp
+                with torch.cuda.device(device):
+                    entry["dev"].copy_(entry["host"], non_blocking=True)
+                    entry["copied"] = torch.cuda.Event()
+                    entry["copied"].record(torch.cuda.current_stream(device))
             with torch.cuda.device(device):
                 rc = _lib.lib().coat_fp8_adamw_multi_step(
                     entry["dev"].data_ptr(), entry["prefix"].data_ptr(), len(idxs), entry["total"],

@@ -1,9 +1,12 @@
 /*
  * coat_b200 — C ABI of the B200-native (sm_100a) COAT quantization hot path.
  *
- * Every entry point takes raw device pointers, sizes, dtype enums and a CUDA
- * stream (passed as void*, a cudaStream_t), allocates nothing, launches
+ * Every compute entry point takes raw device pointers, sizes, dtype enums and a
+ * CUDA stream (passed as void*, a cudaStream_t), allocates nothing, launches
  * asynchronously on that stream and returns 0 or a negative COAT_E_* code.
+ * The only entry points that allocate are the set-up helpers of the sharded
+ * optimizer step, coat_peer_buffer_create / _open (cudaMalloc and CUDA IPC,
+ * outside any step); the status getters synchronise.
  * No C++ or torch types cross this boundary.  Tensors are dense row-major
  * unless a stride is passed explicitly.
  *
@@ -198,8 +201,14 @@ int coat_fp8_quantize_pertensor(const void* x, uint8_t* y, uint8_t* y_t, void* s
                                 int in_dtype, int scale_dtype, int flags, void* stream);
 
 /* Synchronises, returns and clears the quantizers' device status word (COAT_E_TIMEOUT if a bounded wait on a
- * staging copy or at the grid barrier ran out; never expected). */
+ * staging copy or at the grid barrier ran out; never expected).  A call that timed out has written wrong
+ * codes, but it leaves the sync words of coat_fp8_quantize_pertensor zero like any other call. */
 int coat_fp8_quantize_device_status(void);
+
+/* Diagnostic (no counterpart in the reference): how many polls a CTA of the one-launch per-tensor kernels spends
+ * at their grid barrier before it gives up, on the current device; polls < 0 restores the default (about one
+ * second).  The tests lower it to 0 to see a timeout reported and healed without making any GPU wait. */
+int coat_fp8_quantize_set_barrier_limit(int polls);
 
 /* One pass: 1x16 groups along the rows -> (y, s_y[M, N/16]) and 1x16 groups of the transposed matrix
  * (16 consecutive rows of one column) -> (y_t[N, M], s_y_t[N, M/16]).  QB must be 16, M a multiple of 16.
@@ -225,7 +234,8 @@ int coat_fp8_dequantize(const uint8_t* x, const void* s_x, void* y_bf16, int64_t
  * (COAT_E_TOOBIG beyond that).  All calls on a device share that array: back-to-back calls on one
  * stream are fine, calls that overlap on the GPU race.  The first call on a device queries the array's
  * address and should be made before any stream capture starts.  Results are identical to
- * coat_fp8_group_scales_amax + coat_fp8_division.  y or y_t may be NULL (not both). */
+ * coat_fp8_group_scales_amax + coat_fp8_division.  y or y_t may be NULL (not both).  Round-to-nearest only:
+ * COAT_QUANT_STOCHASTIC in flags is rejected with COAT_E_BADARG. */
 int coat_fp8_quantize_pertensor_static(const void* x, uint8_t* y, uint8_t* y_t, void* s_out, int64_t M,
                                        int64_t N, int64_t ldx, int fmt, int in_dtype, int scale_dtype,
                                        int flags, void* stream);
@@ -393,7 +403,7 @@ int coat_rope_bf16(const void* x, int64_t sxb, int64_t sxs, int64_t sxh, const v
 
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).
- * coat_fp8_adamw_debug_counters: later launches add to 8 device counters (uint64): groups on the guarded
+ * coat_fp8_adamw_debug_counters: later launches made by the calling host thread add to 8 device counters (uint64): groups on the guarded
  *   fast path, groups on the exact path, exactly recomputed max/min candidates, exactly recomputed
  *   roundings, -, -, and (as float bit patterns in the low 32 bits) the largest observed fraction of the
  *   modelled error bound actually used by the first / second moment.  NULL switches counting off.

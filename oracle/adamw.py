@@ -43,6 +43,9 @@ def lib():
         _lib.oracle_decode_fp8.argtypes = [vp, vp, i64, i]
         _lib.oracle_float_to_bf16.argtypes = [f]
         _lib.oracle_float_to_bf16.restype = ctypes.c_uint16
+        _lib.oracle_set_num_threads.argtypes = [i]
+        _lib.oracle_set_num_threads.restype = None
+        _lib.oracle_max_threads.restype = i
     return _lib
 
 
@@ -103,3 +106,9 @@ def decode_fp8(c, fmt="E4M3"):
     out = torch.empty(c.shape, dtype=torch.float32)
     lib().oracle_decode_fp8(_ptr(c), _ptr(out), c.numel(), 0 if fmt == "E4M3" else 1)
     return out
+
+
+def set_num_threads(n):
+    """Use `n` OpenMP threads in the step functions, whatever OMP_NUM_THREADS says; returns the count in effect."""
+    lib().oracle_set_num_threads(int(n))
+    return int(lib().oracle_max_threads())

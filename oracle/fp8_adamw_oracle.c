@@ -25,6 +25,9 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define QGROUP 128
 #define WARPSIZE 32
@@ -301,4 +304,24 @@ void oracle_encode_fp8(const float* x, uint8_t* out, int64_t n, int fmt) {
 }
 void oracle_decode_fp8(const uint8_t* c, float* out, int64_t n, int fmt) {
     for (int64_t i = 0; i < n; ++i) out[i] = fmt == 0 ? oracle_e4m3_to_float(c[i]) : oracle_e5m2_to_float(c[i]);
+}
+
+
+/* Number of OpenMP threads the step functions above use: set it explicitly (a launcher may have exported
+ * OMP_NUM_THREADS=1 into the environment) and read back what the runtime will actually use.  Without OpenMP
+ * both report one thread. */
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
 }

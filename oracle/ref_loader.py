@@ -1,0 +1,77 @@
+"""Access to the staged reference (TEST / BASELINE INFRASTRUCTURE ONLY): the reference's compiled optimizer extension
+and its Triton operator layer, as oracle/build_ref.py put them into oracle/_ref/.  Used by the tests (as the
+checker) and by bench.py's "reference on this GPU" baseline figures; never by the product package."""
+import importlib
+import os
+import sys
+
+REF_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref")
+_PKG = "coat_ref.activation.real_quantization"
+_loaded = {}
+
+
+def load_ref_qoptim():
+    """The reference's `qoptim_cuda` module built into oracle/_ref, or None."""
+    so = os.path.join(REF_DIR, "qoptim_cuda.so")
+    if not os.path.exists(so):
+        return None
+    import torch  # noqa: F401  (the extension links against torch)
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        return importlib.import_module("qoptim_cuda")
+    except Exception:
+        return None
+
+
+def _one_config(obj, seen):
+    """Walk a Triton kernel wrapper chain (Heuristics -> Autotuner -> JITFunction) and keep ONE of the
+    autotuner's own candidate configurations, so that nothing is benchmarked: every candidate computes
+    the same values (the kernels reduce with max only, tile by tile), the choice only affects speed.
+    The smallest tile of the list is kept (least register pressure, quickest to compile)."""
+    from triton.runtime.autotuner import Autotuner
+    while obj is not None and id(obj) not in seen:
+        seen.add(id(obj))
+        if isinstance(obj, Autotuner) and len(obj.configs) > 1:
+            def area(c):
+                kw = c.kwargs
+                return kw.get("BLOCK_M", 1) * kw.get("BLOCK_N", 1), c.num_warps, c.num_stages
+            obj.configs = [min(obj.configs, key=area)]
+        obj = getattr(obj, "fn", None)
+
+
+def load_ref_triton(one_config=True):
+    """The reference's operator layer (its Triton kernels and python wrappers) as staged into
+    oracle/_ref/coat_ref/, or None when it has not been staged.  GPU only.  one_config=True (the parity tests)
+    restricts every autotuned kernel to one of its own candidate configurations; one_config=False (timing) leaves
+    the reference's autotuning as it is.  The first call in a process decides."""
+    if "mod" in _loaded:
+        return _loaded["mod"]
+    pkg = os.path.join(REF_DIR, "coat_ref", "activation", "real_quantization")
+    if not os.path.isdir(pkg):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    mod = importlib.import_module(_PKG)
+    if one_config:
+        seen = set()
+        for name in sorted(os.listdir(pkg)):
+            if not name.endswith(".py") or name == "__init__.py":
+                continue
+            try:
+                sub = importlib.import_module(f"{_PKG}.{name[:-3]}")
+            except Exception:
+                continue
+            for val in list(vars(sub).values()):
+                for k in (val.values() if isinstance(val, dict) else (val,)):
+                    if hasattr(k, "fn"):
+                        _one_config(k, seen)
+    _loaded["mod"] = mod
+    return mod
+
+
+def ref_module(name, one_config=True):
+    """A submodule of the staged reference package, e.g. ref_module('_quantize_transpose')."""
+    if load_ref_triton(one_config) is None:
+        return None
+    return importlib.import_module(f"{_PKG}.{name}")

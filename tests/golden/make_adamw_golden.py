@@ -76,7 +76,9 @@ def run_case(ref_root, seed, shape, positive):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("COAT_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("usage: python " + sys.argv[0] + " /path/to/reference   (or COAT_REFERENCE_ROOT)")
     sys.path.insert(0, ref_root)
     blob = {}
     for name, seed, shape, positive in CASES:

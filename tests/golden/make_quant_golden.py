@@ -16,7 +16,9 @@ import torch
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("COAT_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("usage: python " + sys.argv[0] + " /path/to/reference   (or COAT_REFERENCE_ROOT)")
     sys.path.insert(0, ref_root)
     src = open(os.path.join(ref_root, "tests", "test_utils.py")).read().replace(".cuda()", "")
     ns = {"__name__": "reference_test_utils"}

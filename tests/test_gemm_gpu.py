@@ -111,7 +111,7 @@ def test_fp8linear_module_trains():
 
 
 def test_llama_mlp_shapes_sampled():
-    """BASELINE.json configuration 3 at full size (8192 x 4096 x 11008, forward, dgrad with E5M2 gradients,
+    """The FP8 linear benchmark configuration at full size (8192 x 4096 x 11008, forward, dgrad with E5M2 gradients,
     wgrad); checked on 64 sampled rows against the fp64 product."""
     linear, _lib = mods()
     M, H, I = 8192, 4096, 11008

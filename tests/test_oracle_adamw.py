@@ -176,3 +176,26 @@ def test_plain_step_scale_is_amax_over_448():
     assert torch.equal(st["s_m"], (amax.double() + 1e-20).float() / 448)
     deq = O.decode_fp8(st["m"]) * st["s_m"].repeat_interleave(128)
     assert (deq - m1).abs().max() <= amax.max() / 16  # E4M3 keeps 3 mantissa bits
+
+
+@pytest.mark.parametrize("case", ["ref_seed0_2x128", "seed1_2x128_pos", "seed2_8x128_pos", "seed3_64x128_pos"])
+def test_pure_pytorch_restatement_equals_the_reference_expectation(case):
+    """oracle/adamw_torch.py (the pure-PyTorch path bench.py times on the host cores) against what the reference's
+    own test text computes (tests/golden/make_adamw_golden.py): every output identical, NaNs included."""
+    import numpy as np
+    from oracle import adamw_torch as T
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "adamw_expand_golden.npz"))
+    inp = lambda k: torch.from_numpy(g[f"{case}/in/{k}"].copy())
+    hyp = lambda k: float(g[f"{case}/hyper/{k}"])
+    out = lambda k: torch.from_numpy(g[f"{case}/out/{k}"].copy())
+    p, gr = inp("params").flatten().clone(), inp("grads").flatten()
+    m = T.dequantize_state(inp("exp_avg"), inp("scale_exp_avg"), inp("expand_exp_avg"), inp("sqrtminmax_exp_avg"))
+    v = T.dequantize_state(inp("exp_avg_sq"), inp("scale_exp_avg_sq"), inp("expand_exp_avg_sq"),
+                           inp("sqrtminmax_exp_avg_sq"))
+    got = T.pure_pytorch_expand_step(p, gr, m, v, hyp("beta1"), hyp("beta2"), hyp("lr"), hyp("wd"), hyp("eps"),
+                                     int(hyp("step")))
+    names = dict(q_m="Qexp_avg_py", s_m="Sexp_avg_py", k_m="B1Exp", r_m="block_sqrt_minmax1", q_v="Qexp_avg_sq_py",
+                 s_v="Sexp_avg_sq_py", k_v="B2Exp", r_v="block_sqrt_minmax2")
+    for mine, ref in list(names.items()) + [(None, "params_py")]:
+        a, b = (p if mine is None else got[mine]), out(ref)
+        assert bool(((a == b) | (a.isnan() & b.isnan())).all()), (case, ref)

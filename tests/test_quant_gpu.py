@@ -287,6 +287,35 @@ def test_one_launch_pertensor_many_trips_equals_two_pass():
     assert _lib.lib().coat_fp8_quantize_device_status() == 0
 
 
+@pytest.mark.parametrize("transposed", [False, True])
+def test_one_launch_pertensor_timeout_is_reported_and_heals(transposed):
+    """The grid barrier of the one-launch kernels is bounded.  With the bound lowered to zero polls (a diagnostic
+    switch; nothing waits, nothing hangs) the first CTAs to arrive give up: the status word must read
+    COAT_E_TIMEOUT, the sync words must be back at zero, and the next call with the normal bound on the SAME sync
+    words must give the right result."""
+    r, _ = ops()
+    from coat_b200 import _lib
+    from coat_b200.activation.real_quantization import _ops
+    L = _lib.lib()
+    x = make_x(2048, 1024, seed=5).cuda()
+    fn = (lambda: r.fp8_quantize_pertensor_transpose(x, 16, "E4M3")) if transposed else \
+         (lambda: r.fp8_quantize_pertensor(x, 16, "E4M3"))
+    good = fn()
+    assert L.coat_fp8_quantize_device_status() == 0
+    words = _ops._sync_words(x.device)[1]
+    assert L.coat_fp8_quantize_set_barrier_limit(0) == 0
+    try:
+        fn()
+        assert L.coat_fp8_quantize_device_status() == _lib.E_TIMEOUT
+    finally:
+        assert L.coat_fp8_quantize_set_barrier_limit(-1) == 0
+    assert words.tolist()[:3] == [0, 0, 0], "a call that timed out must leave the sync words clean"
+    again = fn()
+    assert L.coat_fp8_quantize_device_status() == 0
+    for a, b in zip(good, again):
+        assert torch.equal(a.view(torch.uint8) if a.dtype.itemsize == 1 else a, b.view(torch.uint8) if b.dtype.itemsize == 1 else b)
+
+
 def test_one_launch_transposed_falls_back_for_ragged_row_counts():
     """M not a multiple of 16: the operator takes the two-call path; results agree with the straight one-launch kernel."""
     r, _ = ops()

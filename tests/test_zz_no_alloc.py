@@ -59,3 +59,15 @@ def test_static_scratch_variant_rejects_oversized_input():
     assert rc == -7   # COAT_E_TOOBIG
     with pytest.raises(RuntimeError, match="maximum"):
         _lib.check(rc, "quantize_pertensor_static")
+
+
+def test_static_scratch_variant_rejects_stochastic_rounding():
+    """Round-to-nearest only: the stochastic flag is refused (COAT_E_BADARG), not silently dropped."""
+    from coat_b200 import _lib
+    x = torch.zeros(16, 64, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(16, 64, dtype=torch.uint8, device="cuda")
+    s = torch.empty((), dtype=torch.bfloat16, device="cuda")
+    rc = _lib.lib().coat_fp8_quantize_pertensor_static(x.data_ptr(), y.data_ptr(), None, s.data_ptr(), 16, 64, 64,
+                                                       _lib.E4M3, _lib.BF16, _lib.BF16, _lib.QUANT_STOCHASTIC,
+                                                       _lib.stream_ptr(x.device))
+    assert rc == _lib.E_BADARG
