@@ -431,12 +431,21 @@ struct StepConsts {
 
 __device__ __forceinline__ bool sane_pos(float x) { return x >= kSaneLo && x <= kSaneHi; }
 
-// Relative error bound of  ex2(lg2(c*s) * ik) * r  against libdevice powf(c*s, ik) * r, for any
-// E4M3 magnitude c in [2^-9, 448]; lgs = lg2(s) (approximate is fine, 1e-3 is added).
+// Relative error bound of the approximate dequantisation  ex2(fma(L[c], ik, c0)) * r  against the reference's
+// fl(powf(fl(c*s), ik) * r), for any E4M3 magnitude c in [2^-9, 448], where L[c] is the table of correctly rounded
+// lg2(c) (|error| <= 2^-22: |lg2 c| < 8 except the exact entries -9 and -8), lgs = lg2.approx(s) and
+// c0 = fl(lgs * ik).  Absolute error of the exponent handed to ex2:
+//     ik * 2^-22                      table entry
+//   + ik * max(|lgs|, 1) * 2^-22      lg2.approx(s) (relative 2^-22 outside [0.5, 2], absolute 2^-22 inside)
+//   + 2^-24 * (|c0| + |t|)            the two roundings, |c0| <= ik |lgs|, |t| <= ik (9 + |lgs|) =: tb
+// times ln 2 as a relative error of the power; plus ik * 2^-24 for the reference's rounded product c*s, ex2.approx,
+// the deviation allowed to libdevice's powf, and the rounded multiplication by r.  lgs may be off by its own error
+// in this bound: 1e-3 is added.
 __device__ __forceinline__ float fast_dequant_eps(float ik, float lgs, float& tb) {
-    float lb = 9.0f + fabsf(lgs) + 1e-3f;          // |lg2(c*s)| <= lb
-    tb = ik * lb;                                   // |exponent handed to ex2| <= tb
-    return kSafety * (kLn2 * tb * (kLgErr + k2m24) + kEx2Err + kPowDev + k2m23);
+    const float al = fabsf(lgs) + 1e-3f;
+    tb = ik * (9.0f + al);                          // |exponent handed to ex2| <= tb
+    const float e_exp = ik * kLgErr * (1.0f + fmaxf(al, 1.0f)) + k2m24 * (ik * al + tb);
+    return kSafety * (kLn2 * e_exp + ik * k2m24 + kEx2Err + kPowDev + k2m23);
 }
 
 template <int N>
@@ -493,7 +502,10 @@ constexpr int kTile = COAT_ADAMW_TILE;
 constexpr int kTiledThreads = COAT_ADAMW_TILED_THREADS;
 constexpr int kTiledWarps = kTiledThreads / COAT_WARP;
 constexpr int kCandPerGroup = 16;
-constexpr int kPendCap = 64;
+#ifndef COAT_ADAMW_PEND_CAP
+#define COAT_ADAMW_PEND_CAP 32
+#endif
+constexpr int kPendCap = COAT_ADAMW_PEND_CAP;
 constexpr float kTiny = 7.8886091e-31f;   // 2^-100: below this the flush-to-zero MUFU forms lose accuracy
 
 struct __align__(16) WarpTile {
@@ -507,6 +519,7 @@ struct __align__(16) WarpTile {
     float old_sc[kTile][8];      // s_m, 1/k_m, r_m, eps_dm, s_v, 1/k_v, r_v, eps_dv
     float newc[kTile][2][8];     // r', k', s', 1/r', scale_lo, scale_hi, D (first moment), in-range flag
     float delta[kTile][2];       // absolute error bound of |m'| and of v' in this group
+    float c0[kTile][2];          // lg2(s) / k of the stored scale and exponent, per moment: the constant part of the dequantisation's exponent
     uint32_t stat[kTile][4];     // exact max m, min m, max v, min v (float bit patterns)
     unsigned long long ptr_p[kTile], ptr_g[kTile], ptr_m[kTile], ptr_v[kTile], ptr_bf[kTile];
     long long local[kTile];      // group index inside its tensor
@@ -563,19 +576,17 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 
 __device__ int g_adamw_device_status = 0;   // set to COAT_E_TIMEOUT if a bounded wait ran out
 
-// Magnitudes of four packed E4M3 codes as floats, without the conversion unit: the 7 magnitude bits of a
-// code, placed at bit 20 of a float, read as 2^(e-127)*1.mmm (or as the float subnormal 0.mmm*2^-126 when
-// e == 0), which is the code's value times 2^-120 in both cases; the multiplication by 2^120 is exact.
-// A NaN code (0x7f) would come out as 480: the caller rejects words that contain one (has_nan_code).
-__device__ __forceinline__ void e4m3x4_magnitudes(uint32_t w, float (&f)[4]) {
-    const float k2p120 = 1.3292279957849159e36f;
-    f[0] = __uint_as_float((w << 20) & 0x07f00000u) * k2p120;
-    f[1] = __uint_as_float((w << 12) & 0x07f00000u) * k2p120;
-    f[2] = __uint_as_float((w << 4) & 0x07f00000u) * k2p120;
-    f[3] = __uint_as_float((w >> 4) & 0x07f00000u) * k2p120;
+// lg2 of the magnitudes of four packed E4M3 codes, from a 128-entry table in shared memory (entry 0 = -inf: the
+// code zero dequantises to zero; entry 127 = NaN: a NaN code surfaces as a NaN moment and sends its group to the
+// exact path).  One shift, one mask and one shared load per code in place of a conversion, a multiplication and
+// a lg2 on the transcendental unit.
+__device__ __forceinline__ void e4m3x4_lg2(const float* lut, uint32_t w, float (&f)[4]) {
+    const char* base = reinterpret_cast<const char*>(lut);
+    f[0] = *reinterpret_cast<const float*>(base + ((w << 2) & 0x1fcu));
+    f[1] = *reinterpret_cast<const float*>(base + ((w >> 6) & 0x1fcu));
+    f[2] = *reinterpret_cast<const float*>(base + ((w >> 14) & 0x1fcu));
+    f[3] = *reinterpret_cast<const float*>(base + ((w >> 22) & 0x1fcu));
 }
-// non-zero iff one of the four bytes has magnitude bits 0x7f
-__device__ __forceinline__ uint32_t has_nan_code(uint32_t w) { return ((w & 0x7f7f7f7fu) + 0x01010101u) & 0x80808080u; }
 
 __device__ __forceinline__ float lg2_ftz(float x) { float r; asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ float ex2_ftz(float x) { float r; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
@@ -641,7 +652,7 @@ __device__ __noinline__ void queue_exact(WarpTile& w, int slot, int lane, uint32
 
 // Shared memory, not registers, limits how many CTAs share an SM; telling the compiler so lets it use the
 // registers that occupancy leaves free instead of spilling.
-constexpr size_t kTiledSmem = kTiledWarps * (sizeof(WarpTile) + kGroup * sizeof(float));
+constexpr size_t kTiledSmem = kTiledWarps * sizeof(WarpTile);
 // The broadcast variant stages a tile's bf16 weights (256 bytes per group) per warp behind everything else,
 // and sends them to this GPU's buffer and to every peer's with bulk stores of up to a whole tile.
 constexpr size_t kBcastStageBytes = kTile * kGroup * sizeof(__nv_bfloat16);
@@ -651,7 +662,7 @@ constexpr size_t kTiledSmemBcast = kTiledSmem + kTiledWarps * kBcastStageBytes;
 // chain was most of the latency of a tile's set-up.
 constexpr int kPrefixCap = 512;
 constexpr int tiled_ctas_per_sm(bool bcast) {
-    return (int)((227 * 1024) / ((bcast ? kTiledSmemBcast : kTiledSmem) + 1024 + kPrefixCap * sizeof(int)));
+    return (int)((227 * 1024) / ((bcast ? kTiledSmemBcast : kTiledSmem) + 1024 + kPrefixCap * sizeof(int) + 128 * sizeof(float)));
 }
 static_assert(kTiledSmem % 16 == 0 && kBcastStageBytes % 16 == 0, "bulk copies need 16-byte aligned staging");
 
@@ -664,7 +675,6 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     WarpTile& w = reinterpret_cast<WarpTile*>(smem_raw)[warp];
-    float* smem_min = reinterpret_cast<float*>(smem_raw + kTiledWarps * sizeof(WarpTile)) + warp * kGroup;
     uint2* bf_stage = reinterpret_cast<uint2*>(smem_raw + kTiledSmem + warp * kBcastStageBytes);   // BCAST only
     typedef Elem4<scalar_t> E;
 
@@ -682,10 +692,14 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     unsigned long long n_fast = 0, n_exact = 0, n_cand_total = 0, n_pend_total = 0;
     __shared__ int s_prefix[MULTI ? kPrefixCap : 1];
     const bool prefix_cached = MULTI && n_tensors <= kPrefixCap && total_groups < (1ll << 31);
-    if (prefix_cached) {
+    if (prefix_cached)
         for (int i = threadIdx.x; i < n_tensors; i += kTiledThreads) s_prefix[i] = (int)group_prefix[i];
-        __syncthreads();
-    }
+    // lg2 of every E4M3 magnitude, correctly rounded (through double): see e4m3x4_lg2
+    __shared__ float s_lg2[128];
+    for (int i = threadIdx.x; i < 128; i += kTiledThreads)
+        s_lg2[i] = i == 127 ? __int_as_float(0x7fffffff)
+                            : (i == 0 ? -kInf : (float)log2((double)coat_e4m3_to_float((uint8_t)i)));
+    __syncthreads();
     if (lane == 0) {
         w.n_pend = 0;
         w.n_cand = 0;
@@ -770,8 +784,11 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             const float s_m = t.s_m[group], r_m = t.r_m[group], s_v = t.s_v[group], r_v = t.r_v[group];
             const float ik_m = __fdiv_rn(1.0f, t.k_m[group]), ik_v = __fdiv_rn(1.0f, t.k_v[group]);
             float tb_m, tb_v;
-            const float eps_dm = fast_dequant_eps(ik_m, fast_lg2(s_m), tb_m);
-            const float eps_dv = fast_dequant_eps(ik_v, fast_lg2(s_v), tb_v);
+            const float lgs_m = fast_lg2(s_m), lgs_v = fast_lg2(s_v);
+            const float eps_dm = fast_dequant_eps(ik_m, lgs_m, tb_m);
+            const float eps_dv = fast_dequant_eps(ik_v, lgs_v, tb_v);
+            w.c0[lane][0] = __fmul_rn(lgs_m, ik_m);
+            w.c0[lane][1] = __fmul_rn(lgs_v, ik_v);
             const bool ok = sane_pos(s_m) && sane_pos(r_m) && sane_pos(s_v) && sane_pos(r_v) && ik_m >= 0.015625f &&
                             ik_m <= 64.0f && ik_v >= 0.015625f && ik_v <= 64.0f && tb_m <= 60.0f && tb_v <= 60.0f;
             float* sc = w.old_sc[lane];
@@ -808,18 +825,19 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 float xm[4], xv[4], m1[4], v1[4];
                 const float4 sa = reinterpret_cast<const float4*>(w.old_sc[slot])[0];   // s_m, 1/k_m, r_m, eps_dm
                 const float4 sb = reinterpret_cast<const float4*>(w.old_sc[slot])[1];   // s_v, 1/k_v, r_v, eps_dv
-                e4m3x4_magnitudes(mw, xm);
-                e4m3x4_magnitudes(vw, xv);
-                // a NaN code, or a negative second-moment code, sends the group to the exact path (via the NaN
-                // that max_nan carries into the group maximum)
-                float mx_a = (has_nan_code(mw) | has_nan_code(vw) | (vw & 0x80808080u)) ? __int_as_float(0x7fffffff) : 0.f;
+                e4m3x4_lg2(s_lg2, mw, xm);
+                e4m3x4_lg2(s_lg2, vw, xv);
+                const float c0_m = w.c0[slot][0], c0_v = w.c0[slot][1];
+                // a negative second-moment code sends the group to the exact path (via the NaN that max_nan carries
+                // into the group maximum); a NaN code arrives as a NaN moment through the table
+                float mx_a = (vw & 0x80808080u) ? __int_as_float(0x7fffffff) : 0.f;
                 float mn_a = kInf, mx_am = 0.f, mx_v = 0.f, mn_v = kInf;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float xmj = xm[j] * sa.x, xvj = xv[j] * sb.x;   // magnitudes; the sign is applied below
-                    const float mt = __uint_as_float(__float_as_uint(ex2_ftz(lg2_ftz(xmj) * sa.y) * sa.z) |
+                    // |m| = (c s)^(1/k) r = ex2(lg2(c) / k + lg2(s) / k) r; the sign of the code is put back on
+                    const float mt = __uint_as_float(__float_as_uint(ex2_ftz(__fmaf_rn(xm[j], sa.y, c0_m)) * sa.z) |
                                                      ((mw << (24 - 8 * j)) & 0x80000000u));
-                    const float vt = ex2_ftz(lg2_ftz(xvj) * sb.y) * sb.z;
+                    const float vt = ex2_ftz(__fmaf_rn(xv[j], sb.y, c0_v)) * sb.z;
                     m1[j] = adam_first(h.beta1, mt, c.om_beta1, g[j]);
                     v1[j] = adam_second(h.beta2, vt, c.om_beta2, g[j]);
                     const float a1 = fabsf(m1[j]);
@@ -891,8 +909,11 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             }
             if (!ok) {
                 const TensorDesc& t = MULTI ? table[w.ti[slot]] : single;
+                // scratch of the exact minimum tree (128 floats): this slot's gradient staging, which a group that
+                // leaves the fast path no longer needs (the exact routine reads its inputs from global memory)
                 process_group_exact<scalar_t, true, BCAST>(t, w.local[slot], lane, h, c.om_beta1, c.om_beta2, c.correction1,
-                                                    c.correction2_sqrt, desc_vec_ok(t, E::kVecAlign), smem_min);
+                                                    c.correction2_sqrt, desc_vec_ok(t, E::kVecAlign),
+                                                    reinterpret_cast<float*>(&w.v1[slot][0]));
                 ++n_exact;
             }
         }
@@ -1018,7 +1039,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             reinterpret_cast<uint32_t*>(code_m)[lane] = cm;
             reinterpret_cast<uint32_t*>(code_v)[lane] = cv;
             __syncwarp();
-            if (w.n_pend >= 32u) { PHASE_CLOCK(4); flush_pending<scalar_t>(w, lane, h, c); PHASE_CLOCK(5); }
+            if (w.n_pend >= (uint32_t)(kPendCap < 32 ? kPendCap : 32)) { PHASE_CLOCK(4); flush_pending<scalar_t>(w, lane, h, c); PHASE_CLOCK(5); }
         }
         PHASE_CLOCK(4);
     }
