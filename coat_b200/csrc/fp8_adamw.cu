@@ -516,7 +516,7 @@ struct __align__(16) WarpTile {
     float4 v1[kTile][32];        // g on arrival
     uint32_t cw_m[kTile][32];
     uint32_t cw_v[kTile][32];
-    float old_sc[kTile][8];      // s_m, 1/k_m, r_m, eps_dm, s_v, 1/k_v, r_v, eps_dv
+    float old_sc[kTile][8];      // s_m, 1/k_m, r_m, eps_dm * max|beta1 m~|, s_v, 1/k_v, r_v, eps_dv
     float newc[kTile][2][8];     // r', k', s', 1/r', scale_lo, scale_hi, D (first moment), in-range flag
     float delta[kTile][2];       // absolute error bound of |m'| and of v' in this group
     float c0[kTile][2];          // lg2(s) / k of the stored scale and exponent, per moment: the constant part of the dequantisation's exponent
@@ -792,7 +792,12 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             const bool ok = sane_pos(s_m) && sane_pos(r_m) && sane_pos(s_v) && sane_pos(r_v) && ik_m >= 0.015625f &&
                             ik_m <= 64.0f && ik_v >= 0.015625f && ik_v <= 64.0f && tb_m <= 60.0f && tb_v <= 60.0f;
             float* sc = w.old_sc[lane];
-            sc[0] = s_m; sc[1] = ik_m; sc[2] = r_m; sc[3] = eps_dm; sc[4] = s_v; sc[5] = ik_v; sc[6] = r_v; sc[7] = eps_dv;
+            // largest |beta1 * m~| any code of the group can dequantise to (the code 448; the dequantisation is monotone
+            // in the code's magnitude, 2^-20 covers the approximation's own wobble), times the relative bound: the
+            // absolute error the first moment inherits from the dequantisation
+            const float mam = fabsf(h.beta1) * (ex2_ftz(__fmaf_rn(8.8073549f /* lg2 448 */, ik_m, w.c0[lane][0])) * r_m) *
+                              (1.0f + 9.5367432e-07f);
+            sc[0] = s_m; sc[1] = ik_m; sc[2] = r_m; sc[3] = eps_dm * mam; sc[4] = s_v; sc[5] = ik_v; sc[6] = r_v; sc[7] = eps_dv;
             if (ok) w.flags[lane] |= 1u;
         }
         __syncwarp();
@@ -823,7 +828,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 const float g[4] = {g4.x, g4.y, g4.z, g4.w};
                 const uint32_t mw = w.cw_m[slot][lane], vw = w.cw_v[slot][lane];
                 float xm[4], xv[4], m1[4], v1[4];
-                const float4 sa = reinterpret_cast<const float4*>(w.old_sc[slot])[0];   // s_m, 1/k_m, r_m, eps_dm
+                const float4 sa = reinterpret_cast<const float4*>(w.old_sc[slot])[0];   // s_m, 1/k_m, r_m, eps_dm * max|beta1 m~|
                 const float4 sb = reinterpret_cast<const float4*>(w.old_sc[slot])[1];   // s_v, 1/k_v, r_v, eps_dv
                 e4m3x4_lg2(s_lg2, mw, xm);
                 e4m3x4_lg2(s_lg2, vw, xv);
@@ -831,7 +836,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 // a negative second-moment code sends the group to the exact path (via the NaN that max_nan carries
                 // into the group maximum); a NaN code arrives as a NaN moment through the table
                 float mx_a = (vw & 0x80808080u) ? __int_as_float(0x7fffffff) : 0.f;
-                float mn_a = kInf, mx_am = 0.f, mx_v = 0.f, mn_v = kInf;
+                float mn_a = kInf, mx_v = 0.f, mn_v = kInf;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     // |m| = (c s)^(1/k) r = ex2(lg2(c) / k + lg2(s) / k) r; the sign of the code is put back on
@@ -843,18 +848,17 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                     const float a1 = fabsf(m1[j]);
                     mx_a = max_nan(mx_a, a1);   // a NaN anywhere must surface in the maxima
                     mn_a = fminf(mn_a, a1);
-                    mx_am = fmaxf(mx_am, fabsf(h.beta1 * mt));
                     mx_v = max_nan(mx_v, v1[j]);
                     mn_v = fminf(mn_v, v1[j]);
                 }
-                // all five are non-negative (or NaN, which orders above everything): unsigned order == float order
+                // all four are non-negative (or NaN, which orders above everything): unsigned order == float order
                 const float MA = __uint_as_float(redux_max_f(mx_a)), mA = __uint_as_float(redux_min_f(mn_a));
-                const float MAM = __uint_as_float(redux_max_f(mx_am));
                 const float MV = __uint_as_float(redux_max_f(mx_v)), mV = __uint_as_float(redux_min_f(mn_v));
                 // error bounds of the approximate moments.  First moment (the two terms may cancel), absolute
-                // and uniform over the group: |m~' - m'| <= eps_dm*max|beta1*m~| + 2^-22*max|m'| = d_m.
+                // and uniform over the group: |m~' - m'| <= eps_dm*max|beta1*m~| + 2^-22*max|m'| = d_m (the first product comes
+                // ready-made from the set-up: sa.w).
                 // Second moment (both terms >= 0), relative per element: |v~' - v'| <= (eps_dv + 2^-22) * v'.
-                const float d_m = __fmaf_rn(sa.w, MAM, k2m22 * MA);
+                const float d_m = __fmaf_rn(k2m22, MA, sa.w);
                 const float e_v = sb.w + k2m22;
                 // no possible exact zero / sign change / NaN / denormal, and nothing overflowed
                 ok = (mA - d_m > kTiny) && (mV > kTiny) && (MA <= kSaneHi) && (MV <= kSaneHi);
