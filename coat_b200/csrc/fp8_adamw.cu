@@ -594,6 +594,11 @@ __device__ __forceinline__ float rcp_ftz(float x) { float r; asm("rcp.approx.ftz
 __device__ __forceinline__ float sqrt_ftz(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ float max_nan(float a, float b) { float r; asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r; }
 
+// Two-wide fp32 arithmetic (one instruction for two lanes of a 64-bit register pair on sm_100; each half is
+// rounded to nearest like the scalar instruction, so results are bit-identical to the scalar form)
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
 template <typename scalar_t>
 __device__ __noinline__ void flush_pending(WarpTile& w, int lane, const AdamwHyper& h, const StepConsts& c) {
     __syncwarp();
@@ -838,13 +843,22 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 float mx_a = (vw & 0x80808080u) ? __int_as_float(0x7fffffff) : 0.f;
                 float mn_a = kInf, mx_v = 0.f, mn_v = kInf;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int jj = 0; jj < 4; jj += 2) {
                     // |m| = (c s)^(1/k) r = ex2(lg2(c) / k + lg2(s) / k) r; the sign of the code is put back on
-                    const float mt = __uint_as_float(__float_as_uint(ex2_ftz(__fmaf_rn(xm[j], sa.y, c0_m)) * sa.z) |
-                                                     ((mw << (24 - 8 * j)) & 0x80000000u));
-                    const float vt = ex2_ftz(__fmaf_rn(xv[j], sb.y, c0_v)) * sb.z;
-                    m1[j] = adam_first(h.beta1, mt, c.om_beta1, g[j]);
-                    v1[j] = adam_second(h.beta2, vt, c.om_beta2, g[j]);
+                    const float2 tm = __ffma2_rn(f2(xm[jj], xm[jj + 1]), f2(sa.y), f2(c0_m));
+                    const float2 tv = __ffma2_rn(f2(xv[jj], xv[jj + 1]), f2(sb.y), f2(c0_v));
+                    float2 mt = __fmul2_rn(f2(ex2_ftz(tm.x), ex2_ftz(tm.y)), f2(sa.z));
+                    const float2 vt = __fmul2_rn(f2(ex2_ftz(tv.x), ex2_ftz(tv.y)), f2(sb.z));
+                    mt.x = __uint_as_float(__float_as_uint(mt.x) | ((mw << (24 - 8 * jj)) & 0x80000000u));
+                    mt.y = __uint_as_float(__float_as_uint(mt.y) | ((mw << (16 - 8 * jj)) & 0x80000000u));
+                    const float2 gg = f2(g[jj], g[jj + 1]);
+                    // beta1 m + (1-beta1) g  and  beta2 v + ((1-beta2) g) g, as adam_first / adam_second round them
+                    const float2 m2 = __ffma2_rn(f2(h.beta1), mt, __fmul2_rn(f2(c.om_beta1), gg));
+                    const float2 v2 = __ffma2_rn(f2(h.beta2), vt, __fmul2_rn(__fmul2_rn(f2(c.om_beta2), gg), gg));
+                    m1[jj] = m2.x; m1[jj + 1] = m2.y; v1[jj] = v2.x; v1[jj + 1] = v2.y;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
                     const float a1 = fabsf(m1[j]);
                     mx_a = max_nan(mx_a, a1);   // a NaN anywhere must surface in the maxima
                     mn_a = fminf(mn_a, a1);
@@ -877,10 +891,13 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 if (ok) {
                     // weights from the approximate moments (they are not quantised)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float denom = __fmaf_rn(sqrt_ftz(v1[j]), c.p_a, c.p_b);
-                        const float update = __fmaf_rn(h.wd, p[j], m1[j] * rcp_ftz(denom));
-                        p[j] = __fmaf_rn(-h.lr, update, p[j]);
+                    for (int jj = 0; jj < 4; jj += 2) {
+                        const float2 denom = __ffma2_rn(f2(sqrt_ftz(v1[jj]), sqrt_ftz(v1[jj + 1])), f2(c.p_a), f2(c.p_b));
+                        const float2 pj = f2(p[jj], p[jj + 1]);
+                        const float2 update = __ffma2_rn(f2(h.wd), pj, __fmul2_rn(f2(m1[jj], m1[jj + 1]),
+                                                                                  f2(rcp_ftz(denom.x), rcp_ftz(denom.y))));
+                        const float2 pn = __ffma2_rn(f2(-h.lr), update, pj);
+                        p[jj] = pn.x; p[jj + 1] = pn.y;
                     }
                     E::store(pp, p);
                     if (w.ptr_bf[slot]) {
@@ -1014,21 +1031,27 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             const float m1[4] = {m4.x, m4.y, m4.z, m4.w}, v1[4] = {v4.x, v4.y, v4.z, v4.w};
             float ql[4], qh[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float a1 = fabsf(m1[j]);
-                const float e = ex2_ftz(qa_m.y * lg2_ftz(a1 * qa_m.w));
+            for (int jj = 0; jj < 4; jj += 2) {
+                const float2 a1 = f2(fabsf(m1[jj]), fabsf(m1[jj + 1]));
+                const float2 arg = __fmul2_rn(a1, f2(qa_m.w));
+                const float2 t = __fmul2_rn(f2(qa_m.y), f2(lg2_ftz(arg.x), lg2_ftz(arg.y)));
+                const float2 e = f2(ex2_ftz(t.x), ex2_ftz(t.y));
                 // 2^-floor(log2 a1) >= 1/a1, from the exponent field alone (a1 is a normal number here)
-                const float ia = __uint_as_float(0x7f000000u - (__float_as_uint(a1) & 0x7f800000u));
-                ql[j] = e * __fmaf_rn(-qb_m.z, ia, qb_m.x);
-                qh[j] = e * __fmaf_rn(qb_m.z, ia, qb_m.y);
+                const float2 ia = f2(__uint_as_float(0x7f000000u - (__float_as_uint(a1.x) & 0x7f800000u)),
+                                     __uint_as_float(0x7f000000u - (__float_as_uint(a1.y) & 0x7f800000u)));
+                const float2 lo = __fmul2_rn(e, __ffma2_rn(f2(-qb_m.z), ia, f2(qb_m.x)));
+                const float2 hi = __fmul2_rn(e, __ffma2_rn(f2(qb_m.z), ia, f2(qb_m.y)));
+                ql[jj] = lo.x; ql[jj + 1] = lo.y; qh[jj] = hi.x; qh[jj + 1] = hi.y;
             }
             uint32_t cm = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
             uint32_t dm = cm ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float e = ex2_ftz(qa_v.y * lg2_ftz(v1[j] * qa_v.w));
-                ql[j] = e * qb_v.x;
-                qh[j] = e * qb_v.y;
+            for (int jj = 0; jj < 4; jj += 2) {
+                const float2 arg = __fmul2_rn(f2(v1[jj], v1[jj + 1]), f2(qa_v.w));
+                const float2 t = __fmul2_rn(f2(qa_v.y), f2(lg2_ftz(arg.x), lg2_ftz(arg.y)));
+                const float2 e = f2(ex2_ftz(t.x), ex2_ftz(t.y));
+                const float2 lo = __fmul2_rn(e, f2(qb_v.x)), hi = __fmul2_rn(e, f2(qb_v.y));
+                ql[jj] = lo.x; ql[jj + 1] = lo.y; qh[jj] = hi.x; qh[jj + 1] = hi.y;
             }
             uint32_t cv = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
             uint32_t dv = cv ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
