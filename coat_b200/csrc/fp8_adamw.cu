@@ -44,8 +44,9 @@ struct AdamwHyper {
 template <bool BCAST>
 __device__ __forceinline__ void store_bf16x4_bcast(__nv_bfloat16* dst, const float (&q)[4], const AdamwHyper& h) {
     uint2 t;
-    t.x = (uint32_t)coat_float_to_bf16_bits(q[0]) | ((uint32_t)coat_float_to_bf16_bits(q[1]) << 16);
-    t.y = (uint32_t)coat_float_to_bf16_bits(q[2]) | ((uint32_t)coat_float_to_bf16_bits(q[3]) << 16);
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(q[0], q[1]), hi = __floats2bfloat162_rn(q[2], q[3]);
+    t.x = *reinterpret_cast<const uint32_t*>(&lo);
+    t.y = *reinterpret_cast<const uint32_t*>(&hi);
     *reinterpret_cast<uint2*>(dst) = t;
     if constexpr (BCAST)
         for (int i = 0; i < h.n_peers; ++i)
@@ -173,12 +174,20 @@ __device__ __forceinline__ float adam_second(float beta2, float v, float om_beta
 #define COAT_EXPAND_MIN_VAL 1e-30
 #define COAT_PLAIN_MIN_VAL 1e-20
 
+// x + 1e-30 evaluated in double and rounded back to float, as the reference's expression does.  For x >= 2^-70 the
+// addend is below a quarter of x's last place, so the rounded sum is x itself: the double-precision unit (slow on
+// this GPU) is only used for smaller, zero, negative or NaN inputs.
+__device__ __forceinline__ float coat_add_expand_min_val(float x) {
+    if (x >= 8.4703295e-22f /* 2^-70 */ && x <= 3.0e38f) return x;
+    return x + COAT_EXPAND_MIN_VAL;
+}
+
 __device__ __forceinline__ void expand_group_scalars(float absmax, float absmin, int expand_min,
                                                      float& maxv, float& sqrt_minmax, float& expo,
                                                      float& new_scale) {
     float fp8MaxVal = 448;
-    float firstMaxVal = absmax + COAT_EXPAND_MIN_VAL;
-    float firstMinVal = absmin + COAT_EXPAND_MIN_VAL;
+    float firstMaxVal = coat_add_expand_min_val(absmax);
+    float firstMinVal = coat_add_expand_min_val(absmin);
     float firstRatio = firstMaxVal / firstMinVal;
     float firstSqrtMinMax = sqrt(firstMaxVal) * sqrt(firstMinVal);
     float ratioUpperBound = fp8MaxVal * fp8MaxVal / 2;
@@ -906,8 +915,9 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                         for (int j = 0; j < 4; ++j) q[j] = E::round(p[j]);
                         if (BCAST && (w.ptr_bf[slot] & 15ull) == 0) {   // staged; sent after the loop
                             uint2 t2;
-                            t2.x = (uint32_t)coat_float_to_bf16_bits(q[0]) | ((uint32_t)coat_float_to_bf16_bits(q[1]) << 16);
-                            t2.y = (uint32_t)coat_float_to_bf16_bits(q[2]) | ((uint32_t)coat_float_to_bf16_bits(q[3]) << 16);
+                            const __nv_bfloat162 lo = __floats2bfloat162_rn(q[0], q[1]), hi = __floats2bfloat162_rn(q[2], q[3]);
+                            t2.x = *reinterpret_cast<const uint32_t*>(&lo);
+                            t2.y = *reinterpret_cast<const uint32_t*>(&hi);
                             bf_stage[slot * 32 + lane] = t2;
                             staged |= 1u << slot;
                         } else {
