@@ -1146,6 +1146,179 @@ fp8_adamw_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
     }
 }
 
+// =====================================================================================
+// Guarded fast path of the step WITHOUT expansion (fp8_adamw_cuda_kernel.cu:38-124)
+// =====================================================================================
+// Without the powers the moments cost a handful of exact fp32 operations, so m', v', the group maxima and the new
+// scales are computed exactly as the reference does (same operations, same contractions).  What made the exact
+// kernel instruction bound are its IEEE divisions and square root: four divisions and a square root per element,
+// ~50 instructions.  Here
+//   * a code is taken from m' * rcp(s') evaluated at both ends of an interval (relative half-width 2^-21) that
+//     contains the reference's correctly rounded m' / s'; only if the two ends round to different codes is that
+//     element divided exactly (about one element in 1e5);
+//   * the weights use sqrt.approx / rcp.approx and differ from the reference's by a few 1e-7 of one update (the
+//     tolerance stated for the expansion kernel's default mode); COAT_ADAMW_EXACT_POW selects the exact kernel.
+// A group that is partial, unaligned, or whose maximum is not a finite number in the modelled range goes to the
+// exact routine.
+constexpr int kPlainThreads = 256;
+
+template <bool MULTI>
+__global__ void __launch_bounds__(kPlainThreads)
+fp8_adamw_plain_fast_kernel(TensorDesc single, const TensorDesc* __restrict__ table,
+                            const int64_t* __restrict__ group_prefix, int n_tensors, int64_t total_groups,
+                            AdamwHyper h, unsigned long long* dbg) {
+    __shared__ float smem_min[kPlainThreads / COAT_WARP][kGroup];   // scratch the exact routine's signature asks for
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    StepConsts c;
+    c.om_beta1 = 1 - h.beta1;
+    c.om_beta2 = 1 - h.beta2;
+    c.correction1 = 1.0f - powf(h.beta1, h.step);
+    c.correction2_sqrt = sqrtf(1.0f - powf(h.beta2, h.step));
+    c.p_a = c.correction1 / c.correction2_sqrt;
+    c.p_b = h.eps * c.correction1;
+    const float kRelHalfWidth = 4.7683716e-07f;   // 2^-21: rcp.approx (2^-23) + two roundings, doubled
+    const int64_t warps_total = (int64_t)gridDim.x * (kPlainThreads / COAT_WARP);
+    // One group's inputs, loaded a trip ahead of their use so that a warp always has a group's worth of loads in
+    // flight while it computes on the previous one.
+    struct Inputs {
+        float4 p4, g4;
+        uint32_t mw, vw;
+        float s_m, s_v;
+        int64_t group;
+        int ti;
+        bool ok;
+    };
+    int ti_cursor = 0;
+    auto fetch = [&](int64_t gi, Inputs& in) {
+        in.group = gi;
+        in.ti = 0;
+        if (MULTI) {
+            if (gi >= group_prefix[ti_cursor + 1]) {   // group_prefix is sorted; successive gi only move forward
+                int lo = ti_cursor + 1, hi = n_tensors - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                }
+                ti_cursor = lo;
+            }
+            in.ti = ti_cursor;
+            in.group = gi - group_prefix[ti_cursor];
+        }
+        const TensorDesc& t = MULTI ? table[in.ti] : single;
+        const int64_t base = in.group * kGroup + lane * 4;
+        in.ok = desc_vec_ok(t, 16) && (t.numel - in.group * kGroup >= kGroup);
+        if (in.ok) {
+            in.p4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(t.p) + base);
+            in.g4 = __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(t.g) + base));
+            in.mw = *reinterpret_cast<const uint32_t*>(t.m + base);
+            in.vw = *reinterpret_cast<const uint32_t*>(t.v + base);
+            in.s_m = t.s_m[in.group];
+            in.s_v = t.s_v[in.group];
+        }
+    };
+    Inputs cur, nxt;
+    int64_t gi = (int64_t)blockIdx.x * (kPlainThreads / COAT_WARP) + warp;
+    if (gi < total_groups) fetch(gi, cur);
+    for (; gi < total_groups; gi += warps_total, cur = nxt) {
+        if (gi + warps_total < total_groups) fetch(gi + warps_total, nxt);
+        const TensorDesc& t = MULTI ? table[cur.ti] : single;
+        const int64_t group = cur.group;
+        const int64_t base = group * kGroup + lane * 4;
+        bool ok = cur.ok;
+        float p[4], g[4], m1[4], v1[4];
+        float new_scale_m = 0.f, new_scale_v = 0.f;
+        if (ok) {
+            const float4 p4 = cur.p4, g4 = cur.g4;
+            const uint32_t mw = cur.mw, vw = cur.vw;
+            const float s_m = cur.s_m, s_v = cur.s_v;
+            p[0] = p4.x; p[1] = p4.y; p[2] = p4.z; p[3] = p4.w;
+            g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+            float fm[4], fv[4];
+            coat_fp8x4_to_float4<COAT_E4M3>(mw, fm);
+            coat_fp8x4_to_float4<COAT_E4M3>(vw, fv);
+            float mx_m = 0.f, mx_v = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 4; jj += 2) {   // adam_first / adam_second, two elements per instruction
+                const float2 gg = f2(g[jj], g[jj + 1]);
+                const float2 m2 = __ffma2_rn(f2(h.beta1), __fmul2_rn(f2(fm[jj], fm[jj + 1]), f2(s_m)),
+                                             __fmul2_rn(f2(c.om_beta1), gg));
+                const float2 v2 = __ffma2_rn(f2(h.beta2), __fmul2_rn(f2(fv[jj], fv[jj + 1]), f2(s_v)),
+                                             __fmul2_rn(__fmul2_rn(f2(c.om_beta2), gg), gg));
+                m1[jj] = m2.x; m1[jj + 1] = m2.y; v1[jj] = v2.x; v1[jj + 1] = v2.y;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                mx_m = max_nan(mx_m, fabsf(m1[j]));
+                mx_v = max_nan(mx_v, fabsf(v1[j]));
+            }
+            // non-negative or NaN (which orders above everything): unsigned order == float order
+            mx_m = __uint_as_float(redux_max_f(mx_m));
+            mx_v = __uint_as_float(redux_max_f(mx_v));
+            // x + 1e-20 in double, rounded to float: x itself from 2^-40 up (the addend is below a quarter of its last place)
+            const float a_m = (mx_m >= 9.094947e-13f && mx_m <= 3.0e38f) ? mx_m : (float)((double)mx_m + COAT_PLAIN_MIN_VAL);
+            const float a_v = (mx_v >= 9.094947e-13f && mx_v <= 3.0e38f) ? mx_v : (float)((double)mx_v + COAT_PLAIN_MIN_VAL);
+            new_scale_m = __fdiv_rn(a_m, 448.0f);
+            new_scale_v = __fdiv_rn(a_v, 448.0f);
+            // finite maxima and scales whose reciprocal the approximate unit handles at full accuracy
+            ok = mx_m <= 1.0e30f && mx_v <= 1.0e30f && new_scale_m >= 1.0e-30f && new_scale_v >= 1.0e-30f;
+        }
+        if (!ok) {   // warp-uniform
+            process_group_exact<float, false, false>(t, group, lane, h, c.om_beta1, c.om_beta2, c.correction1,
+                                                     c.correction2_sqrt, desc_vec_ok(t, 16), smem_min[warp]);
+            if (dbg && lane == 0) atomicAdd(dbg + 1, 1ull);
+            continue;
+        }
+        // codes: both ends of the interval around m' / s'
+        const float r_m = rcp_ftz(new_scale_m), r_v = rcp_ftz(new_scale_v);
+        const float2 rm2 = f2(r_m * (1.0f - kRelHalfWidth), r_m * (1.0f + kRelHalfWidth));
+        const float2 rv2 = f2(r_v * (1.0f - kRelHalfWidth), r_v * (1.0f + kRelHalfWidth));
+        float ql[4], qh[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 q = __fmul2_rn(f2(m1[j]), rm2);
+            ql[j] = q.x; qh[j] = q.y;
+        }
+        uint32_t cm = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
+        const uint32_t dm = cm ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 q = __fmul2_rn(f2(v1[j]), rv2);
+            ql[j] = q.x; qh[j] = q.y;
+        }
+        uint32_t cv = coat_float4_to_fp8x4<COAT_E4M3>(ql[0], ql[1], ql[2], ql[3]);
+        const uint32_t dv = cv ^ coat_float4_to_fp8x4<COAT_E4M3>(qh[0], qh[1], qh[2], qh[3]);
+        if (dm | dv) {   // rare: the exact division for the elements whose interval straddles a rounding boundary
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if ((dm >> (8 * j)) & 0xffu)
+                    cm = (cm & ~(0xffu << (8 * j))) | (coat_float_to_fp8<COAT_E4M3>(__fdiv_rn(m1[j], new_scale_m)) << (8 * j));
+                if ((dv >> (8 * j)) & 0xffu)
+                    cv = (cv & ~(0xffu << (8 * j))) | (coat_float_to_fp8<COAT_E4M3>(__fdiv_rn(v1[j], new_scale_v)) << (8 * j));
+            }
+        }
+        *reinterpret_cast<uint32_t*>(t.m + base) = cm;
+        *reinterpret_cast<uint32_t*>(t.v + base) = cv;
+        if (lane == 0) {
+            t.s_m[group] = new_scale_m;
+            t.s_v[group] = new_scale_v;
+        }
+        // weights from approximate square root and reciprocal (they are not quantised)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj += 2) {
+            const float2 denom = __ffma2_rn(f2(sqrt_ftz(v1[jj]), sqrt_ftz(v1[jj + 1])), f2(c.p_a), f2(c.p_b));
+            const float2 pj = f2(p[jj], p[jj + 1]);
+            const float2 update = __ffma2_rn(f2(h.wd), pj, __fmul2_rn(f2(m1[jj], m1[jj + 1]),
+                                                                      f2(rcp_ftz(denom.x), rcp_ftz(denom.y))));
+            const float2 pn = __ffma2_rn(f2(-h.lr), update, pj);
+            p[jj] = pn.x; p[jj + 1] = pn.y;
+        }
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(t.p) + base) = make_float4(p[0], p[1], p[2], p[3]);
+        if (t.bf16_out) store_bf16x4_bcast<false>(reinterpret_cast<__nv_bfloat16*>(t.bf16_out) + base, p, h);
+        if (dbg && lane == 0) atomicAdd(dbg + 0, 1ull);
+    }
+}
+
 thread_local unsigned long long* g_debug_counters = nullptr;   // per host thread: only the caller's own launches count
 
 int grid_for(int64_t total_groups) {
@@ -1176,6 +1349,23 @@ int launch_typed(const TensorDesc& single, const TensorDesc* table, const int64_
             const int grid = (int)(ctas_needed < cap ? ctas_needed : cap);
             kern<<<grid, kTiledThreads, smem, st>>>(single, table, prefix, n_tensors, total_groups, h,
                                                           g_debug_counters);
+            return coat_launch_status();
+        }
+    }
+    if constexpr (!EXPAND && std::is_same<scalar_t, float>::value) {
+        if (!(flags & COAT_ADAMW_EXACT_POW) && !(MULTI && h.n_peers > 0)) {
+            const int64_t ctas_needed = (total_groups + kPlainThreads / COAT_WARP - 1) / (kPlainThreads / COAT_WARP);
+            // persistent: exactly as many CTAs as are resident at once (a second wave would start when the first is done)
+            static int per_sm = 0;
+            if (per_sm == 0) {
+                int n = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fp8_adamw_plain_fast_kernel<MULTI>, kPlainThreads, 0) !=
+                    cudaSuccess || n < 1) n = 2;
+                per_sm = n;
+            }
+            const int64_t cap = (int64_t)coat_sm_count() * per_sm;
+            fp8_adamw_plain_fast_kernel<MULTI><<<(int)(ctas_needed < cap ? ctas_needed : cap), kPlainThreads, 0, st>>>(
+                single, table, prefix, n_tensors, total_groups, h, g_debug_counters);
             return coat_launch_status();
         }
     }

@@ -110,19 +110,32 @@ def test_expand_bit_exact_vs_reference_kernel(n):
         a["p"].copy_(b["p"])   # keep the three runs on the same trajectory
 
 
-@pytest.mark.parametrize("n", [129, 4096 * 16 + 3])
+@pytest.mark.parametrize("n", [129, 4096 * 16 + 3, 4096 * 512])
 def test_plain_bit_exact_vs_reference_kernel(n):
+    """The step without expansion.  Exact mode: every array bit-identical to the reference's kernel.  Default mode
+    (approximate square root / reciprocal in the weight update, guarded reciprocal in the requantisation): codes
+    and scales bit-identical, weights within the tolerance stated for the default mode."""
     ref = load_ref_qoptim()
     if ref is None:
         pytest.skip("oracle/_ref/qoptim_cuda.so not built (python oracle/build_ref.py)")
     st0, gen = fresh(n, seed=11)
-    a, b = to(st0, "cuda"), to(st0, "cuda")
+    a, b, x = to(st0, "cuda"), to(st0, "cuda"), to(st0, "cuda")
     for step in range(1, 11):
         g = (torch.randn(n, generator=gen) * 1e-3).cuda()
+        if step == 4:   # a few adversarial groups: all zero, all equal, huge dynamic range
+            gv = g[: (n // 128) * 128].view(-1, 128)
+            gv[0] = 0.0
+            if gv.shape[0] > 2:
+                gv[1] = 3e-4
+                gv[2] *= torch.logspace(-12, 2, 128, device="cuda")
         plain_step(mine(), a, g, step)
+        plain_step(mine(), x, g, step, flags=EXACT_POW)
         plain_step(ref, b, g, step, fp8_views=True)
         torch.cuda.synchronize()
-        assert_bit_equal(a, b, keys=("p", "m", "v", "s_m", "s_v"), what=f"plain n={n} step={step}")
+        assert_bit_equal(x, b, keys=("p", "m", "v", "s_m", "s_v"), what=f"plain exact n={n} step={step}")
+        assert_bit_equal(a, b, keys=("m", "v", "s_m", "s_v"), what=f"plain default n={n} step={step}")
+        assert_weights_close(a, b, HYPER["lr"], what=f"plain default n={n} step={step}")
+        a["p"].copy_(b["p"])
 
 
 def test_expand_benchmark_tensor_bit_exact_vs_reference_kernel():
