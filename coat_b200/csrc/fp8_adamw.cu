@@ -531,6 +531,7 @@ struct __align__(16) WarpTile {
     float c0[kTile][2];          // lg2(s) / k of the stored scale and exponent, per moment: the constant part of the dequantisation's exponent
     uint32_t stat[kTile][4];     // exact max m, min m, max v, min v (float bit patterns)
     unsigned long long ptr_p[kTile], ptr_g[kTile], ptr_m[kTile], ptr_v[kTile], ptr_bf[kTile];
+    unsigned long long pair_bf[kTile];   // broadcast: bf16 destinations of a pair's first tile when it is not one run
     long long local[kTile];      // group index inside its tensor
     int ti[kTile];               // tensor index
     uint32_t flags[kTile];       // bit 0: stored scalars are in the modelled range; bit 1: full, aligned group
@@ -667,9 +668,9 @@ __device__ __noinline__ void queue_exact(WarpTile& w, int slot, int lane, uint32
 // Shared memory, not registers, limits how many CTAs share an SM; telling the compiler so lets it use the
 // registers that occupancy leaves free instead of spilling.
 constexpr size_t kTiledSmem = kTiledWarps * sizeof(WarpTile);
-// The broadcast variant stages a tile's bf16 weights (256 bytes per group) per warp behind everything else,
-// and sends them to this GPU's buffer and to every peer's with bulk stores of up to a whole tile.
-constexpr size_t kBcastStageBytes = kTile * kGroup * sizeof(__nv_bfloat16);
+// The broadcast variant stages the bf16 weights of two adjacent tiles (256 bytes per group) per warp behind
+// everything else, and sends them to this GPU's buffer and to every peer's with bulk stores of up to both tiles.
+constexpr size_t kBcastStageBytes = 2 * kTile * kGroup * sizeof(__nv_bfloat16);   // two tiles: see the tile order below
 constexpr size_t kTiledSmemBcast = kTiledSmem + kTiledWarps * kBcastStageBytes;
 // A table launch also keeps the tensors' group offsets in (static) shared memory: the binary search that maps a
 // tile to its tensor is a chain of dependent loads, 9 deep for the 291 tensors of Llama-2-7B, and from L2 that
@@ -727,7 +728,18 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     long long phase_t = clock64();
 #endif
 
-    for (int64_t tile = (int64_t)blockIdx.x * kTiledWarps + warp; tile < n_tiles; tile += warps_total) {
+    // Tile order.  Plain: warp w of the grid takes tiles w, w + W, w + 2W, ...  Broadcast: it takes PAIRS of adjacent
+    // tiles (2w, 2w+1), (2(w+W), 2(w+W)+1), ... so that the bf16 weights of a pair are one contiguous run of up to
+    // 3 KB, which leaves as ONE bulk store per destination once the second tile is staged.
+    const int64_t first_unit = (int64_t)blockIdx.x * kTiledWarps + warp;
+    uint32_t pair_staged = 0;          // broadcast: slots of the pair's first tile that wait in bf_stage
+    unsigned long long pair_ptr = 0;   // broadcast: destination of the first tile's run (0: not one contiguous run)
+    int pair_slots = 0;
+    for (int64_t it = 0;; ++it) {
+        const int half = BCAST ? (int)(it & 1) : 0;
+        const int64_t tile = BCAST ? 2 * (first_unit + (it >> 1) * warps_total) + half : first_unit + it * warps_total;
+        if (tile >= n_tiles) break;
+        const bool pair_open = BCAST && half == 0 && tile + 1 < n_tiles;   // a second tile follows: hold the stores back
         const int64_t g0 = tile * kTile;
         const int n_slots = (int)((total_groups - g0) < kTile ? (total_groups - g0) : kTile);
 
@@ -828,8 +840,9 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
         // ================= phase 1: lanes over the elements of one group =================
         uint32_t live = 0;   // slots that stay on the fast path (warp-uniform)
         uint32_t staged = 0;   // BCAST: slots whose bf16 weights wait in bf_stage (warp-uniform)
+        uint2* const stage = bf_stage + half * (kTile * 32);
         if constexpr (BCAST) {
-            bulk_wait_read();   // the previous tile's bulk stores have read bf_stage (no-op for other lanes)
+            if (half == 0) bulk_wait_read();   // the previous pair's bulk stores have read bf_stage (no-op for other lanes)
             __syncwarp();
         }
 #pragma unroll 1
@@ -918,7 +931,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                             const __nv_bfloat162 lo = __floats2bfloat162_rn(q[0], q[1]), hi = __floats2bfloat162_rn(q[2], q[3]);
                             t2.x = *reinterpret_cast<const uint32_t*>(&lo);
                             t2.y = *reinterpret_cast<const uint32_t*>(&hi);
-                            bf_stage[slot * 32 + lane] = t2;
+                            stage[slot * 32 + lane] = t2;
                             staged |= 1u << slot;
                         } else {
                             store_bf16x4_bcast<BCAST>(reinterpret_cast<__nv_bfloat16*>(w.ptr_bf[slot]) + lane * 4, q, h);
@@ -950,21 +963,51 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
         }
         __syncwarp();
         if constexpr (BCAST) {
-            if (staged) {
+            const uint32_t group_bytes = kGroup * (uint32_t)sizeof(__nv_bfloat16);
+            const bool run = bulk && staged == (1u << n_slots) - 1u;   // this tile's weights are one contiguous staged run
+            if (pair_open) {   // first tile of a pair: remember it, send together with the second
+                pair_staged = staged;
+                pair_ptr = run ? w.ptr_bf[0] : 0ull;
+                pair_slots = n_slots;
+            } else if (staged | pair_staged) {
                 fence_proxy_async();   // the staged words (generic stores) become visible to the bulk copies
                 __syncwarp();
-                if (lane <= h.n_peers) {   // lane 0: this GPU's buffer; lane i: peer i-1
-                    const long long delta = lane == 0 ? 0ll : h.peer_delta[lane - 1];
-                    const uint32_t group_bytes = kGroup * (uint32_t)sizeof(__nv_bfloat16);
-                    if (bulk && staged == (1u << n_slots) - 1u) {   // one contiguous run: one store per destination
-                        bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[0]) + delta, bf_stage, (uint32_t)n_slots * group_bytes);
+                if (lane <= h.n_peers) {   // lane 0: this GPU's buffer; lane i: a peer, the order rotated by warp
+                    long long delta = 0ll;
+                    if (lane > 0) {
+                        int peer = lane - 1 + (int)(first_unit % h.n_peers);
+                        if (peer >= h.n_peers) peer -= h.n_peers;
+                        delta = h.peer_delta[peer];
+                    }
+                    const bool joined = half == 1 && pair_ptr != 0ull && run &&
+                                        w.ptr_bf[0] == pair_ptr + (unsigned long long)pair_slots * group_bytes;
+                    if (joined) {   // both tiles: one store per destination
+                        bulk_s2g(reinterpret_cast<char*>(pair_ptr) + delta, bf_stage, (uint32_t)(pair_slots + n_slots) * group_bytes);
                     } else {
-                        for (int slot = 0; slot < n_slots; ++slot)
-                            if (staged & (1u << slot))
-                                bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[slot]) + delta, bf_stage + slot * 32, group_bytes);
+                        if (half == 1 && pair_staged) {   // the held-back first tile on its own
+                            if (pair_ptr != 0ull) {
+                                bulk_s2g(reinterpret_cast<char*>(pair_ptr) + delta, bf_stage, (uint32_t)pair_slots * group_bytes);
+                            } else {
+                                for (int slot = 0; slot < pair_slots; ++slot)
+                                    if (pair_staged & (1u << slot))
+                                        bulk_s2g(reinterpret_cast<char*>(w.pair_bf[slot]) + delta, bf_stage + slot * 32, group_bytes);
+                            }
+                        }
+                        if (run) {
+                            bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[0]) + delta, stage, (uint32_t)n_slots * group_bytes);
+                        } else {
+                            for (int slot = 0; slot < n_slots; ++slot)
+                                if (staged & (1u << slot))
+                                    bulk_s2g(reinterpret_cast<char*>(w.ptr_bf[slot]) + delta, stage + slot * 32, group_bytes);
+                        }
                     }
                     bulk_commit();
                 }
+                pair_staged = 0;
+                pair_ptr = 0ull;
+            }
+            if (pair_open && !run && staged) {   // scattered first tile: its destinations are needed after ptr_bf is rewritten
+                if (lane < n_slots) w.pair_bf[lane] = w.ptr_bf[lane];
             }
         }
         PHASE_CLOCK(1);

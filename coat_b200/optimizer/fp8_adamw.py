@@ -148,6 +148,10 @@ class CoatAdamW(Optimizer):
         assert value.dtype in _STATE_DTYPES, f"unexpected optimizer state dtype {value.dtype}"
         return value.to(device=param.device)  # do not cast optimizer states
 
+    # Flags handed to the kernels of the one-launch path (0: guarded fast arithmetic; _lib.ADAMW_EXACT_POW: the exact
+    # routines everywhere, bit-identical weights too).  A non-zero value also sends single tensors through that path.
+    kernel_flags = 0
+
     # ---- state ---------------------------------------------------------------------------
     def _use_expansion(self):
         # Only these two spellings switch the expansion on (coat/optimizer/fp8_adamw.py:293);
@@ -214,7 +218,7 @@ class CoatAdamW(Optimizer):
             beta1, beta2 = group["betas"]
             hyper = dict(beta1=beta1, beta2=beta2, lr=group["lr"], weight_decay=group["weight_decay"],
                          eps=group["eps"], qgroup_size=self.qargs.qgroup_size, expand_min=self.qargs.expand_min)
-            if self.multi_tensor and len(params) > 1:
+            if (self.multi_tensor and len(params) > 1) or self.kernel_flags:
                 self._multi_tensor_step(gi, params, states, use_expansion, **hyper)
             else:
                 key = (lambda s, k: [st[k] for st in s])
@@ -301,7 +305,7 @@ class CoatAdamW(Optimizer):
                 rc = _lib.lib().coat_fp8_adamw_multi_step(
                     entry["dev"].data_ptr(), entry["prefix"].data_ptr(), len(idxs), entry["total"],
                     int(use_expansion), beta1, beta2, lr, weight_decay, eps, step, qgroup_size, expand_min,
-                    _lib.F32, 0, _lib.stream_ptr(device))
+                    _lib.F32, int(self.kernel_flags), _lib.stream_ptr(device))
             _lib.check(rc, "fp8_adamw_multi_step")
 
 

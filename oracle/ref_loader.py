@@ -75,3 +75,26 @@ def ref_module(name, one_config=True):
     if load_ref_triton(one_config) is None:
         return None
     return importlib.import_module(f"{_PKG}.{name}")
+
+
+def load_ref_optimizer():
+    """The reference's own `CoatAdamW` class and `QuantizationConfig` (coat/optimizer/fp8_adamw.py,
+    coat/utils/_fp8_quantization_config.py, staged unmodified) on top of its compiled extension, or None.
+    The reference's step() calls `Optimizer._cuda_graph_capture_health_check`, which current torch spells
+    `_accelerator_graph_capture_health_check`: the missing name is added to torch's Optimizer class as an alias on
+    this (oracle) side, the reference file is not touched."""
+    if "opt" in _loaded:
+        return _loaded["opt"]
+    if load_ref_qoptim() is None or not os.path.exists(os.path.join(REF_DIR, "coat_ref", "optimizer", "fp8_adamw.py")):
+        return None
+    from torch.optim.optimizer import Optimizer
+    if not hasattr(Optimizer, "_cuda_graph_capture_health_check"):
+        alias = getattr(Optimizer, "_accelerator_graph_capture_health_check", None)
+        Optimizer._cuda_graph_capture_health_check = alias if alias is not None else (lambda self: None)
+    try:
+        mod = importlib.import_module("coat_ref.optimizer.fp8_adamw")
+        cfg = importlib.import_module("coat_ref.utils._fp8_quantization_config")
+    except Exception:
+        return None
+    _loaded["opt"] = (mod.CoatAdamW, cfg.QuantizationConfig)
+    return _loaded["opt"]

@@ -156,3 +156,72 @@ def test_fused_bf16_copy_of_master_weights():
         assert torch.equal(c, p.detach().flatten().to(torch.bfloat16))
     with pytest.raises(ValueError):
         opt.attach_bf16_weights([(params[0], torch.zeros(3, dtype=torch.bfloat16, device="cuda"))])
+
+
+# ------------------------------------------------------------------------------------------------------
+# interchange with the REFERENCE's optimizer class (its python class on its own compiled kernels)
+# ------------------------------------------------------------------------------------------------------
+INTERCHANGE_SHAPES = [(256, 128), (1000,), (77, 3), (128,), (4096, 9), (512, 512)]
+
+
+def _pair(seed, qargs_kw):
+    """The same parameters twice: one set for the reference's CoatAdamW, one for this repository's."""
+    from _ref import load_ref_optimizer
+    ref = load_ref_optimizer()
+    if ref is None:
+        pytest.skip("the reference's optimizer class is not staged (python oracle/build_ref.py)")
+    RefAdamW, RefConfig = ref
+    gen = torch.Generator().manual_seed(seed)
+    init = [torch.randn(s, generator=gen) * 0.02 for s in INTERCHANGE_SHAPES]
+    pr = [torch.nn.Parameter(t.clone().cuda()) for t in init]
+    pm = [torch.nn.Parameter(t.clone().cuda()) for t in init]
+    hyper = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    return pr, RefAdamW(pr, qargs=RefConfig(**qargs_kw), **hyper), pm, (lambda: CoatAdamW(pm, qargs=QuantizationConfig(**qargs_kw), **hyper))
+
+
+@pytest.mark.parametrize("expansion", ["true", "false"])
+def test_state_dict_written_by_the_reference_class_loads_and_continues_bit_for_bit(expansion):
+    """Three steps with the reference's own CoatAdamW (its class, its compiled kernels), its state_dict saved with
+    torch.save, loaded into this repository's CoatAdamW, then both continue for three more steps on the same
+    gradients: keys, dtypes and shapes of the state as the reference wrote them; after the continuation every
+    quantised state array bit-identical, weights bit-identical in exact mode and within the stated tolerance of the
+    default mode."""
+    from coat_b200 import _lib
+    kw = dict(first_order_expansion=expansion, second_order_expansion=expansion)
+    pr, ref_opt, pm, make_mine = _pair(31, kw)
+    run(pr, ref_opt, 3)
+    buf = io.BytesIO()
+    torch.save(ref_opt.state_dict(), buf)
+    buf.seek(0)
+    sd = torch.load(buf, map_location="cpu", weights_only=False)
+    with torch.no_grad():
+        for a, b in zip(pr, pm):
+            b.copy_(a)
+    for exact in (True, False):
+        with torch.no_grad():
+            start = [p.detach().clone() for p in pr]
+        mine = make_mine()
+        mine.load_state_dict(copy.deepcopy(sd))
+        for p in pm:
+            st = mine.state[p]
+            assert st["exp_avg"].dtype == torch.float8_e4m3fn and st["exp_avg"].is_cuda and float(st["step"]) == 3.0
+            assert st["scale_exp_avg"].dtype == torch.float32
+        ref_sd = copy.deepcopy(ref_opt.state_dict())
+        old_flags = getattr(mine, "kernel_flags", None)
+        if exact:
+            mine.kernel_flags = _lib.ADAMW_EXACT_POW
+        run(pr, ref_opt, 3, seed0=300)
+        run(pm, mine, 3, seed0=300)
+        same_state(ref_opt, mine)
+        for a, b in zip(pr, pm):
+            if exact:
+                assert torch.equal(a, b)
+            else:
+                assert bool(((a - b).abs() <= 2.4e-7 * a.abs() + 1e-5 * 1e-3 * 10 * 3).all())
+        # rewind both for the second mode
+        ref_opt.load_state_dict(ref_sd)
+        with torch.no_grad():
+            for p, s0, q in zip(pr, start, pm):
+                p.copy_(s0)
+                q.copy_(s0)
+        del old_flags
