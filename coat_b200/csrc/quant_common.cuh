@@ -59,6 +59,11 @@ struct GroupScaleDivider {
         if (!IEEE) asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(scale));
     }
     __device__ __forceinline__ float operator()(float x) const { return IEEE ? __fdiv_rn(x, s) : x * r; }
+    // two quotients at once: one two-wide multiplication (each half rounds like the scalar instruction)
+    __device__ __forceinline__ float2 pair(float a, float b) const {
+        if (IEEE) return make_float2(__fdiv_rn(a, s), __fdiv_rn(b, s));
+        return __fmul2_rn(make_float2(a, b), make_float2(r, r));
+    }
     template <int N>
     __device__ __forceinline__ void apply(const float (&v)[N], float (&q)[N]) const {
 #pragma unroll

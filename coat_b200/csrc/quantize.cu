@@ -575,8 +575,10 @@ template <int FMT, int C, typename Divider>
 __device__ __forceinline__ void store_row_codes(uint8_t* dst, const float (&v)[C], const Divider& d) {
     uint32_t w[C / 4];
 #pragma unroll
-    for (int i = 0; i < C / 4; ++i)
-        w[i] = coat_float4_to_fp8x4<FMT>(d(v[4 * i]), d(v[4 * i + 1]), d(v[4 * i + 2]), d(v[4 * i + 3]));
+    for (int i = 0; i < C / 4; ++i) {
+        const float2 lo = d.pair(v[4 * i], v[4 * i + 1]), hi = d.pair(v[4 * i + 2], v[4 * i + 3]);
+        w[i] = coat_float4_to_fp8x4<FMT>(lo.x, lo.y, hi.x, hi.y);
+    }
     if constexpr (C == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
 }
@@ -584,6 +586,7 @@ __device__ __forceinline__ void store_row_codes(uint8_t* dst, const float (&v)[C
 struct DivFullDivider {   // the division instruction itself, out of line (scales outside [2^-120, 2^120])
     float s;
     __device__ __forceinline__ float operator()(float x) const { return div_full_outlined(x, s); }
+    __device__ __forceinline__ float2 pair(float a, float b) const { return make_float2((*this)(a), (*this)(b)); }
 };
 
 // FUSED (scalar-scale variant only): the kernel also finds the tensor's amax itself.  Launched cooperatively, every
@@ -720,7 +723,10 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
                 a = fmaxf(a, __shfl_xor_sync(COAT_FULL_MASK, a, 16));
                 const float cs = group_scale(a);
                 const GroupScaleDivider<IEEE> d(cs);
-                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+                {
+                    const float2 lo = d.pair(v[0][i], v[1][i]), hi = d.pair(v[2][i], v[3][i]);
+                    tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(lo.x, lo.y, hi.x, hi.y);
+                }
                 if ((i & 3) == mb) scale_t[n_loc + i][m_loc >> 4] = cs;   // the four lanes of a group share the stores
             }
         } else if (IEEE || by_scalar.fast) {
@@ -732,7 +738,10 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
             }
 #pragma unroll
             for (int i = 0; i < C; ++i)
-                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+                {
+                    const float2 lo = d.pair(v[0][i], v[1][i]), hi = d.pair(v[2][i], v[3][i]);
+                    tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(lo.x, lo.y, hi.x, hi.y);
+                }
         } else {
             const DivFullDivider d{scalar};
             if (STRAIGHT && inside) {
@@ -741,7 +750,10 @@ transpose_quant_tma_kernel(const __grid_constant__ CUtensorMap map_x, uint8_t* _
             }
 #pragma unroll
             for (int i = 0; i < C; ++i)
-                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+                {
+                    const float2 lo = d.pair(v[0][i], v[1][i]), hi = d.pair(v[2][i], v[3][i]);
+                    tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(lo.x, lo.y, hi.x, hi.y);
+                }
         }
         // The one barrier of the tile: stage s has been read by everyone (it can be refilled) and this tile's
         // transposed codes and scales are complete.  Tile k+1 writes the other pair of buffers, and nobody
