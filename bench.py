@@ -513,7 +513,7 @@ def blockscaled_extras(torch, device, peak, iters=10):
     return out
 
 
-def layer_extras(torch, device, iters=5):
+def layer_extras(torch, device, iters=5, with_reference_operators=False):
     """Forward + backward of ONE Llama-2-7B decoder layer (hidden 4096, 32 heads, MLP 11008) on 4 x 2048 tokens
     through the FP8 layer of this package, and, beside it, the same layer in plain bf16 torch (cuBLAS GEMMs,
     SDPA, eager elementwise ops) as a yardstick on the same GPU.  Weights N(0, 0.02), input N(0, 1) * 0.5,
@@ -572,6 +572,48 @@ def layer_extras(torch, device, iters=5):
     pos = torch.arange(S, device=device)[None, :]
     rope = tuple(t.unsqueeze(1) for t in llama_rotary_embeddings(pos, Hd // heads, 10000.0, torch.bfloat16))
     out = {"tokens": B * S}
+
+    def time_leg(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / iters
+
+    if with_reference_operators:
+        # the SAME composition on the reference's own operators (its Triton kernels with their own autotuning), as a
+        # baseline on this GPU: the reference's functions are put in place of this package's in the layer module, the
+        # weight cache and the quantise-in/out modules (oracle/ref_loader.py says which three calls are composed of
+        # reference calls and which one operator, the RMSNorm backward, stays this package's on both sides)
+        from oracle import ref_loader
+        ref = ref_loader.load_ref_triton(one_config=False)
+        if ref is None:
+            out["fp8_layer_on_reference_operators"] = {"reference": "oracle/_ref/coat_ref not staged"}
+        else:
+            import coat_b200.activation.real_quantization as mine
+            import coat_b200.activation.real_quantization.func_quantize as fq
+            import coat_b200.models.coat_llama as layer_mod
+            import coat_b200.utils._fp8_weightcache as cache_mod
+            ops = ref_loader.reference_layer_operators(ref, mine)
+            saved = []
+            for mod in (layer_mod, cache_mod, fq):
+                for name, fn in ops.items():
+                    if hasattr(mod, name):
+                        saved.append((mod, name, getattr(mod, name)))
+                        setattr(mod, name, fn)
+            try:
+                ms = time_leg(fp8_step)
+                out["fp8_layer_on_reference_operators"] = {"fwd_bwd_ms": ms, "tokens_per_s": B * S / (ms / 1e3)}
+            except Exception as exc:
+                out["fp8_layer_on_reference_operators"] = {"reference": f"did not run: {str(exc)[:160]}"}
+            finally:
+                for mod, name, fn in saved:
+                    setattr(mod, name, fn)
     for name, fn in (("fp8_layer", fp8_step), ("bf16_torch_layer", bf16_step)):
         for _ in range(3):
             fn()
@@ -585,6 +627,9 @@ def layer_extras(torch, device, iters=5):
         ms = e0.elapsed_time(e1) / iters
         out[name] = {"fwd_bwd_ms": ms, "tokens_per_s": B * S / (ms / 1e3)}
     out["fp8_over_bf16"] = out["bf16_torch_layer"]["fwd_bwd_ms"] / out["fp8_layer"]["fwd_bwd_ms"]
+    ref_leg = out.get("fp8_layer_on_reference_operators", {})
+    if "fwd_bwd_ms" in ref_leg:
+        out["ours_over_reference_operators"] = ref_leg["fwd_bwd_ms"] / out["fp8_layer"]["fwd_bwd_ms"]
     return out
 
 
@@ -829,6 +874,7 @@ def run_kernel_workload(args):
         extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10)))}
     elif args.workload == "reference-gpu":
         extras = {"reference_on_this_gpu": reference_on_this_gpu(torch, device, peak),
+                  "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, with_reference_operators=True),
                   "fp8_peak_yardstick": fp8_peak_yardstick(torch, device)}
     else:
         extras = {"fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device, iters=max(1, args.steps))}
@@ -999,7 +1045,7 @@ def run_gpu_arm(args):
             line["extras"] = {"quantizers_8192x4096_bf16": quantizer_extras(torch, device, peak),
                               "fused_operators_8192_tokens": fused_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
-                              "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device),
+                              "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, with_reference_operators=True),
                               "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak),
                               "reference_on_this_gpu": reference_on_this_gpu(torch, device, peak)}
         if cpu_v is not None:

@@ -735,6 +735,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
     uint32_t pair_staged = 0;          // broadcast: slots of the pair's first tile that wait in bf_stage
     unsigned long long pair_ptr = 0;   // broadcast: destination of the first tile's run (0: not one contiguous run)
     int pair_slots = 0;
+    int ti_cursor = 0;                 // table launches: the tensor this lane's previous group lay in
     for (int64_t it = 0;; ++it) {
         const int half = BCAST ? (int)(it & 1) : 0;
         const int64_t tile = BCAST ? 2 * (first_unit + (it >> 1) * warps_total) + half : first_unit + it * warps_total;
@@ -750,21 +751,30 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             int ti = 0;
             int64_t group = gi;
             if (MULTI) {
-                int lo = 0, hi = n_tensors - 1;
+                // a lane's groups only move forward from tile to tile: start at the tensor of its previous group, and
+                // search (binary, above it) only when the group has left that tensor
+                int lo = ti_cursor, hi = n_tensors - 1;
                 if (prefix_cached) {
-                    while (lo < hi) {
-                        const int mid = (lo + hi + 1) >> 1;
-                        if ((int64_t)s_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                    if (lo < hi && (int64_t)s_prefix[lo + 1] <= gi) {
+                        ++lo;
+                        while (lo < hi) {
+                            const int mid = (lo + hi + 1) >> 1;
+                            if ((int64_t)s_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                        }
                     }
                     group = gi - s_prefix[lo];
                 } else {
-                    while (lo < hi) {
-                        const int mid = (lo + hi + 1) >> 1;
-                        if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                    if (lo < hi && group_prefix[lo + 1] <= gi) {
+                        ++lo;
+                        while (lo < hi) {
+                            const int mid = (lo + hi + 1) >> 1;
+                            if (group_prefix[mid] <= gi) lo = mid; else hi = mid - 1;
+                        }
                     }
                     group = gi - group_prefix[lo];
                 }
                 ti = lo;
+                ti_cursor = lo;
             }
             const TensorDesc& t = MULTI ? table[ti] : single;
             const int64_t e0 = group * kGroup;
@@ -782,8 +792,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
         fence_proxy_async();   // this lane's generic accesses to the staging buffers precede the next bulk write
         __syncwarp();
         // stage the tile's inputs: one bulk copy per array when the tile is one contiguous, aligned run
-        bool all_mem_ok = true;
-        for (int sl = 0; sl < n_slots; ++sl) all_mem_ok = all_mem_ok && (w.flags[sl] & 2u);
+        const bool all_mem_ok = __ballot_sync(COAT_FULL_MASK, lane < n_slots && !(w.flags[lane] & 2u)) == 0u;
         const bool bulk = all_mem_ok && w.ti[0] == w.ti[n_slots - 1];
         if (bulk) {
             if (lane == 0) {

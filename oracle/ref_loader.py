@@ -98,3 +98,35 @@ def load_ref_optimizer():
         return None
     _loaded["opt"] = (mod.CoatAdamW, cfg.QuantizationConfig)
     return _loaded["opt"]
+
+
+def reference_layer_operators(ref, mine):
+    """name -> callable with this repository's operator signatures, running the REFERENCE's kernels: what has to be
+    exchanged in coat_b200.models.coat_llama (and the weight cache, and func_quantize) to run the decoder-layer
+    composition on the reference's operators.  Three calls have no reference counterpart and are replaced by the
+    reference calls they stand for (fp8_silu_mul_forward, fp8_mul_silu_backward, the scale-only weight pass); ONE
+    operator stays this repository's: the RMSNorm backward, because the reference's kernel waits on a device-side
+    spin lock without a bound (func_rmsnorm.py:186-196) and is not run on shared GPUs."""
+    def silu_mul_forward(gate_x, gate_s, up_x, up_s, QB, transpose_output_2d=False):
+        silu_x, silu_s = ref.fp8_silu_forward(gate_x, gate_s, QB)
+        return (silu_x, silu_s), ref.fp8_mul_forward(silu_x, silu_s, up_x, up_s, QB, transpose_output_2d)
+
+    def mul_silu_backward(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type):
+        d_silu, up_grad = ref.fp8_mul_backward(silu_x, silu_s, up_x, up_s, g, QB, fp8type,
+                                               output_quantized_transpose=True)
+        gate_grad = ref.fp8_silu_backward(gate_x, gate_s, d_silu, QB, fp8type, output_quantized_transpose=True)
+        return up_grad, gate_grad
+
+    def rmsnorm_backward(x, s_x, g, w, v, QB, num_warps, more_g=()):
+        for t in more_g:   # bf16 sums, left to right, as the separate add kernels of the reference's autograd give
+            g = g + t.reshape(g.shape)
+        return mine.fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps)
+
+    ops = {n: getattr(ref, n) for n in (
+        "fp8_add_Ifp_Ifp_Ofp_Og16", "fp8_add_Ifp_Ifp_Ofp_Opt", "fp8_division", "fp8_division_transpose",
+        "fp8_linear_backward", "fp8_linear_forward", "fp8_quantize_pertensor", "fp8_quantize_pertensor_transpose",
+        "fp8_rmsnorm_forward", "fp8_transpose", "fp8_quantize")}
+    ops.update(fp8_silu_mul_forward=silu_mul_forward, fp8_mul_silu_backward=mul_silu_backward,
+               fp8_rmsnorm_backward=rmsnorm_backward,
+               fp8_pertensor_scale=lambda w, fp8type: ref.fp8_division_transpose(w, 16, fp8type)[1])
+    return ops

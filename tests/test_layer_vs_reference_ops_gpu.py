@@ -14,12 +14,15 @@ backward, because the reference's kernel waits on a device-side spin lock withou
 call on the reference side.
 
 Tolerance stated up front: relative Frobenius error <= 2^-6 per tensor (layer output, input gradient, every weight
-gradient).  Since every operator involved is bit-identical to the reference's, the observed difference is zero,
-which the test prints."""
+gradient).  Since every operator involved is bit-identical to the reference's, the observed difference is zero for
+the output and for every gradient that does not pass through the attention backward; the query gradient of torch's
+attention kernel is accumulated with atomics (run-to-run differences of 1e-4 relative in the q projection's, the
+input's and the first norm's gradients at the full shape, on either side alike).  The test prints what it sees."""
 import pytest
 import torch
 
 from _ref import load_ref_triton
+from oracle.ref_loader import reference_layer_operators
 
 pytestmark = pytest.mark.gpu
 
@@ -59,33 +62,6 @@ def _run(layer, qargs, x, up):
     return y.detach().clone(), x.grad.detach().clone(), {n: p.grad.detach().clone() for n, p in layer.named_parameters()}
 
 
-def _reference_operators(ref, mine):
-    """name -> callable with this repository's signature, running the reference's kernels."""
-    def silu_mul_forward(gate_x, gate_s, up_x, up_s, QB, transpose_output_2d=False):
-        silu_x, silu_s = ref.fp8_silu_forward(gate_x, gate_s, QB)
-        return (silu_x, silu_s), ref.fp8_mul_forward(silu_x, silu_s, up_x, up_s, QB, transpose_output_2d)
-
-    def mul_silu_backward(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type):
-        d_silu, up_grad = ref.fp8_mul_backward(silu_x, silu_s, up_x, up_s, g, QB, fp8type,
-                                               output_quantized_transpose=True)
-        gate_grad = ref.fp8_silu_backward(gate_x, gate_s, d_silu, QB, fp8type, output_quantized_transpose=True)
-        return up_grad, gate_grad
-
-    def rmsnorm_backward(x, s_x, g, w, v, QB, num_warps, more_g=()):
-        for t in more_g:   # bf16 sums, left to right, as the separate add kernels of the reference's autograd give
-            g = g + t.reshape(g.shape)
-        return mine.fp8_rmsnorm_backward(x, s_x, g, w, v, QB, num_warps)
-
-    ops = {n: getattr(ref, n) for n in (
-        "fp8_add_Ifp_Ifp_Ofp_Og16", "fp8_add_Ifp_Ifp_Ofp_Opt", "fp8_division", "fp8_division_transpose",
-        "fp8_linear_backward", "fp8_linear_forward", "fp8_quantize_pertensor", "fp8_quantize_pertensor_transpose",
-        "fp8_rmsnorm_forward", "fp8_transpose", "fp8_quantize")}
-    ops.update(fp8_silu_mul_forward=silu_mul_forward, fp8_mul_silu_backward=mul_silu_backward,
-               fp8_rmsnorm_backward=rmsnorm_backward,
-               fp8_pertensor_scale=lambda w, fp8type: ref.fp8_division_transpose(w, 16, fp8type)[1])
-    return ops
-
-
 @pytest.mark.parametrize("shape", ["small", "llama2_7b"])
 def test_decoder_layer_equals_the_composition_of_reference_operators(shape, monkeypatch):
     ref = load_ref_triton()
@@ -99,7 +75,7 @@ def test_decoder_layer_equals_the_composition_of_reference_operators(shape, monk
     layer, qargs, x, up = _build(H, I, heads, B, S)
     ours = _run(layer, qargs, x, up)
 
-    ops = _reference_operators(ref, mine)
+    ops = reference_layer_operators(ref, mine)
     replaced = 0
     for mod in (layer_mod, cache_mod, fq):
         for name, fn in ops.items():
