@@ -187,3 +187,40 @@ def _peer_setup_worker(rank, world, port, failing_rank, how):
 def test_peer_buffer_setup_failure_reaches_every_rank_world2_gloo(failing_rank, how):
     port = 33500 + os.getpid() % 2000 + (0 if failing_rank is None else 1 + failing_rank)
     mp.spawn(_peer_setup_worker, args=(2, port, failing_rank, how), nprocs=2, join=True)
+
+
+def _verify_worker(rank, world, port, corrupt_rank):
+    """bench.verify_gathered on two gloo ranks: consistent buffers -> True on every rank; one wrong element in ONE
+    rank's copy of a peer's slot -> False on every rank."""
+    import types
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = ShardPlan([128 * 5, 77, 128 * 3 + 1, 4096], world)
+        n = plan.shard_numel
+        bounds = plan.bucket_bounds(2)
+        gen = torch.Generator().manual_seed(5)
+        shards = [torch.randn(n, generator=gen) for _ in range(world)]        # every rank can rebuild every shard
+        gathered = torch.zeros(world * n, dtype=torch.bfloat16)
+        bucket_all = []
+        for b in range(len(bounds) - 1):
+            lo, hi = int(bounds[b]) * GROUP, int(bounds[b + 1]) * GROUP
+            whole = gathered[lo * world: hi * world]
+            for r in range(world):
+                whole[r * (hi - lo):(r + 1) * (hi - lo)] = shards[r][lo:hi].to(torch.bfloat16)
+            bucket_all.append(whole)
+        if rank == corrupt_rank:
+            gathered[3] += 1.0   # element 3 of rank 0's slot in bucket 0, as seen by `corrupt_rank` only
+        opt = types.SimpleNamespace(device=torch.device("cpu"), world_size=world, rank=rank, n_buckets=len(bounds) - 1,
+                                    bounds=bounds, param=shards[rank], _bucket_all=bucket_all)
+        ok = bench.verify_gathered(opt, torch, dist)
+        assert ok == (corrupt_rank is None), (rank, ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("corrupt_rank", [None, 1])
+def test_gather_verification_of_the_benchmark_world2_gloo(corrupt_rank):
+    port = 35500 + os.getpid() % 2000 + (0 if corrupt_rank is None else 7)
+    mp.spawn(_verify_worker, args=(2, port, corrupt_rank), nprocs=2, join=True)
