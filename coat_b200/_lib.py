@@ -54,6 +54,7 @@ SIGNATURES = {
     "coat_fp8_act_backward": [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_gelu_forward": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_mul_forward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _vp],
+    "coat_fp8_mul_forward_pertensor": [_vp] * 8 + [_i64, _i64, _i, _i, _i, _i, _vp],
     "coat_fp8_mul_backward": [_vp] * 9 + [_i64, _i64, _i, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_add": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_silu_mul_forward": [_vp] * 9 + [_i64, _i64, _i, _i, _i, _i, _vp],
@@ -67,6 +68,7 @@ SIGNATURES = {
     "coat_fp8_layernorm_backward": [_vp] * 8 + [_i, _vp, _vp, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_gemm": [_vp] * 7 + [_i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_gemm_device_status": [],
+    "coat_cross_entropy_inplace": [_vp, _i, _i64, _vp, _vp, _i64, _i64, _i64, _f, _vp],
     "coat_fp8_adamw_debug_counters": [_vp],
     "coat_fp8_adamw_device_status": [],
 }

@@ -863,6 +863,223 @@ int launch_transpose_tma_fused(const void* x, uint8_t* y, uint8_t* y_t, void* s_
 }
 
 // =================================================================================================
+// 4b. fp8_mul_forward in ONE launch (mul_fwd.py:51-254: product kernel -> bf16 y + group scales, `s_y.max()`,
+//     fp8_division_transpose of y)
+// =================================================================================================
+// The two-kernel form writes the bf16 product to memory and reads it back only because the per-tensor scale
+// needs the whole tensor's maximum first: 8.4 bytes per element moved for 4.25 of inputs and outputs.  Here the
+// tile kernel's one-launch pattern is applied to the product itself: every CTA walks its 128 x 128 tiles forwards
+// (the codes of both operands and their 1x16 scales arrive by four bulk tensor copies per tile) taking the maximum
+// of |(c1 s1)(c2 s2)|, all CTAs meet at the bounded grid barrier, and the second pass walks the same tiles
+// BACKWARDS (the tail of the first pass is still in L2), recomputes the product, rounds it to bf16 as the
+// reference's intermediate tensor does, divides by the per-tensor scale and writes codes and transposed codes.
+// Bit-identical to the two-kernel form.  bf16 scales, QB = 16, M % 16 == 0, N % 128 == 0 (row pitch of the scale
+// matrices a multiple of 16 bytes); other cases take the two kernels.
+struct MulMaps { CUtensorMap q1, q2, s1, s2; };
+constexpr uint32_t kMulCodeBytes = kWT * kWT, kMulScaleBytes = kWT * (kWT / 16) * 2;
+constexpr uint32_t kMulStageBytes = 2 * kMulCodeBytes + 2 * kMulScaleBytes;
+constexpr size_t kMulSmem = (size_t)kTmaStages * kMulStageBytes + 2 * kTileTBytes + 64 + 128;
+
+template <int FMT, bool IEEE>
+__global__ void __launch_bounds__(TmaShape<8>::kThreads, 2)
+mul_pertensor_tma_kernel(const __grid_constant__ MulMaps maps, uint8_t* __restrict__ y, uint8_t* __restrict__ y_t,
+                         void* __restrict__ s_out, int scale_dtype, int M, int N, int tiles_m, int tiles_n,
+                         unsigned int* __restrict__ sync) {
+    constexpr int C = 8;
+    constexpr int kThreads = TmaShape<C>::kThreads;
+    const int n_tiles = tiles_m * tiles_n;
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 127) & ~(uintptr_t)127);
+    unsigned char* after_stages = base + (size_t)kTmaStages * kMulStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(after_stages + 2 * kTileTBytes);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int m_loc, n_loc;
+    tma_thread_origin<C>(warp, lane, m_loc, n_loc);
+    const int word = ((m_loc >> 2) + 4 * (n_loc / C)) & 31;
+    const int n_mine = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int k_end = 2 * n_mine;
+    auto tile_of = [&](int use) -> int {
+        const int i = use >= n_mine ? 2 * n_mine - 1 - use : use;
+        return (int)blockIdx.x + i * (int)gridDim.x;
+    };
+    auto issue = [&](int use) {   // thread 0 only
+        unsigned char* st = base + (size_t)(use % kTmaStages) * kMulStageBytes;
+        uint64_t* bar = &full[use % kTmaStages];
+        int tm, tn;
+        tile_coords(tile_of(use), tiles_n, tm, tn);
+        coat_tma::mbar_expect_tx(bar, kMulStageBytes);
+        coat_tma::load_2d(st, &maps.q1, tn * kWT, tm * kWT, bar);
+        coat_tma::load_2d(st + kMulCodeBytes, &maps.q2, tn * kWT, tm * kWT, bar);
+        coat_tma::load_2d(st + 2 * kMulCodeBytes, &maps.s1, tn * (kWT / 16), tm * kWT, bar);
+        coat_tma::load_2d(st + 2 * kMulCodeBytes + kMulScaleBytes, &maps.s2, tn * (kWT / 16), tm * kWT, bar);
+    };
+    auto give_up = [&](int use) {   // a wait ran out (never expected): leave only after our copies in flight have landed
+        if (threadIdx.x == 0) {
+            g_quant_device_status = COAT_E_TIMEOUT;
+            for (int q = 0; q < kTmaStages; ++q)
+                if (use + q < k_end)
+                    coat_tma::mbar_wait(&full[(use + q) % kTmaStages], (uint32_t)((use + q) / kTmaStages) & 1u, kTmaWaitLimit);
+        }
+        __syncthreads();
+        pertensor_depart(sync);
+    };
+    // the four rows x eight columns of this thread: (c1 s1) (c2 s2) in fp32, as the reference's product kernel
+    auto products = [&](const unsigned char* st, float (&v)[4][C]) {
+        const __nv_bfloat16* s1 = reinterpret_cast<const __nv_bfloat16*>(st + 2 * kMulCodeBytes);
+        const __nv_bfloat16* s2 = reinterpret_cast<const __nv_bfloat16*>(st + 2 * kMulCodeBytes + kMulScaleBytes);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int row = m_loc + j;
+            const uint2 a = *reinterpret_cast<const uint2*>(st + row * kWT + n_loc);
+            const uint2 b = *reinterpret_cast<const uint2*>(st + kMulCodeBytes + row * kWT + n_loc);
+            const float sa = __bfloat162float(s1[row * (kWT / 16) + (n_loc >> 4)]);
+            const float sb = __bfloat162float(s2[row * (kWT / 16) + (n_loc >> 4)]);
+            float fa[8], fb[8];
+            coat_fp8x4_to_float4<FMT>(a.x, *reinterpret_cast<float (*)[4]>(&fa[0]));
+            coat_fp8x4_to_float4<FMT>(a.y, *reinterpret_cast<float (*)[4]>(&fa[4]));
+            coat_fp8x4_to_float4<FMT>(b.x, *reinterpret_cast<float (*)[4]>(&fb[0]));
+            coat_fp8x4_to_float4<FMT>(b.y, *reinterpret_cast<float (*)[4]>(&fb[4]));
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const float2 x1 = __fmul2_rn(make_float2(fa[i], fa[i + 1]), make_float2(sa, sa));
+                const float2 x2 = __fmul2_rn(make_float2(fb[i], fb[i + 1]), make_float2(sb, sb));
+                const float2 pr = __fmul2_rn(x1, x2);
+                v[j][i] = pr.x; v[j][i + 1] = pr.y;
+            }
+        }
+    };
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kTmaStages; ++s) coat_tma::mbar_init(&full[s], 1);
+        coat_tma::mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < kTmaStages; ++s)
+            if (s < k_end) issue(s);
+    }
+    // ---- pass 1: the tensor's maximum
+    int k = 0;
+    float amax = 0.f;
+    for (; k < n_mine; ++k) {
+        const unsigned char* st = base + (size_t)(k % kTmaStages) * kMulStageBytes;
+        const bool arrived = coat_tma::mbar_wait(&full[k % kTmaStages], (uint32_t)(k / kTmaStages) & 1u, kTmaWaitLimit);
+        float v[4][C];
+        products(st, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) amax = fmaxf(amax, absmax_cols<C>(v[j]));   // parts outside the matrix are zero-filled
+        if (!__syncthreads_and(arrived)) { give_up(k); return; }
+        if (threadIdx.x == 0 && k + kTmaStages < k_end) issue(k + kTmaStages);
+    }
+    amax = coat_warp_max(amax);
+    float* wmax = reinterpret_cast<float*>(after_stages);   // the transposed-tile buffer is free until the second pass
+    if (lane == 0) wmax[warp] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = wmax[0];
+        for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, wmax[w]);
+        atomicMax(&sync[0], __float_as_uint(m));
+    }
+    unsigned int amax_word;
+    if (!grid_barrier_once(&sync[1], &sync[0], &amax_word)) { give_up(k); return; }
+    const float scalar = tensor_scale_from_amax<FMT, IEEE>(&amax_word, scale_dtype);
+    if (s_out && blockIdx.x == 0 && threadIdx.x == 0) store_scale(s_out, 0, scale_dtype, scalar);
+    const ScaleDivider<IEEE> by_scalar(scalar);
+    // ---- pass 2: the same tiles in reverse order
+    for (; k < k_end; ++k) {
+        const int t = tile_of(k);
+        const unsigned char* st = base + (size_t)(k % kTmaStages) * kMulStageBytes;
+        uint32_t (*tile_t)[32] = reinterpret_cast<uint32_t (*)[32]>(after_stages + (size_t)(k & 1) * kTileTBytes);
+        const bool arrived = coat_tma::mbar_wait(&full[k % kTmaStages], (uint32_t)(k / kTmaStages) & 1u, kTmaWaitLimit);
+        float v[4][C];
+        products(st, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < C; ++i) v[j][i] = __bfloat162float(__float2bfloat16_rn(v[j][i]));   // the reference's bf16 y
+        int tm, tn;
+        tile_coords(t, tiles_n, tm, tn);
+        const int m_tile = tm * kWT, n_tile = tn * kWT;
+        const int m0 = m_tile + m_loc, n0 = n_tile + n_loc;
+        const bool inside = m0 < M && n0 < N;
+        if (IEEE || by_scalar.fast) {
+            const GroupScaleDivider<IEEE> d(scalar);
+            if (inside) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) store_row_codes<FMT, C>(y + (int64_t)(m0 + j) * N + n0, v[j], d);
+            }
+#pragma unroll
+            for (int i = 0; i < C; ++i) {
+                const float2 lo = d.pair(v[0][i], v[1][i]), hi = d.pair(v[2][i], v[3][i]);
+                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(lo.x, lo.y, hi.x, hi.y);
+            }
+        } else {
+            const DivFullDivider d{scalar};
+            if (inside) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) store_row_codes<FMT, C>(y + (int64_t)(m0 + j) * N + n0, v[j], d);
+            }
+#pragma unroll
+            for (int i = 0; i < C; ++i)
+                tile_t[n_loc + i][word] = coat_float4_to_fp8x4<FMT>(d(v[0][i]), d(v[1][i]), d(v[2][i]), d(v[3][i]));
+        }
+        if (!__syncthreads_and(arrived)) { give_up(k); return; }
+        if (threadIdx.x == 0 && k + kTmaStages < k_end) issue(k + kTmaStages);
+#pragma unroll
+        for (int it = 0; it < kWT * 8 / kThreads; ++it) {   // transposed rows leave in 16-byte pieces
+            const int idx = it * kThreads + threadIdx.x;
+            const int r = idx >> 3, c = idx & 7;
+            const int n = n_tile + r, m = m_tile + c * 16;
+            if (n < N && m < M)
+                *reinterpret_cast<uint4*>(y_t + (int64_t)n * M + m) =
+                    *reinterpret_cast<const uint4*>(&tile_t[r][(4 * c + 4 * (r / C)) & 31]);
+        }
+    }
+    pertensor_depart(sync);
+}
+
+template <int FMT, bool IEEE>
+int launch_mul_pertensor(const uint8_t* x1, const void* s1, const uint8_t* x2, const void* s2, uint8_t* y, uint8_t* y_t,
+                         void* s_out, int scale_dtype, unsigned int* sync, int64_t M, int64_t N, cudaStream_t st) {
+    MulMaps maps;
+    if (!coat_tma::make_map_2d(&maps.q1, x1, 1, M, N, N, kWT, kWT) || !coat_tma::make_map_2d(&maps.q2, x2, 1, M, N, N, kWT, kWT) ||
+        !coat_tma::make_map_2d(&maps.s1, s1, 2, M, N / 16, (N / 16) * 2, kWT, kWT / 16) ||
+        !coat_tma::make_map_2d(&maps.s2, s2, 2, M, N / 16, (N / 16) * 2, kWT, kWT / 16))
+        return COAT_E_DEVICE;
+    auto kern = mul_pertensor_tma_kernel<FMT, IEEE>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMulSmem) != cudaSuccess)
+        return COAT_E_LAUNCH;
+    static int ctas_per_sm = 0;   // per instantiation
+    if (ctas_per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, TmaShape<8>::kThreads, kMulSmem) != cudaSuccess || n < 1)
+            return COAT_E_LAUNCH;
+        ctas_per_sm = n;
+    }
+    const int64_t tiles_n = (N + kWT - 1) / kWT, tiles_m = (M + kWT - 1) / kWT;
+    const int64_t n_tiles = tiles_n * tiles_m;
+    const int64_t cap = (int64_t)coat_sm_count() * ctas_per_sm;
+    const int grid = (int)(n_tiles < cap ? n_tiles : cap);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(TmaShape<8>::kThreads);
+    cfg.dynamicSmemBytes = kMulSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeCooperative;
+    attr.val.cooperative = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, maps, y, y_t, s_out, scale_dtype, (int)M, (int)N, (int)tiles_m, (int)tiles_n, sync) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return COAT_E_LAUNCH;
+    }
+    return coat_launch_status();
+}
+
+// =================================================================================================
 // 5. byte transpose (_transpose.py:39-82)
 // =================================================================================================
 __global__ void __launch_bounds__(kTileThreads)
@@ -1091,6 +1308,29 @@ extern "C" int coat_fp8_quantize_device_status(void) {
     if (cudaMemcpyFromSymbol(&v, g_quant_device_status, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
     if (v != 0 && cudaMemcpyToSymbol(g_quant_device_status, &zero, sizeof(int)) != cudaSuccess) return COAT_E_LAUNCH;
     return v;
+}
+
+// fp8_mul_forward with a per-tensor output in one cooperative launch (see mul_pertensor_tma_kernel): q = fp8(bf16((c1 s1)(c2 s2)) / s),
+// q_t its transpose, *s_out = s = the maximum of the rounded 1xQB group scales of the product.  sync_words as for
+// coat_fp8_quantize_pertensor.  COAT_E_SHAPE unless QB == 16, M % 16 == 0 and N % 128 == 0 (use coat_fp8_mul_forward +
+// coat_fp8_division there); scales must be bf16.
+extern "C" int coat_fp8_mul_forward_pertensor(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                                              uint8_t* y, uint8_t* y_t, void* s_out, unsigned int* sync_words, int64_t M,
+                                              int64_t N, int QB, int fmt, int scale_dtype, int flags, void* stream) {
+    if (M < 0 || N < 0 || (fmt != COAT_E4M3 && fmt != COAT_E5M2)) return COAT_E_BADARG;
+    if (M == 0 || N == 0) return COAT_OK;
+    if (!x1 || !s_x1 || !x2 || !s_x2 || !y || !y_t || !s_out || !sync_words) return COAT_E_BADARG;
+    if (scale_dtype != COAT_BF16 || (flags & COAT_QUANT_STOCHASTIC)) return COAT_E_BADARG;
+    if (QB != 16 || M % 16 != 0 || N % 128 != 0 || !tma_tiles_fit(M, N)) return COAT_E_SHAPE;
+    if (!coat_aligned(x1, 16) || !coat_aligned(x2, 16) || !coat_aligned(s_x1, 16) || !coat_aligned(s_x2, 16) ||
+        !coat_aligned(y, 16) || !coat_aligned(y_t, 16)) return COAT_E_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool ieee = flags & COAT_QUANT_IEEE_DIV;
+    if (fmt == COAT_E4M3)
+        return ieee ? launch_mul_pertensor<COAT_E4M3, true>(x1, s_x1, x2, s_x2, y, y_t, s_out, scale_dtype, sync_words, M, N, st)
+                    : launch_mul_pertensor<COAT_E4M3, false>(x1, s_x1, x2, s_x2, y, y_t, s_out, scale_dtype, sync_words, M, N, st);
+    return ieee ? launch_mul_pertensor<COAT_E5M2, true>(x1, s_x1, x2, s_x2, y, y_t, s_out, scale_dtype, sync_words, M, N, st)
+                : launch_mul_pertensor<COAT_E5M2, false>(x1, s_x1, x2, s_x2, y, y_t, s_out, scale_dtype, sync_words, M, N, st);
 }
 
 // Diagnostic: number of polls a CTA spends at the grid barrier of the one-launch per-tensor kernels before it gives up

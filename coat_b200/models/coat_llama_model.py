@@ -11,7 +11,8 @@ cross-entropy loss; `make_state_dict_compatible` renames the keys of a stock Lla
 The classes are plain `nn.Module`s (no `PreTrainedModel` base, no generation or KV-cache plumbing: this is the
 training model), so they do not depend on a particular transformers release.  The rotary tables are computed
 once per forward and shared by all layers.  The loss is the token-mean cross entropy of the shifted logits,
-computed in chunks of rows so that the fp32 logits of the whole batch never exist at once (the reference
+computed in chunks of rows so that the fp32 logits of the whole batch never exist at once, each chunk through the
+cross-entropy kernel that writes the gradient in place of the logits (the reference
 delegates this to a fused linear-cross-entropy from Liger, coat_llama.py:1407-1411; it is not part of the FP8
 path).
 """
@@ -21,6 +22,8 @@ from typing import NamedTuple, Optional
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+from ..activation.liger.cross_entropy import LigerCrossEntropyFunction
 
 from ..activation.real_quantization.func_quantize import Coat_quantize_bgn, Coat_quantize_end
 from ..utils._fp8_quantization_config import QuantizationConfig
@@ -110,7 +113,13 @@ def chunked_causal_lm_loss(hidden, lm_head_weight, labels, ignore_index=-100, ch
     total = hidden.new_zeros((), dtype=torch.float32)
     for i in range(0, h.shape[0], chunk_rows):
         logits = F.linear(h[i:i + chunk_rows], lm_head_weight).float()
-        total = total + F.cross_entropy(logits, y[i:i + chunk_rows], ignore_index=ignore_index, reduction="sum")
+        if logits.is_cuda:
+            # the loss head of the reference (LigerForCausalLMLoss): the gradient overwrites the chunk's logits, so
+            # autograd keeps no second [rows, vocabulary] tensor (log-softmax) per chunk
+            part, _ = LigerCrossEntropyFunction.apply(logits, y[i:i + chunk_rows], ignore_index, 0.0, 0.0, "sum")
+        else:   # evaluation on the host (tests of the model's plumbing)
+            part = F.cross_entropy(logits, y[i:i + chunk_rows], ignore_index=ignore_index, reduction="sum")
+        total = total + part
     return total / n_valid
 
 

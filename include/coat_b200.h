@@ -286,6 +286,17 @@ int coat_fp8_mul_forward(const uint8_t* x1, const void* s_x1, const uint8_t* x2,
                          void* y_bf16, void* s_y, unsigned int* amax_bits, int64_t M, int64_t N, int QB,
                          int fmt, int scale_dtype, int flags, void* stream);
 
+/* fp8_mul_forward with its per-tensor output in ONE cooperative launch (replaces the whole of fp8_mul_forward,
+ * mul_fwd.py:191-254: product kernel :51-188, `s_y.max()`, fp8_division_transpose): y = fp8(bf16((c1 s1)(c2 s2)) / s)
+ * [M,N], y_t its transpose [N,M], *s_out = s = the maximum of the rounded 1x16 group scales of the product.  The
+ * product is recomputed from the FP8 inputs in a second pass instead of going through a bf16 tensor in memory;
+ * results are bit-identical to coat_fp8_mul_forward + coat_fp8_division.  sync_words: 12 bytes of caller scratch,
+ * zero on entry and zero again on return (as for coat_fp8_quantize_pertensor).  bf16 scales only; COAT_E_SHAPE unless
+ * QB == 16, M % 16 == 0 and N % 128 == 0 (use the two calls there); all pointers 16-byte aligned. */
+int coat_fp8_mul_forward_pertensor(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
+                                   uint8_t* y, uint8_t* y_t, void* s_out, unsigned int* sync_words, int64_t M,
+                                   int64_t N, int QB, int fmt, int scale_dtype, int flags, void* stream);
+
 /* y1 = bf16(g * x2), y2 = bf16(g * x1) with group scales (bf16) and tensor amax of y2.  Replaces the kernel
  * of fp8_mul_backward (mul_bwd.py:221-315, kernel :49-218). */
 int coat_fp8_mul_backward(const uint8_t* x1, const void* s_x1, const uint8_t* x2, const void* s_x2,
@@ -400,6 +411,15 @@ int coat_fp8_gemm_blockscaled(const uint8_t* a, const float* scale_a, int64_t ld
 int coat_rope_bf16(const void* x, int64_t sxb, int64_t sxs, int64_t sxh, const void* cos_t, const void* sin_t,
                    void* y, int64_t B, int64_t S, int64_t H, int64_t D, int64_t cos_batch_stride, int backward,
                    void* stream);
+
+/* Cross-entropy loss with the gradient written in place of the logits: replaces liger_cross_entropy_kernel as
+ * cross_entropy_forward launches it for the loss head (coat/activation/liger/cross_entropy.py:25-198, :212-278; hard
+ * labels, label_smoothing = lse_square_scale = 0, no soft-capping: the configuration LigerForCausalLMLoss uses,
+ * :387-410).  x [rows, V], fp32 or bf16, row pitch ld elements, is overwritten with d(sum of the returned losses)/dx;
+ * loss[r] = (logsumexp(x_r) - x_r[target_r]) * inv_n; rows whose target equals ignore_index get zero loss and zero
+ * gradients.  inv_n = 1 / (number of counted rows) for the mean reduction, 1 for the sum. */
+int coat_cross_entropy_inplace(void* x, int x_dtype, int64_t ld, const int64_t* target, float* loss, int64_t rows,
+                               int64_t V, int64_t ignore_index, float inv_n, void* stream);
 
 /*
  * Debug / health entry points of the optimizer kernels (no counterpart in the reference).

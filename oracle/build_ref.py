@@ -16,8 +16,8 @@ machine as built files):
 
 2. ``coat_ref/``: an importable staging of the reference's python operator layer
    (coat/activation/real_quantization/*.py, the Triton kernels and their
-   wrappers; coat/optimizer/fp8_adamw.py with the one configuration class it
-   imports).  The files are byte-for-byte the reference's; only the package
+   wrappers; coat/activation/liger/*.py, the loss head; coat/optimizer/fp8_adamw.py
+   with the one configuration class it imports).  The files are byte-for-byte the reference's; only the package
    root is renamed so that it cannot shadow, or be shadowed by, anything else.
    The module that drags in plotting and model code (fp8linear.py) is left out.
    On a GPU the parity tests run these Triton kernels next to the CUDA kernels
@@ -38,6 +38,7 @@ _STAGED = {
     # reference directory -> (destination under coat_ref/, file filter)
     ("coat", "activation", "real_quantization"): (("activation", "real_quantization"),
                                                   lambda n: n.endswith(".py") and n != "fp8linear.py"),
+    ("coat", "activation", "liger"): (("activation", "liger"), lambda n: n.endswith(".py")),
     ("coat", "optimizer"): (("optimizer",), lambda n: n == "fp8_adamw.py"),
     ("coat", "utils"): (("utils",), lambda n: n == "_fp8_quantization_config.py"),
 }

@@ -130,3 +130,15 @@ def reference_layer_operators(ref, mine):
                fp8_rmsnorm_backward=rmsnorm_backward,
                fp8_pertensor_scale=lambda w, fp8type: ref.fp8_division_transpose(w, 16, fp8type)[1])
     return ops
+
+
+def load_ref_liger():
+    """The reference's loss-head module (coat/activation/liger/cross_entropy.py, staged unmodified), or None."""
+    if not os.path.exists(os.path.join(REF_DIR, "coat_ref", "activation", "liger", "cross_entropy.py")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        return importlib.import_module("coat_ref.activation.liger.cross_entropy")
+    except Exception:
+        return None

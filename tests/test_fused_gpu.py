@@ -315,3 +315,27 @@ def test_silu_mul_forward_equals_the_two_operators(flags):
     u8 = lambda t: t.view(torch.uint8)
     assert torch.equal(u8(f_silu_q), u8(silu_q)) and torch.equal(f_silu_s, silu_s)
     assert f_mul_s == mul_s and torch.equal(u8(f_mul_q), u8(mul_q)) and torch.equal(u8(f_mul_t), u8(mul_t))
+
+
+@pytest.mark.parametrize("M,N", [(256, 384), (1040, 1280), (4096, 11008)])
+@pytest.mark.parametrize("flags", [0, IEEE])
+def test_mul_forward_one_launch_equals_the_two_kernel_form(M, N, flags):
+    """fp8_mul_forward as one cooperative launch (the product recomputed from the FP8 inputs in the second pass)
+    against the two-kernel form (bf16 product in memory + division/transpose): same scale, codes and transposed
+    codes, in both division modes; ragged tile edges (1040 rows = 8 tiles + 16 rows) included."""
+    r = R()
+    from coat_b200 import _lib
+    from coat_b200.activation.real_quantization import _ops
+    q1, s1 = qinput(M, N, 31)
+    q2, s2 = qinput(M, N, 32, scale=3.0)
+    args = (q1.cuda(), s1.cuda(), q2.cuda(), s2.cuda(), QB)
+    assert _ops._ONE_LAUNCH
+    one = r.fp8_mul_forward(*args, flags=flags)
+    try:
+        _ops._ONE_LAUNCH = False
+        two = r.fp8_mul_forward(*args, flags=flags)
+    finally:
+        _ops._ONE_LAUNCH = True
+    for a, b in zip(one, two):
+        same(a, b)
+    assert _lib.lib().coat_fp8_quantize_device_status() == 0
