@@ -46,6 +46,7 @@ SIGNATURES = {
     "coat_fp8_quantize_transpose": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_quantize_pertensor_static": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],
     "coat_rope_bf16": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "coat_rope_bf16_f32tables": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "coat_fp8_gemm_blockscaled": [_vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _vp],
     "coat_fp8_quantize_block128": [_vp, _i64, _i64, _i64] + [_vp] * 8 + [_i, _i, _i, _i, _vp],
     "coat_fp8_transpose": [_vp, _vp, _i64, _i64, _vp],

@@ -23,4 +23,4 @@ from .silu_bwd import fp8_silu_backward  # noqa: F401
 from .silu_fwd import fp8_silu_forward  # noqa: F401
 from .linear import fp8_linear_backward, fp8_linear_forward  # noqa: F401
 from ._quantize_transpose import fp8_quantize_transpose  # noqa: F401
-from ._fused import fp8_mul_silu_backward, fp8_silu_mul_forward  # noqa: F401  (extensions: the gated product's two operators in one kernel, forward and backward)
+from ._fused import fp8_mul_silu_backward, fp8_mul_silu_backward_joint, fp8_silu_mul_forward  # noqa: F401  (extensions: the gated product's two operators in one kernel, forward and backward)

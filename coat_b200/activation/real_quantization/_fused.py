@@ -217,6 +217,43 @@ def fp8_mul_silu_backward(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8
     return (_unflat(q_up, bs), smax_up, q_up_t), (_unflat(q_gate, bs), smax_gate, q_gate_t)
 
 
+def fp8_mul_silu_backward_joint(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type, *, flags=None):
+    """Backward of `silu(gate) * up` when the up and gate projections are ONE fused linear layer (the OLMo block,
+    coat/models/coat_olmo.py:596-611 of the reference): the gradients d_up and d_gate are concatenated along the last
+    dimension and quantised per tensor with the larger of their two scales,
+        fp8_division_transpose(cat([d_up, d_gate], -1), QB, fp8type, max(cat([s_up_groups, s_gate_groups])))
+    with d_up, d_gate and the group scales as fp8_mul_backward and fp8_silu_backward return them.  Returns
+    (codes [M, 2N], scale, transposed codes [2N, M]); same bits.  One elementwise kernel leaves both bf16 gradients
+    and their common amax; two division passes write the transposed codes straight into the halves of the joint
+    buffer, and only the one-byte codes are concatenated."""
+    (a, sa, b, sb, c, sc, g2), bs = _flat(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g)
+    assert a.shape == b.shape == c.shape == g2.shape and sa.shape == sb.shape == sc.shape
+    assert a.dtype == b.dtype == c.dtype and sa.dtype == sb.dtype == sc.dtype
+    M, N = a.shape
+    fp8type = _fp8_dtype(fp8type)
+    dev = a.device
+    y_up = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    y_gate = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    s_up = torch.empty(sa.shape, dtype=torch.bfloat16, device=dev)
+    s_gate = torch.empty(sa.shape, dtype=torch.bfloat16, device=dev)
+    amax = _amax_word(dev)   # one word for both gradients: the maximum over the concatenation
+    q_up = torch.empty((M, N), dtype=fp8type, device=dev)
+    q_gate = torch.empty((M, N), dtype=fp8type, device=dev)
+    q_t = torch.empty((2 * N, M), dtype=fp8type, device=dev)
+    s_max = torch.empty((), dtype=torch.bfloat16, device=dev)
+    fmt = _lib.fp8_format(fp8type)[0]
+    with torch.cuda.device(dev):
+        _call("coat_fp8_mul_silu_backward", a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(), c.data_ptr(),
+              sc.data_ptr(), g2.data_ptr(), y_up.data_ptr(), s_up.data_ptr(), amax.data_ptr(), y_gate.data_ptr(),
+              s_gate.data_ptr(), amax.data_ptr(), M, N, QB, _lib.fp8_enum_of(a), _lib.float_dtype(sa),
+              _lib.float_dtype(g2), fmt, _flags(flags), _lib.stream_ptr(dev))
+        for y, q, rows in ((y_up, q_up, q_t[:N]), (y_gate, q_gate, q_t[N:])):
+            _call("coat_fp8_division", y.data_ptr(), q.data_ptr(), rows.data_ptr(), None, s_max.data_ptr(),
+                  amax.data_ptr(), M, N, N, fmt, _lib.float_dtype(y), _lib.float_dtype(torch.bfloat16), _flags(flags),
+                  _lib.stream_ptr(dev))
+    return _unflat(torch.cat((q_up, q_gate), dim=-1), bs), s_max, q_t
+
+
 def _add(x1, x2, QB, fp8type, want_codes, want_amax, flags):
     (a, b), bs = _flat(x1, x2)
     assert a.shape == b.shape

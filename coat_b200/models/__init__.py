@@ -12,3 +12,11 @@ from .coat_llama_model import (  # noqa: F401
     chunked_causal_lm_loss,
     make_state_dict_compatible,
 )
+from .coat_olmo import (  # noqa: F401
+    CoatOLMoAfterAttentionResidual,
+    CoatOLMoBeforeAttentionResidual,
+    CoatOLMoBlock,
+    CoatOLMoConfig,
+    CoatOLMoMLPResidual,
+    CoatOLMoSequentialBlock,
+)

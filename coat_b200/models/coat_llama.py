@@ -387,8 +387,8 @@ def _rotate_half(x):
 
 
 class _FusedRotary(torch.autograd.Function):
-    """y = x * cos + rotate_half(x) * sin on bf16 [B, S, H, D] in one kernel (coat_rope_bf16); the backward pass is
-    the same kernel with the transposed rotation."""
+    """y = x * cos + rotate_half(x) * sin on bf16 [B, S, H, D] in one kernel (coat_rope_bf16, or its variant for fp32
+    cos / sin tables); the backward pass is the same kernel with the transposed rotation."""
 
     @staticmethod
     def _run(x4, cos, sin, backward):
@@ -396,10 +396,10 @@ class _FusedRotary(torch.autograd.Function):
         B, S, H, D = x4.shape
         y = torch.empty((B, S, H, D), dtype=x4.dtype, device=x4.device)
         with torch.cuda.device(x4.device):
-            rc = _lib.lib().coat_rope_bf16(x4.data_ptr(), x4.stride(0), x4.stride(1), x4.stride(2), cos.data_ptr(),
-                                           sin.data_ptr(), y.data_ptr(), B, S, H, D,
-                                           0 if cos.shape[0] == 1 else cos.stride(0), int(backward),
-                                           _lib.stream_ptr(x4.device))
+            fn = _lib.lib().coat_rope_bf16 if cos.dtype == torch.bfloat16 else _lib.lib().coat_rope_bf16_f32tables
+            rc = fn(x4.data_ptr(), x4.stride(0), x4.stride(1), x4.stride(2), cos.data_ptr(), sin.data_ptr(),
+                    y.data_ptr(), B, S, H, D, 0 if cos.shape[0] == 1 else cos.stride(0), int(backward),
+                    _lib.stream_ptr(x4.device))
         _lib.check(rc, "rope_bf16")
         return y
 

@@ -412,6 +412,13 @@ int coat_rope_bf16(const void* x, int64_t sxb, int64_t sxs, int64_t sxh, const v
                    void* y, int64_t B, int64_t S, int64_t H, int64_t D, int64_t cos_batch_stride, int backward,
                    void* stream);
 
+/* coat_rope_bf16 with fp32 cos / sin tables: the rotary embedding in full precision of the OLMo blocks
+ * (coat/models/coat_olmo.py:866-868 calls the host trainer's RotaryEmbedding, which multiplies in fp32 and rounds
+ * once to bf16 when rope_full_precision is set). */
+int coat_rope_bf16_f32tables(const void* x, int64_t sxb, int64_t sxs, int64_t sxh, const void* cos_t,
+                             const void* sin_t, void* y, int64_t B, int64_t S, int64_t H, int64_t D,
+                             int64_t cos_batch_stride, int backward, void* stream);
+
 /* Cross-entropy loss with the gradient written in place of the logits: replaces liger_cross_entropy_kernel as
  * cross_entropy_forward launches it for the loss head (coat/activation/liger/cross_entropy.py:25-198, :212-278; hard
  * labels, label_smoothing = lse_square_scale = 0, no soft-capping: the configuration LigerForCausalLMLoss uses,

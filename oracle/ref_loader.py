@@ -102,9 +102,10 @@ def load_ref_optimizer():
 
 def reference_layer_operators(ref, mine):
     """name -> callable with this repository's operator signatures, running the REFERENCE's kernels: what has to be
-    exchanged in coat_b200.models.coat_llama (and the weight cache, and func_quantize) to run the decoder-layer
-    composition on the reference's operators.  Three calls have no reference counterpart and are replaced by the
-    reference calls they stand for (fp8_silu_mul_forward, fp8_mul_silu_backward, the scale-only weight pass); ONE
+    exchanged in coat_b200.models.coat_llama / coat_olmo (and the weight cache, and func_quantize) to run the
+    decoder-layer composition on the reference's operators.  Four calls have no reference counterpart and are replaced
+    by the reference calls they stand for (fp8_silu_mul_forward, fp8_mul_silu_backward, fp8_mul_silu_backward_joint,
+    the scale-only weight pass); ONE
     operator stays this repository's: the RMSNorm backward, because the reference's kernel waits on a device-side
     spin lock without a bound (func_rmsnorm.py:186-196) and is not run on shared GPUs."""
     def silu_mul_forward(gate_x, gate_s, up_x, up_s, QB, transpose_output_2d=False):
@@ -117,6 +118,15 @@ def reference_layer_operators(ref, mine):
         gate_grad = ref.fp8_silu_backward(gate_x, gate_s, d_silu, QB, fp8type, output_quantized_transpose=True)
         return up_grad, gate_grad
 
+    def mul_silu_backward_joint(silu_x, silu_s, up_x, up_s, gate_x, gate_s, g, QB, fp8type):
+        import torch
+        # the OLMo block's sequence (coat/models/coat_olmo.py:596-611)
+        mul_g1, (mul_g2, mul_gs2) = ref.fp8_mul_backward(silu_x, silu_s, up_x, up_s, g, QB, fp8type)
+        silu_g, silu_gs = ref.fp8_silu_backward(gate_x, gate_s, mul_g1, QB, fp8type)
+        gateup_g = torch.cat([mul_g2, silu_g], dim=-1)
+        gateup_gs = torch.max(torch.cat([mul_gs2, silu_gs]))
+        return ref.fp8_division_transpose(gateup_g, QB, fp8type, gateup_gs, stochastic=False)
+
     def rmsnorm_backward(x, s_x, g, w, v, QB, num_warps, more_g=()):
         for t in more_g:   # bf16 sums, left to right, as the separate add kernels of the reference's autograd give
             g = g + t.reshape(g.shape)
@@ -125,8 +135,10 @@ def reference_layer_operators(ref, mine):
     ops = {n: getattr(ref, n) for n in (
         "fp8_add_Ifp_Ifp_Ofp_Og16", "fp8_add_Ifp_Ifp_Ofp_Opt", "fp8_division", "fp8_division_transpose",
         "fp8_linear_backward", "fp8_linear_forward", "fp8_quantize_pertensor", "fp8_quantize_pertensor_transpose",
-        "fp8_rmsnorm_forward", "fp8_transpose", "fp8_quantize")}
+        "fp8_rmsnorm_forward", "fp8_transpose", "fp8_quantize", "fp8_layernorm_noparam_forward",
+        "fp8_layernorm_noparam_backward")}
     ops.update(fp8_silu_mul_forward=silu_mul_forward, fp8_mul_silu_backward=mul_silu_backward,
+               fp8_mul_silu_backward_joint=mul_silu_backward_joint,
                fp8_rmsnorm_backward=rmsnorm_backward,
                fp8_pertensor_scale=lambda w, fp8type: ref.fp8_division_transpose(w, 16, fp8type)[1])
     return ops
