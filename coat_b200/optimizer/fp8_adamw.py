@@ -32,6 +32,52 @@ _TABLE_DTYPE = np.dtype([(n, np.uint64) for n in
                         + [("numel", np.int64)])
 
 
+def _dtensor_type():
+    try:
+        from torch.distributed.tensor import DTensor
+    except Exception:   # a torch without the distributed tensor package
+        return None
+    return DTensor
+
+
+def local_tensor(t):
+    """The tensor the kernels see: a DTensor's local shard (FSDP2 / `fully_shard` parameters, their gradients and the
+    optimizer state kept as DTensors), anything else as it is."""
+    DTensor = _dtensor_type()
+    if DTensor is not None and isinstance(t, DTensor):
+        return t._local_tensor
+    return t
+
+
+def _group_state_layout(p, group_size):
+    """For a DTensor parameter: (global shape, placements) under which a per-group vector of the LOCAL shard is itself a
+    shard of one global tensor, or None when the groups of the local shards do not line up with the groups of the
+    flattened full tensor.  They line up when the parameter is sharded along dimension 0 only (what `fully_shard` does)
+    and every row holds a whole number of groups: then rank r's groups are rows of the [rows, row_numel / group_size]
+    matrix of group values, sharded along dimension 0 exactly like the parameter, and a checkpoint of the sharded state
+    is a checkpoint of the unsharded state cut along rows, whatever the world size.  One-dimensional parameters qualify
+    when every rank's chunk (ceil(n / world) elements, the last one shorter) is a multiple of the group size."""
+    from torch.distributed.tensor import Replicate, Shard
+    placements = tuple(p.placements)
+    sharded = [pl for pl in placements if not isinstance(pl, Replicate)]
+    if not sharded:   # replicated everywhere: the local tensor is the full tensor
+        return (-(-p.numel() // group_size),), placements
+    if len(sharded) != 1 or not isinstance(sharded[0], Shard) or sharded[0].dim != 0 or p.dim() == 0:
+        return None
+    row = p.numel() // p.shape[0] if p.shape[0] else 0
+    if p.dim() >= 2 and row % group_size == 0 and row > 0:
+        return (p.shape[0], row // group_size), placements
+    if p.dim() == 1:
+        world = 1
+        for pl, size in zip(placements, p.device_mesh.shape):
+            if isinstance(pl, Shard):
+                world = size
+        chunk = -(-p.shape[0] // world)
+        if chunk % group_size == 0:
+            return (-(-p.shape[0] // group_size),), placements
+    return None
+
+
 class CoatAdamW(Optimizer):
     def __init__(
         self,
@@ -74,6 +120,7 @@ class CoatAdamW(Optimizer):
         the bf16 tensor, inside the same kernel (no separate cast pass).  An extension: the reference leaves the
         cast to the surrounding framework."""
         for master, copy in pairs:
+            master = local_tensor(master)   # a DTensor parameter: the copy mirrors this rank's shard
             if copy.dtype != torch.bfloat16 or copy.numel() != master.numel() or not copy.is_contiguous() \
                     or copy.device != master.device:
                 raise ValueError("a bf16 copy must be a contiguous bfloat16 tensor of the parameter's size and device")
@@ -172,6 +219,9 @@ class CoatAdamW(Optimizer):
             raise RuntimeError("CoatAdamW does not support amsgrad")
         q = self.qargs
         state["step"] = torch.tensor(0.0)
+        lp = local_tensor(p)
+        if lp is not p:
+            return self._init_sharded_state(state, p, lp, use_expansion)
         groups = (p.numel() + q.qgroup_size - 1) // q.qgroup_size
         vec = dict(device=p.device, dtype=p.dtype)
         state["exp_avg"] = torch.zeros_like(p, dtype=convert_str_to_fp8[q.first_order_bit],
@@ -186,6 +236,44 @@ class CoatAdamW(Optimizer):
         if use_expansion:
             state["expand_exp_avg_sq"] = torch.ones(groups, **vec)
             state["sqrt_minmax_exp_avg_sq"] = torch.ones(groups, **vec)
+        return state
+
+    def _init_sharded_state(self, state, p, lp, use_expansion):
+        """State of a DTensor parameter (FSDP2): every rank quantises its local shard in groups of 128 counted from the
+        start of the shard.  The moments are DTensors laid out like the parameter; the per-group vectors are DTensors
+        too wherever the local groups are the groups of the full tensor (_group_state_layout), so that
+        torch.distributed.checkpoint and get_optimizer_state_dict see one global state; otherwise they stay plain
+        rank-local tensors (training works, the state of that parameter is then specific to the world size)."""
+        from torch.distributed.tensor import DTensor
+        q = self.qargs
+        mesh, placements = p.device_mesh, tuple(p.placements)
+        layout = _group_state_layout(p, q.qgroup_size)
+        groups = (lp.numel() + q.qgroup_size - 1) // q.qgroup_size
+        vec = dict(device=lp.device, dtype=lp.dtype)
+
+        def like_param(dtype):
+            local = torch.zeros_like(lp, dtype=dtype, memory_format=torch.contiguous_format)
+            return DTensor.from_local(local, mesh, placements, run_check=False, shape=p.shape, stride=p.stride())
+
+        def per_group(fill):
+            local = torch.full((groups,), fill, **vec)
+            if layout is None:
+                return local
+            shape, pls = layout
+            local = local.view((-1,) + tuple(shape[1:]))
+            stride = tuple(torch.empty(shape, device="meta").stride())
+            return DTensor.from_local(local, mesh, pls, run_check=False, shape=torch.Size(shape), stride=stride)
+
+        state["exp_avg"] = like_param(convert_str_to_fp8[q.first_order_bit])
+        state["scale_exp_avg"] = per_group(0.0)
+        if use_expansion:
+            state["expand_exp_avg"] = per_group(1.0)
+            state["sqrt_minmax_exp_avg"] = per_group(1.0)
+        state["exp_avg_sq"] = like_param(convert_str_to_fp8[q.second_order_bit])
+        state["scale_exp_avg_sq"] = per_group(0.0)
+        if use_expansion:
+            state["expand_exp_avg_sq"] = per_group(1.0)
+            state["sqrt_minmax_exp_avg_sq"] = per_group(1.0)
         return state
 
     # ---- step ------------------------------------------------------------------------------
@@ -208,7 +296,8 @@ class CoatAdamW(Optimizer):
 
         use_expansion = self._use_expansion()
         for gi, group in enumerate(self.param_groups):
-            params = [p for p in group["params"] if p.grad is not None]
+            # (a rank whose shard of an unevenly divided parameter is empty has nothing to step)
+            params = [p for p in group["params"] if p.grad is not None and local_tensor(p).numel() > 0]
             if not params:
                 continue
             for p in params:
@@ -221,10 +310,10 @@ class CoatAdamW(Optimizer):
             if (self.multi_tensor and len(params) > 1) or self.kernel_flags:
                 self._multi_tensor_step(gi, params, states, use_expansion, **hyper)
             else:
-                key = (lambda s, k: [st[k] for st in s])
+                key = (lambda s, k: [local_tensor(st[k]) for st in s])
                 exp = use_expansion
                 Coatadamw(
-                    self.qargs, params, [p.grad for p in params],
+                    self.qargs, [local_tensor(p) for p in params], [local_tensor(p.grad) for p in params],
                     key(states, "exp_avg"), key(states, "scale_exp_avg"),
                     key(states, "expand_exp_avg") if exp else [], key(states, "sqrt_minmax_exp_avg") if exp else [],
                     key(states, "exp_avg_sq"), key(states, "scale_exp_avg_sq"),
@@ -233,9 +322,9 @@ class CoatAdamW(Optimizer):
                     fused=group["fused"], grad_scale=getattr(self, "grad_scale", None),
                     found_inf=getattr(self, "found_inf", None))
                 for p in params:   # the per-tensor entry points keep the reference's signature: cast afterwards
-                    copy = self._bf16_copies.get(id(p))
+                    copy = self._bf16_copies.get(id(local_tensor(p)))
                     if copy is not None:
-                        copy.view(-1).copy_(p.detach().view(-1))
+                        copy.view(-1).copy_(local_tensor(p).detach().view(-1))
         return loss
 
     def _multi_tensor_step(self, gi, params, states, use_expansion, *, beta1, beta2, lr, weight_decay, eps,
@@ -244,6 +333,9 @@ class CoatAdamW(Optimizer):
         if qgroup_size != 128:
             raise RuntimeError("Only Support 128 per-group quantization currently")
         buckets = defaultdict(list)
+        grads = [local_tensor(p.grad) for p in params]
+        params = [local_tensor(p) for p in params]   # DTensor parameters: the kernels step the local shards
+        states = [{k: local_tensor(v) for k, v in st.items()} for st in states]
         for i, (p, st) in enumerate(zip(params, states)):
             st["step"] += 1
             buckets[(p.device, int(st["step"].item()))].append(i)
@@ -282,7 +374,7 @@ class CoatAdamW(Optimizer):
             rows = entry["rows"]
             changed = []
             for row, i in enumerate(idxs):
-                g = params[i].grad
+                g = grads[i]
                 if g.dtype != params[i].dtype or not g.is_contiguous():
                     raise RuntimeError("gradients must be contiguous and match the parameter dtype")
                 gp, pp = g.data_ptr(), params[i].data_ptr()
