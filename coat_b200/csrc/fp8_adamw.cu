@@ -515,10 +515,6 @@ constexpr int kCandPerGroup = 16;
 #define COAT_ADAMW_PEND_CAP 32
 #endif
 constexpr int kPendCap = COAT_ADAMW_PEND_CAP;
-#ifndef COAT_ADAMW_FLUSH_AT
-#define COAT_ADAMW_FLUSH_AT (COAT_ADAMW_PEND_CAP < 32 ? COAT_ADAMW_PEND_CAP : 24)
-#endif
-constexpr int kFlushAt = COAT_ADAMW_FLUSH_AT;   // checked once per tile: a tile adds a few entries
 constexpr float kTiny = 7.8886091e-31f;   // 2^-100: below this the flush-to-zero MUFU forms lose accuracy
 
 struct __align__(16) WarpTile {
@@ -607,9 +603,6 @@ __device__ __forceinline__ float ex2_ftz(float x) { float r; asm("ex2.approx.ftz
 __device__ __forceinline__ float rcp_ftz(float x) { float r; asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ float sqrt_ftz(float x) { float r; asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x)); return r; }
 __device__ __forceinline__ float max_nan(float a, float b) { float r; asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b)); return r; }
-// three-input forms (sm_100): one instruction for two comparisons
-__device__ __forceinline__ float max3_nan(float a, float b, float c) { float r; asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c)); return r; }
-__device__ __forceinline__ float min3(float a, float b, float c) { float r; asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c)); return r; }
 
 // Two-wide fp32 arithmetic (one instruction for two lanes of a 64-bit register pair on sm_100; each half is
 // rounded to nearest like the scalar instruction, so results are bit-identical to the scalar form)
@@ -879,7 +872,7 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 // a negative second-moment code sends the group to the exact path (via the NaN that max_nan carries
                 // into the group maximum); a NaN code arrives as a NaN moment through the table
                 float mx_a = (vw & 0x80808080u) ? __int_as_float(0x7fffffff) : 0.f;
-                float mn_a, mx_v, mn_v;
+                float mn_a = kInf, mx_v = 0.f, mn_v = kInf;
 #pragma unroll
                 for (int jj = 0; jj < 4; jj += 2) {
                     // |m| = (c s)^(1/k) r = ex2(lg2(c) / k + lg2(s) / k) r; the sign of the code is put back on
@@ -895,12 +888,13 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                     const float2 v2 = __ffma2_rn(f2(h.beta2), vt, __fmul2_rn(__fmul2_rn(f2(c.om_beta2), gg), gg));
                     m1[jj] = m2.x; m1[jj + 1] = m2.y; v1[jj] = v2.x; v1[jj + 1] = v2.y;
                 }
-                {   // a NaN anywhere must surface in the maxima; the minima ignore it
-                    const float a0 = fabsf(m1[0]), a1 = fabsf(m1[1]), a2 = fabsf(m1[2]), a3 = fabsf(m1[3]);
-                    mx_a = max3_nan(max3_nan(mx_a, a0, a1), a2, a3);
-                    mn_a = fminf(min3(a0, a1, a2), a3);
-                    mx_v = max_nan(max3_nan(v1[0], v1[1], v1[2]), v1[3]);
-                    mn_v = fminf(min3(v1[0], v1[1], v1[2]), v1[3]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a1 = fabsf(m1[j]);
+                    mx_a = max_nan(mx_a, a1);   // a NaN anywhere must surface in the maxima
+                    mn_a = fminf(mn_a, a1);
+                    mx_v = max_nan(mx_v, v1[j]);
+                    mn_v = fminf(mn_v, v1[j]);
                 }
                 // all four are non-negative (or NaN, which orders above everything): unsigned order == float order
                 const float MA = __uint_as_float(redux_max_f(mx_a)), mA = __uint_as_float(redux_min_f(mn_a));
@@ -1133,12 +1127,10 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
             if (dm | dv) queue_exact<scalar_t>(w, slot, lane, dm, dv, cm, cv, h, c, n_pend_total);
             reinterpret_cast<uint32_t*>(code_m)[lane] = cm;
             reinterpret_cast<uint32_t*>(code_v)[lane] = cv;
+            __syncwarp();
+            if (w.n_pend >= (uint32_t)(kPendCap < 32 ? kPendCap : 32)) { PHASE_CLOCK(4); flush_pending<scalar_t>(w, lane, h, c); PHASE_CLOCK(5); }
         }
         PHASE_CLOCK(4);
-        // exact recomputations wait until a full warp's worth has gathered (an entry that finds the list full is
-        // recomputed on the spot by queue_exact)
-        __syncwarp();
-        if (w.n_pend >= (uint32_t)kFlushAt) { flush_pending<scalar_t>(w, lane, h, c); PHASE_CLOCK(5); }
     }
     flush_pending<scalar_t>(w, lane, h, c);
 #ifdef COAT_ADAMW_PROFILE
