@@ -816,8 +816,10 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
         if (lane < n_slots) {
             const TensorDesc& t = MULTI ? table[w.ti[lane]] : single;
             const int64_t group = w.local[lane];
-            const float s_m = t.s_m[group], r_m = t.r_m[group], s_v = t.s_v[group], r_v = t.r_v[group];
-            const float ik_m = __fdiv_rn(1.0f, t.k_m[group]), ik_v = __fdiv_rn(1.0f, t.k_v[group]);
+            // all six loads leave before the first of them is used (each is a round trip to memory)
+            const float s_m = t.s_m[group], k_m = t.k_m[group], r_m = t.r_m[group];
+            const float s_v = t.s_v[group], k_v = t.k_v[group], r_v = t.r_v[group];
+            const float ik_m = __fdiv_rn(1.0f, k_m), ik_v = __fdiv_rn(1.0f, k_v);
             float tb_m, tb_v;
             const float lgs_m = fast_lg2(s_m), lgs_v = fast_lg2(s_v);
             const float eps_dm = fast_dequant_eps(ik_m, lgs_m, tb_m);
