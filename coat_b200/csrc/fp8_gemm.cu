@@ -148,18 +148,42 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
 // slower).  BM = 128: a tile is one unit.  BM = 256: a tile is two vertically adjacent units (one at an odd
 // matrix edge); when the last, partial round has at most gridDim / 2 tiles, they are split into their units
 // so that the round costs half a tile.
+// When the operands do not fit L2 together, tiles are numbered in bands of kGroupM tile rows: down the rows of a band
+// first, then along its columns, band after band.  The tiles in flight (one per SM) then cover a few tile rows of A
+// and most tile columns of B: B stays in L2 from band to band and A crosses DRAM once, where numbering down whole
+// columns makes every round of tiles pull all of A again (the reference's kernel walks its tiles in GROUP_M = 8
+// order for the same reason, coat/activation/real_quantization/linear.py:94-102).  Measured on the Llama-2-7B MLP
+// shapes (burst TFLOP/s): dgrad 2655 -> 2777, wgrad 2589 -> 2751 with bands of 8 (4 and 16 within 1 %); the forward
+// GEMM, whose operands (78 MB) stay in L2 anyway, lost 3 % with bands and keeps the column order.
+#ifndef COAT_GEMM_GROUP_M
+#define COAT_GEMM_GROUP_M 8
+#endif
+constexpr int kGroupM = COAT_GEMM_GROUP_M;
+// tile number -> (tile row, tile column) in that order; band_rows = 0: down whole columns
+__device__ __forceinline__ void banded_tile(int t, int tiles_m, int tiles_n, int band_rows, int& tile_m, int& tile_n) {
+    if (band_rows > 0) {
+        const int per_band = band_rows * tiles_n;
+        const int band = t / per_band, r = t - band * per_band;
+        const int rows = tiles_m - band * band_rows < band_rows ? tiles_m - band * band_rows : band_rows;
+        tile_n = r / rows;
+        tile_m = band * band_rows + (r - tile_n * rows);
+    } else {
+        tile_m = t % tiles_m;
+        tile_n = t / tiles_m;
+    }
+}
 template <int BM>
 struct TileWalk {
-    int k, rounds, rest, units_m, tiles_m;
-    __device__ TileWalk(int units_m_, int units_n) : k(0), units_m(units_m_) {
+    int k, rounds, rest, units_m, tiles_m, units_n, band_rows;
+    __device__ TileWalk(int units_m_, int units_n_, int band_rows_) : k(0), units_m(units_m_), units_n(units_n_), band_rows(band_rows_) {
         tiles_m = BM == 128 ? units_m_ : (units_m_ + 1) / 2;
         const int total = tiles_m * units_n;
         rounds = total / (int)gridDim.x;
         rest = total - rounds * (int)gridDim.x;
     }
     __device__ void decode(int t, int& unit_m, int& unit_n, int& halves) const {
-        const int tm = t % tiles_m;
-        unit_n = t / tiles_m;
+        int tm;
+        banded_tile(t, tiles_m, units_n, band_rows, tm, unit_n);
         unit_m = BM == 128 ? tm : 2 * tm;
         halves = BM == 128 ? 1 : (units_m - unit_m >= 2 ? 2 : 1);
     }
@@ -200,6 +224,7 @@ struct GemmEpilogue {
     int fmt_c;
     int ieee_div;
     int M, N, K;
+    int band_rows;           // tile order: 0 = down whole columns, else bands of this many tile rows (banded_tile)
 };
 
 __device__ __forceinline__ float ld_scalar(const void* p, int dtype, int64_t i = 0) {
@@ -405,7 +430,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             int it = 0;
-            TileWalk<BM> walk(tiles_m, tiles_n);
+            TileWalk<BM> walk(tiles_m, tiles_n, e.band_rows);
             int unit_m, unit_n, halves;
             while (ok && walk.next(unit_m, unit_n, halves)) {
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
@@ -424,7 +449,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             int it = 0, local = 0;
-            TileWalk<BM> walk(tiles_m, tiles_n);
+            TileWalk<BM> walk(tiles_m, tiles_n, e.band_rows);
             int unit_m, unit_n, halves;
             for (; ok && walk.next(unit_m, unit_n, halves); ++local) {
                 const int buf = local % kBufs, use = local / kBufs;
@@ -460,7 +485,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         const int half = (warp - 2) >> 2;                     // which M=128 accumulator of the tile
         const float sab = ld_scalar(e.scale_a, e.scale_dtype) * ld_scalar(e.scale_b, e.scale_dtype);
         int local = 0;
-        TileWalk<BM> walk(tiles_m, tiles_n);
+        TileWalk<BM> walk(tiles_m, tiles_n, e.band_rows);
         int unit_m, tile_n, halves;
         for (; ok && walk.next(unit_m, tile_n, halves); ++local) {
             const int buf = local % kBufs, use = local / kBufs;
@@ -582,7 +607,8 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
             // ---------------- TMA producer (both CTAs) ----------------
             int it = 0;
             for (int t = pair; t < n_tiles && ok; t += n_pairs) {
-                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+                int tile_m, tile_n;
+                banded_tile(t, tiles_m, tiles_n, e.band_rows, tile_m, tile_n);
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % kPairStages;
                     if (it >= kPairStages) ok = mbar_wait(&empty_bar[s], ((it / kPairStages) - 1) & 1, abort_flag);
@@ -627,7 +653,8 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
         uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
         int local = 0;
         for (int t = pair; t < n_tiles && ok; t += n_pairs, ++local) {
-            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            int tile_m, tile_n;
+                banded_tile(t, tiles_m, tiles_n, e.band_rows, tile_m, tile_n);
             const int buf = local & 1, use = local >> 1;
             ok = __all_sync(COAT_FULL_MASK, mbar_wait(&acc_full[buf], use & 1, abort_flag));
             if (!ok) break;
@@ -724,7 +751,8 @@ fp8_gemm_blockscaled_kernel(const __grid_constant__ CUtensorMap map_a, const __g
         if (lane == 0) {
             int it = 0;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+                int tile_m, tile_n;
+                banded_tile(t, tiles_m, tiles_n, kGroupM, tile_m, tile_n);
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % kBsStages;
                     if (it >= kBsStages) ok = mbar_wait(&empty_bar[s], ((it / kBsStages) - 1) & 1, abort_flag);
@@ -763,7 +791,8 @@ fp8_gemm_blockscaled_kernel(const __grid_constant__ CUtensorMap map_a, const __g
         uint8_t* stg = staging + (size_t)(warp - 2) * 4096;
         int it = 0;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-            const int tile_m = t % tiles_m, tile_n = t / tiles_m;
+            int tile_m, tile_n;
+                banded_tile(t, tiles_m, tiles_n, kGroupM, tile_m, tile_n);
             const int row0 = tile_m * 128 + quarter * 32, row = row0 + lane;
             float acc[64];
 #pragma unroll
@@ -964,6 +993,8 @@ extern "C" int coat_fp8_gemm(const uint8_t* a, const uint8_t* b, void* c, void* 
     e.scale_dtype = scale_dtype; e.bias_dtype = bias_dtype; e.quantize = output_quantize; e.QB = QB;
     e.fmt_c = fmt_a; e.ieee_div = (flags & COAT_QUANT_IEEE_DIV) ? 1 : 0;
     e.M = (int)M; e.N = (int)N; e.K = (int)K;
+    // operands that stay in L2 together (126 MB, of which the output stream takes its share) need no bands
+    e.band_rows = (M + N) * K > (int64_t)96 * 1024 * 1024 ? kGroupM : 0;
     const uint32_t idesc = make_idesc(fmt_a, fmt_b, 128, kBN);
     // work is counted in units of 128 rows x 256 columns for both tile heights
     const int tiles_m = (int)((M + 127) / 128), tiles_n = (int)((N + kBN - 1) / kBN);
