@@ -633,6 +633,103 @@ def layer_extras(torch, device, iters=5, with_reference_operators=False):
     return out
 
 
+def olmo_block_extras(torch, device, iters=5, with_reference_operators=False):
+    """Forward + backward of ONE OLMo-7B block (d_model 4096, 32 heads, ff_proj 22016, LayerNorm without parameters,
+    SwiGLU) on 8 x 2048 tokens, the shape of the reference's per-layer benchmark (benchmark/benchmark_olmolayer.py):
+    the FP8 block of this package, the same block in plain bf16 torch (cuBLAS GEMMs, SDPA, eager elementwise ops) and,
+    on request, the same composition on the reference's own operators.  Weights by the block's own initialisation,
+    input uniform in [0, 1) and upstream gradient uniform in [0, 1) as in that benchmark; memory-efficient weight mode,
+    first micro-batch; gradients reset to None before every step in every leg."""
+    import torch.nn.functional as F
+    from coat_b200.activation.real_quantization.func_quantize import Coat_quantize_bgn, Coat_quantize_end
+    from coat_b200.models.coat_olmo import CoatOLMoConfig, CoatOLMoSequentialBlock, olmo_rotary_tables
+    from coat_b200.utils._fp8_quantization_config import QuantizationConfig
+    from coat_b200.utils._fp8manager import FP8Manager
+    D, HID, heads, B, T = 4096, 22016, 32, 8, 2048
+    qargs = QuantizationConfig(group_size=16, weight_memory_efficient=True)
+    cfg = CoatOLMoConfig(d_model=D, n_heads=heads, mlp_hidden_size=HID, max_sequence_length=T)
+    torch.manual_seed(4)
+    block = CoatOLMoSequentialBlock(0, cfg, qargs)
+    block.reset_parameters()
+    block = block.to(device, torch.bfloat16).train()
+    bgn, end = Coat_quantize_bgn(qargs).train(), Coat_quantize_end(qargs).train()
+    x = torch.rand(B, T, D, device=device).to(torch.bfloat16).requires_grad_(True)
+    up = torch.rand(B, T, D, device=device).to(torch.bfloat16)
+    FP8Manager.is_first_microbatch = True
+
+    def fp8_step():
+        for p in block.parameters():
+            p.grad = None
+        x.grad = None
+        h, qh, sh, _ = block(*bgn(x))
+        end(h, qh, sh).backward(up)
+
+    w = {n: p.detach().clone().requires_grad_(True) for n, p in block.named_parameters()}
+    sin, cos = (t.to(torch.bfloat16).unsqueeze(1) for t in olmo_rotary_tables(T, D // heads, 10000.0, device))
+
+    def bf16_step():
+        ln = lambda t: F.layer_norm(t, (D,), None, None, 1e-5)
+        q, k, v = (t.view(B, T, heads, D // heads).transpose(1, 2)
+                   for t in F.linear(ln(x), w["BeforeAttention.att_proj.weight"]).split((D, D, D), dim=-1))
+        rot = lambda t: torch.cat((-t[..., t.shape[-1] // 2:], t[..., :t.shape[-1] // 2]), dim=-1)
+        q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B, T, D)
+        y = x + F.linear(a, w["AfterAttention.attn_out.weight"])
+        u, g = F.linear(ln(y), w["MLPResidual.ff_proj.weight"]).chunk(2, dim=-1)
+        y = y + F.linear(F.silu(g) * u, w["MLPResidual.ff_out.weight"])
+        for t in w.values():
+            t.grad = None
+        x.grad = None
+        y.backward(up)
+
+    def time_leg(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / iters
+        return {"fwd_bwd_ms": ms, "tokens_per_s": B * T / (ms / 1e3)}
+
+    out = {"tokens": B * T}
+    if with_reference_operators:
+        from oracle import ref_loader
+        ref = ref_loader.load_ref_triton(one_config=False)
+        if ref is None:
+            out["fp8_block_on_reference_operators"] = {"reference": "oracle/_ref/coat_ref not staged"}
+        else:
+            import coat_b200.activation.real_quantization as mine
+            import coat_b200.activation.real_quantization.func_quantize as fq
+            import coat_b200.models.coat_llama as llama_mod
+            import coat_b200.models.coat_olmo as olmo_mod
+            import coat_b200.utils._fp8_weightcache as cache_mod
+            ops = ref_loader.reference_layer_operators(ref, mine)
+            saved = []
+            for mod in (olmo_mod, llama_mod, cache_mod, fq):
+                for name, fn in ops.items():
+                    if hasattr(mod, name):
+                        saved.append((mod, name, getattr(mod, name)))
+                        setattr(mod, name, fn)
+            try:
+                out["fp8_block_on_reference_operators"] = time_leg(fp8_step)
+            except Exception as exc:
+                out["fp8_block_on_reference_operators"] = {"reference": f"did not run: {str(exc)[:160]}"}
+            finally:
+                for mod, name, fn in saved:
+                    setattr(mod, name, fn)
+    out["fp8_block"] = time_leg(fp8_step)
+    out["bf16_torch_block"] = time_leg(bf16_step)
+    out["fp8_over_bf16"] = out["bf16_torch_block"]["fwd_bwd_ms"] / out["fp8_block"]["fwd_bwd_ms"]
+    ref_leg = out.get("fp8_block_on_reference_operators", {})
+    if "fwd_bwd_ms" in ref_leg:
+        out["ours_over_reference_operators"] = ref_leg["fwd_bwd_ms"] / out["fp8_block"]["fwd_bwd_ms"]
+    return out
+
+
 def fused_extras(torch, device, peak):
     """GB/s of the fused quantize-on-save operators, the norms and the optimizer step without expansion, through the
     python operator API (the calls the decoder layer makes, with its arguments), on the benchmark shapes:
@@ -871,10 +968,12 @@ def run_kernel_workload(args):
     elif args.workload == "blockscaled":
         extras = {"deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak)}
     elif args.workload == "layer":
-        extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10)))}
+        extras = {"decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, iters=max(1, min(args.steps, 10))),
+                  "olmo_7b_block_8x2048": olmo_block_extras(torch, device, iters=max(1, min(args.steps, 10)))}
     elif args.workload == "reference-gpu":
         extras = {"reference_on_this_gpu": reference_on_this_gpu(torch, device, peak),
                   "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, with_reference_operators=True),
+                  "olmo_7b_block_8x2048": olmo_block_extras(torch, device, with_reference_operators=True),
                   "fp8_peak_yardstick": fp8_peak_yardstick(torch, device)}
     else:
         extras = {"fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device, iters=max(1, args.steps))}
@@ -1046,6 +1145,7 @@ def run_gpu_arm(args):
                               "fused_operators_8192_tokens": fused_extras(torch, device, peak),
                               "fp8_gemm_llama2_7b_mlp": gemm_extras(torch, device),
                               "decoder_layer_llama2_7b_4x2048": layer_extras(torch, device, with_reference_operators=True),
+                              "olmo_7b_block_8x2048": olmo_block_extras(torch, device, with_reference_operators=True),
                               "deepseek_blockscaled_llama2_7b_mlp": blockscaled_extras(torch, device, peak),
                               "reference_on_this_gpu": reference_on_this_gpu(torch, device, peak)}
         if cpu_v is not None:
