@@ -220,7 +220,12 @@ def run_reference_arm(args):
 # GPU arm
 # ------------------------------------------------------------------------------------------------
 
-NCU_DRAM_BYTES_PER_PARAM = 264.47e6 / (4096 * 4096)
+# DRAM bytes per parameter of the optimizer kernel, from ncu (dram__bytes_read.sum + dram__bytes_write.sum, one launch):
+# at the benchmark's own size, 72.056 GB read + 56.447 GB written for the 6 738 415 616 parameters of one full launch
+# (the two counters take a single pass, so the capture holds nothing back and restores nothing); on the 4096x4096
+# profiling case, whose 308 MB the 126 MB L2 absorbs in part, 171.2 + 94.1 MB for 16 777 216 parameters
+NCU_DRAM_BYTES_PER_PARAM_FULL = (72.055545088e9 + 56.447258112e9) / 6738415616
+NCU_DRAM_BYTES_PER_PARAM_C1 = (171.213824e6 + 94.058240e6) / (4096 * 4096)
 
 
 def fill_synthetic(opt, shapes, torch):
@@ -1107,10 +1112,10 @@ def run_gpu_arm(args):
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = my_params * BYTES_PER_PARAM_BF16 / (kernel_ms / 1e3) / 1e9
-        # DRAM bytes per parameter of this kernel as ncu measured them on the 4096x4096 case
-        # (dram__bytes_read.sum + dram__bytes_write.sum = 264.5 MB for 16 777 216 parameters,
-        # profiles/fp8_adamw_expand_tiled_c1.md), scaled to this launch by its parameter count
-        traffic = NCU_DRAM_BYTES_PER_PARAM * my_params
+        # measured DRAM bytes per parameter (see the constants above) times this launch's parameter count: the
+        # full-size figure for launches that stream far more than L2 holds, the small case's for the small case
+        per_param = NCU_DRAM_BYTES_PER_PARAM_FULL if my_params * BYTES_PER_PARAM_BF16 > 4e9 else NCU_DRAM_BYTES_PER_PARAM_C1
+        traffic = per_param * my_params
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": traffic, "peak_kind": f"of {peak_kind}", "kernel": "fp8_adamw_expand_tiled_kernel<float,table>",
                     "kernel_ms": kernel_ms, "algorithmic_bytes_per_param": BYTES_PER_PARAM_BF16}
