@@ -957,6 +957,23 @@ def reference_on_this_gpu(torch, device, peak):
     pair("fp8_linear_backward_dgrad_and_wgrad",
          lambda: ref.fp8_linear_backward(qx_t, sx, qg, sg, qg_t, qw_t, sw, 16),
          lambda: mine.fp8_linear_backward(qx_t, sx, qg, sg, qg_t, qw_t, sw, 16), 2 * tflop, "TFLOPs")
+    # the loss head: 4096 rows of fp32 logits over a 32000-entry vocabulary, loss and in-place gradient (the logits
+    # are read once and overwritten once: 8 bytes per logit; what a call overwrites is the next call's input, softmax
+    # gradients are as good a set of logits as any)
+    liger = ref_loader.load_ref_liger()
+    if liger is None:
+        out["cross_entropy_4096x32000"] = {"reference": "oracle/_ref/coat_ref/activation/liger not staged"}
+    else:
+        from coat_b200.activation.liger import cross_entropy as my_ce
+        rows, V = 4096, 32000
+        gen = torch.Generator(device=device).manual_seed(3)
+        la = torch.randn(rows, V, generator=gen, device=device) * 3
+        lb = la.clone()
+        tgt = torch.randint(0, V, (rows,), generator=gen, device=device)
+        pair("cross_entropy_4096x32000",
+             lambda: liger.cross_entropy_forward(la, tgt, -100, 0.0, 0.0, "mean", None, False),
+             lambda: my_ce.cross_entropy_forward(lb, tgt, -100, 0.0, 0.0, "mean", None, False),
+             rows * V * 8 / 1e3, "GBps")
     return out
 
 
