@@ -179,7 +179,9 @@ def workload_config(world, exchange, workload="llama2-7b", note=""):
             if workload == "llama2-7b" else "FP8AdamW-expand step over one 4096x4096 tensor (profiling case)")
     how = {"p2p": " stored by the same kernel into every peer's buffer over NVLink (fused step + all-gather), "
                   "one-element all-reduce as the closing barrier",
-           "nccl": " + bucketed NCCL all-gather on a side stream", None: ""}[exchange if world > 1 else None]
+           "nccl": " + bucketed NCCL all-gather on a side stream",
+           "copy": " + bucketed peer copies (DMA engines) of the bf16 weights on side streams",
+           None: ""}[exchange if world > 1 else None]
     return {"workload": what + ", fp32 master weights, E4M3 moments group 128, bf16 weight copy" + how + note,
             "parallelism": f"zero-shard x{world} on 128-element group boundaries",
             "l2": "inputs larger than L2 (>= 10 GB per GPU per step)" if workload == "llama2-7b" else
@@ -1055,9 +1057,9 @@ def run_gpu_arm(args):
     try:
         opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange, **HYPER)
     except RuntimeError as e:   # raised on every rank alike when the peer mapping is not available
-        if exchange != "p2p":
+        if exchange not in ("p2p", "copy"):
             raise
-        exchange, exchange_note = "nccl", f" (p2p set-up failed: {str(e)[:200]})"
+        exchange, exchange_note = "nccl", f" ({exchange} set-up failed: {str(e)[:200]})"
         opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange="nccl", **HYPER)
     fill_synthetic(opt, shapes, torch)
     my_params = sum(pc.numel for pc in opt.my_pieces)
@@ -1189,7 +1191,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled", "reference-gpu"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl", "copy"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
                          "the step kernel itself, or bucketed NCCL all-gathers overlapped with the step")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")

@@ -40,6 +40,7 @@ SIGNATURES = {
     "coat_peer_buffer_open": [_vp, _vp],
     "coat_peer_buffer_close": [_vp],
     "coat_peer_buffer_free": [_vp],
+    "coat_peer_copy_async": [_vp, _vp, _i64, _vp],
     "coat_fp8_quantize": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_group_scales_amax": [_vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _i, _vp],
     "coat_fp8_division": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _i, _vp],

@@ -84,3 +84,16 @@ extern "C" int coat_peer_buffer_free(void* ptr) {
     if (cudaFree(ptr) != cudaSuccess) { cudaGetLastError(); return COAT_E_PEER; }
     return COAT_OK;
 }
+
+// Asynchronous device-to-device copy by raw pointers on `stream`: the source in this GPU's memory, the destination a
+// mapped peer buffer (coat_peer_buffer_open) or local memory.  The DMA engines move the bytes; no SM is involved.
+extern "C" int coat_peer_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return COAT_E_BADARG;
+    if (bytes == 0) return COAT_OK;
+    if (cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream) != cudaSuccess) {
+        cudaGetLastError();
+        return COAT_E_PEER;
+    }
+    return COAT_OK;
+}
+

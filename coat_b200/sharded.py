@@ -192,6 +192,10 @@ class ShardedCoatAdamW:
     barrier that tells every rank that all slices have landed.
     exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
     that the gather of bucket b runs under the step of bucket b+1.
+    exchange="copy": one launch per bucket of the plain step kernel (full occupancy, no staging of the bf16 weights in
+    shared memory); behind an event after bucket b's kernel, side streams (one per peer) push the bucket's bf16 slice
+    into every peer's copy of `self.gathered` with asynchronous peer copies (DMA engines, no SMs) while bucket b+1 is
+    stepped; the same one-element all-reduce closes the step.
 
     With world_size 1 there is one bucket and no exchange.  Gradients are written by the caller
     into `self.grad` (already reduce-scattered, as under ZeRO); the updated bf16 weights of ALL ranks
@@ -214,13 +218,13 @@ class ShardedCoatAdamW:
         self.step_count = 0
         if exchange is None:
             exchange = "p2p" if world_size > 1 else "none"
-        if exchange not in ("none", "p2p", "nccl") or (exchange == "none") != (world_size == 1):
+        if exchange not in ("none", "p2p", "nccl", "copy") or (exchange == "none") != (world_size == 1):
             raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
         if exchange == "p2p" and world_size - 1 > _lib.MAX_PEERS:
             raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
         self.exchange = exchange
         if n_buckets is None:
-            n_buckets = 8 if exchange == "nccl" else 1
+            n_buckets = 8 if exchange in ("nccl", "copy") else 1
         self.bounds = self.plan.bucket_bounds(n_buckets)
         self.n_buckets = len(self.bounds) - 1
         self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
@@ -240,7 +244,7 @@ class ShardedCoatAdamW:
         # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
         self._peer_buffer = None
         self._peer_deltas = None
-        if exchange == "p2p":
+        if exchange in ("p2p", "copy"):
             self._setup_peer_buffer(world_size * n * 2)
         else:
             self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
@@ -251,7 +255,9 @@ class ShardedCoatAdamW:
             self._bucket_all.append(whole)
             self._bucket_mine.append(whole[rank * (hi - lo):(rank + 1) * (hi - lo)])
         self._comm = torch.cuda.Stream(device=dev) if exchange == "nccl" else None
-        self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if self._comm else []
+        self._copy_streams = ([torch.cuda.Stream(device=dev) for _ in range(world_size - 1)]
+                              if exchange == "copy" else [])
+        self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if (self._comm or self._copy_streams) else []
         self._table_cache = {}
         self.set_grad_buffer(self.grad)
 
@@ -346,8 +352,8 @@ class ShardedCoatAdamW:
         if self.world_size == 1:
             return
         import torch.distributed as dist
-        if self.exchange == "p2p":
-            raise RuntimeError("exchange='p2p' has no separate gather: step() does both")
+        if self.exchange in ("p2p", "copy"):
+            raise RuntimeError(f"exchange='{self.exchange}' has no separate gather: step() does both")
         for b in range(self.n_buckets):
             dist.all_gather_into_tensor(self._bucket_all[b], self._bucket_mine[b], group=self.process_group)
 
@@ -361,6 +367,31 @@ class ShardedCoatAdamW:
                 self._launch_bucket(b, bcast=True)
             # stream-ordered barrier: it completes on a rank only after every rank's kernel has
             dist.all_reduce(self._flag, group=self.process_group)
+            return
+        if self.exchange == "copy":
+            compute = torch.cuda.current_stream(self.device)
+            for st in self._copy_streams:
+                st.wait_stream(compute)   # readers of the previous step's gathered weights are done
+            self.step_count += 1
+            peers = [r for r in range(self.world_size) if r != self.rank]
+            base = self._peer_buffer.ptr
+            for b in range(self.n_buckets):
+                self._launch_bucket(b)
+                self._events[b].record(compute)
+                mine = self._bucket_mine[b]
+                nbytes = mine.numel() * 2
+                if nbytes == 0:
+                    continue
+                offset = mine.data_ptr() - base
+                for i, st in enumerate(self._copy_streams):
+                    # rotate the destinations so that at any moment the ranks write to different peers
+                    peer = peers[(i + self.rank) % len(peers)]
+                    st.wait_event(self._events[b])
+                    self._lib.check(self._lib.lib().coat_peer_copy_async(
+                        self._peer_buffer.peers[peer] + offset, mine.data_ptr(), nbytes, st.cuda_stream), "peer_copy_async")
+            for st in self._copy_streams:
+                compute.wait_stream(st)
+            dist.all_reduce(self._flag, group=self.process_group)   # every rank's copies have landed everywhere
             return
         if self.world_size == 1 or self._comm is None:
             self.local_step()

@@ -150,6 +150,10 @@ int coat_peer_buffer_create(int64_t bytes, void** ptr_out, void* handle_out);
 int coat_peer_buffer_open(const void* handle, void** ptr_out);
 int coat_peer_buffer_close(void* ptr);
 int coat_peer_buffer_free(void* ptr);
+/* Asynchronous copy of `bytes` bytes from this GPU's memory to a mapped peer buffer (or local memory) on `stream`,
+ * by the DMA engines: the transport of the bucketed "copy" exchange of the sharded step (no reference counterpart:
+ * the reference leaves the weight all-gather to the host framework's FSDP). */
+int coat_peer_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 
 /* =========================== quantizers ====================================
  * x is an M x N row-major matrix of in_dtype (COAT_BF16 / COAT_F16 / COAT_F32) with row stride ldx
