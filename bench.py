@@ -181,6 +181,9 @@ def workload_config(world, exchange, workload="llama2-7b", note=""):
                   "one-element all-reduce as the closing barrier",
            "nccl": " + bucketed NCCL all-gather on a side stream",
            "copy": " + bucketed peer copies (DMA engines) of the bf16 weights on side streams",
+           "hybrid": " + bf16 weights to most peers by the step kernel's own bulk stores, to the rest by bucketed peer "
+                     "copies (DMA engines) on side streams",
+           "auto": " + exchange chosen by world size",
            None: ""}[exchange if world > 1 else None]
     return {"workload": what + ", fp32 master weights, E4M3 moments group 128, bf16 weight copy" + how + note,
             "parallelism": f"zero-shard x{world} on 128-element group boundaries",
@@ -1054,10 +1057,13 @@ def run_gpu_arm(args):
     numels = [numel(s) for s in shapes]
     total = sum(numels)
     exchange, exchange_note = (args.exchange if world > 1 else None), ""
+    if exchange == "auto":
+        exchange = "copy" if world == 2 else "hybrid"
     try:
-        opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange, **HYPER)
+        opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange,
+                               copy_peers=args.copy_peers, **HYPER)
     except RuntimeError as e:   # raised on every rank alike when the peer mapping is not available
-        if exchange not in ("p2p", "copy"):
+        if exchange not in ("p2p", "copy", "hybrid"):
             raise
         exchange, exchange_note = "nccl", f" ({exchange} set-up failed: {str(e)[:200]})"
         opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange="nccl", **HYPER)
@@ -1191,7 +1197,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled", "reference-gpu"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl", "copy"],
+    ap.add_argument("--copy-peers", type=int, default=None,
+                    help="hybrid exchange: how many peers the DMA engines serve (default: about a third)")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl", "copy", "hybrid"],
                     help="how the bf16 weights reach the other ranks at --gpus > 1: stored into the peers' buffers by "
                          "the step kernel itself, or bucketed NCCL all-gathers overlapped with the step")
     ap.add_argument("--kernel-only", action="store_true", help="skip the e2e and CPU legs (profiling runs)")

@@ -192,7 +192,10 @@ class ShardedCoatAdamW:
     barrier that tells every rank that all slices have landed.
     exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
     that the gather of bucket b runs under the step of bucket b+1.
-    exchange="copy": one launch per bucket of the plain step kernel (full occupancy, no staging of the bf16 weights in
+    exchange="hybrid" (the default with more than two ranks): buckets as in "copy", but only `copy_peers` of the peers
+    (about a third) are served by the DMA engines; the bucket's kernel is the fused one and stores to the others, so that
+    both transports fill the links together.
+    exchange="copy" (the default with two ranks): one launch per bucket of the plain step kernel (full occupancy, no staging of the bf16 weights in
     shared memory); behind an event after bucket b's kernel, side streams (one per peer) push the bucket's bf16 slice
     into every peer's copy of `self.gathered` with asynchronous peer copies (DMA engines, no SMs) while bucket b+1 is
     stepped; the same one-element all-reduce closes the step.
@@ -205,7 +208,7 @@ class ShardedCoatAdamW:
 
     def __init__(self, numels, rank=0, world_size=1, device="cuda", lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
                  weight_decay=1e-2, expand_min=16, use_expansion=True, process_group=None, flags=0,
-                 n_buckets=None, exchange=None):
+                 n_buckets=None, exchange=None, copy_peers=None):
         from . import _lib
         self._lib = _lib
         self.plan = ShardPlan(numels, world_size)
@@ -217,14 +220,16 @@ class ShardedCoatAdamW:
         self.flags = flags
         self.step_count = 0
         if exchange is None:
-            exchange = "p2p" if world_size > 1 else "none"
-        if exchange not in ("none", "p2p", "nccl", "copy") or (exchange == "none") != (world_size == 1):
+            # two ranks: the DMA engines hide the whole exchange under the plain kernel; more ranks: they carry only a
+            # part of what the links can, so the kernel's own stores take most destinations (see "hybrid")
+            exchange = "none" if world_size == 1 else ("copy" if world_size == 2 else "hybrid")
+        if exchange not in ("none", "p2p", "nccl", "copy", "hybrid") or (exchange == "none") != (world_size == 1):
             raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
-        if exchange == "p2p" and world_size - 1 > _lib.MAX_PEERS:
+        if exchange in ("p2p", "hybrid") and world_size - 1 > _lib.MAX_PEERS:
             raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
         self.exchange = exchange
         if n_buckets is None:
-            n_buckets = 8 if exchange in ("nccl", "copy") else 1
+            n_buckets = 8 if exchange in ("nccl", "copy", "hybrid") else 1
         self.bounds = self.plan.bucket_bounds(n_buckets)
         self.n_buckets = len(self.bounds) - 1
         self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
@@ -244,7 +249,19 @@ class ShardedCoatAdamW:
         # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
         self._peer_buffer = None
         self._peer_deltas = None
-        if exchange in ("p2p", "copy"):
+        # which peers receive this rank's slice from the DMA engines (the others from the kernel's stores): the next
+        # `copy_peers` ranks, so that every rank also RECEIVES from exactly that many engines
+        n_peers = world_size - 1
+        if exchange == "copy":
+            k = n_peers
+        elif exchange == "hybrid":
+            k = copy_peers if copy_peers is not None else max(1, round(0.35 * n_peers))
+            k = min(max(int(k), 0), n_peers)
+        else:
+            k = 0
+        self._copy_ranks = [(rank + 1 + i) % world_size for i in range(k)]
+        self._store_ranks = [r for r in range(world_size) if r != rank and r not in self._copy_ranks]
+        if exchange in ("p2p", "copy", "hybrid"):
             self._setup_peer_buffer(world_size * n * 2)
         else:
             self.gathered = torch.zeros(world_size * n, dtype=torch.bfloat16, device=dev)
@@ -255,8 +272,7 @@ class ShardedCoatAdamW:
             self._bucket_all.append(whole)
             self._bucket_mine.append(whole[rank * (hi - lo):(rank + 1) * (hi - lo)])
         self._comm = torch.cuda.Stream(device=dev) if exchange == "nccl" else None
-        self._copy_streams = ([torch.cuda.Stream(device=dev) for _ in range(world_size - 1)]
-                              if exchange == "copy" else [])
+        self._copy_streams = [torch.cuda.Stream(device=dev) for _ in self._copy_ranks]
         self._events = [torch.cuda.Event() for _ in range(self.n_buckets)] if (self._comm or self._copy_streams) else []
         self._table_cache = {}
         self.set_grad_buffer(self.grad)
@@ -269,8 +285,10 @@ class ShardedCoatAdamW:
                                     self.process_group)
         self._peer_buffer = buf
         self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
-        deltas = [buf.peers[r] - buf.ptr for r in range(self.world_size) if r != self.rank]
-        self._peer_deltas = (ctypes.c_int64 * len(deltas))(*deltas)
+        store_ranks = self._store_ranks if self.exchange != "p2p" else [r for r in range(self.world_size) if r != self.rank]
+        deltas = [buf.peers[r] - buf.ptr for r in store_ranks]
+        self._peer_deltas = (ctypes.c_int64 * max(1, len(deltas)))(*deltas)
+        self._n_store_peers = len(deltas)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
 
     def close(self):
@@ -333,7 +351,7 @@ class ShardedCoatAdamW:
                     table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
                     int(self.use_expansion), h["betas"][0], h["betas"][1], h["lr"], h["weight_decay"], h["eps"],
                     self.step_count, GROUP, h["expand_min"], L.F32, self.flags, self._peer_deltas,
-                    len(self._peer_deltas), L.stream_ptr(self.device))
+                    self._n_store_peers, L.stream_ptr(self.device))
             else:
                 rc = L.lib().coat_fp8_adamw_multi_step(
                     table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
@@ -352,7 +370,7 @@ class ShardedCoatAdamW:
         if self.world_size == 1:
             return
         import torch.distributed as dist
-        if self.exchange in ("p2p", "copy"):
+        if self.exchange in ("p2p", "copy", "hybrid"):
             raise RuntimeError(f"exchange='{self.exchange}' has no separate gather: step() does both")
         for b in range(self.n_buckets):
             dist.all_gather_into_tensor(self._bucket_all[b], self._bucket_mine[b], group=self.process_group)
@@ -368,30 +386,28 @@ class ShardedCoatAdamW:
             # stream-ordered barrier: it completes on a rank only after every rank's kernel has
             dist.all_reduce(self._flag, group=self.process_group)
             return
-        if self.exchange == "copy":
+        if self.exchange in ("copy", "hybrid"):
             compute = torch.cuda.current_stream(self.device)
             for st in self._copy_streams:
                 st.wait_stream(compute)   # readers of the previous step's gathered weights are done
             self.step_count += 1
-            peers = [r for r in range(self.world_size) if r != self.rank]
             base = self._peer_buffer.ptr
             for b in range(self.n_buckets):
-                self._launch_bucket(b)
+                # the kernel's own stores serve `_store_ranks` (none of them: the plain kernel at full occupancy)
+                self._launch_bucket(b, bcast=self._n_store_peers > 0)
                 self._events[b].record(compute)
                 mine = self._bucket_mine[b]
                 nbytes = mine.numel() * 2
                 if nbytes == 0:
                     continue
                 offset = mine.data_ptr() - base
-                for i, st in enumerate(self._copy_streams):
-                    # rotate the destinations so that at any moment the ranks write to different peers
-                    peer = peers[(i + self.rank) % len(peers)]
+                for peer, st in zip(self._copy_ranks, self._copy_streams):
                     st.wait_event(self._events[b])
                     self._lib.check(self._lib.lib().coat_peer_copy_async(
                         self._peer_buffer.peers[peer] + offset, mine.data_ptr(), nbytes, st.cuda_stream), "peer_copy_async")
             for st in self._copy_streams:
                 compute.wait_stream(st)
-            dist.all_reduce(self._flag, group=self.process_group)   # every rank's copies have landed everywhere
+            dist.all_reduce(self._flag, group=self.process_group)   # every rank's stores and copies have landed everywhere
             return
         if self.world_size == 1 or self._comm is None:
             self.local_step()
