@@ -1058,7 +1058,7 @@ def run_gpu_arm(args):
     total = sum(numels)
     exchange, exchange_note = (args.exchange if world > 1 else None), ""
     if exchange == "auto":
-        exchange = "copy" if world == 2 else "hybrid"
+        exchange = "copy" if world == 2 else "p2p"   # ShardedCoatAdamW's own default, spelled out for the record
     try:
         opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange,
                                copy_peers=args.copy_peers, **HYPER)

@@ -186,15 +186,15 @@ class ShardedCoatAdamW:
     """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
     weights everywhere.
 
-    exchange="p2p" (the default with more than one rank): ONE kernel per step does both the update and
+    exchange="p2p" (the default with more than two ranks): ONE kernel per step does both the update and
     the exchange; it stores its bf16 slice into every peer's copy of `self.gathered` over NVLink while
     it computes (coat_fp8_adamw_multi_step_bcast), and a one-element all-reduce after it is the
     barrier that tells every rank that all slices have landed.
     exchange="nccl": one launch per bucket and one NCCL all-gather per bucket on a side stream, so
     that the gather of bucket b runs under the step of bucket b+1.
-    exchange="hybrid" (the default with more than two ranks): buckets as in "copy", but only `copy_peers` of the peers
-    (about a third) are served by the DMA engines; the bucket's kernel is the fused one and stores to the others, so that
-    both transports fill the links together.
+    exchange="hybrid": buckets as in "copy", but only `copy_peers` of the peers (about a third) are served by the DMA
+    engines; the bucket's kernel is the fused one and stores to the others (measured equal to "p2p" at four ranks:
+    what bounds the exchange there is the rate at which a GPU takes in writes from all peers at once, not the sender).
     exchange="copy" (the default with two ranks): one launch per bucket of the plain step kernel (full occupancy, no staging of the bf16 weights in
     shared memory); behind an event after bucket b's kernel, side streams (one per peer) push the bucket's bf16 slice
     into every peer's copy of `self.gathered` with asynchronous peer copies (DMA engines, no SMs) while bucket b+1 is
@@ -220,9 +220,10 @@ class ShardedCoatAdamW:
         self.flags = flags
         self.step_count = 0
         if exchange is None:
-            # two ranks: the DMA engines hide the whole exchange under the plain kernel; more ranks: they carry only a
-            # part of what the links can, so the kernel's own stores take most destinations (see "hybrid")
-            exchange = "none" if world_size == 1 else ("copy" if world_size == 2 else "hybrid")
+            # two ranks: the DMA engines hide the whole exchange under the plain kernel (21.8 ms against 26.2 ms for the
+            # fused kernel on the Llama-2-7B set); more ranks: the engines sustain only 350-380 GB/s into several peers
+            # (28.7 ms against 17.6 ms at four ranks, 31.0 against 18.8 ms at eight), the fused kernel's stores 570-630
+            exchange = "none" if world_size == 1 else ("copy" if world_size == 2 else "p2p")
         if exchange not in ("none", "p2p", "nccl", "copy", "hybrid") or (exchange == "none") != (world_size == 1):
             raise ValueError(f"exchange={exchange!r} does not fit world_size={world_size}")
         if exchange in ("p2p", "hybrid") and world_size - 1 > _lib.MAX_PEERS:
