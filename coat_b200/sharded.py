@@ -250,6 +250,7 @@ class ShardedCoatAdamW:
         # all ranks' bf16 slices, bucket-major; this rank's kernel writes straight into its own slots
         self._peer_buffer = None
         self._peer_deltas = None
+        self._n_store_peers = None   # how many entries of _peer_deltas the kernel stores to (None: all of them)
         # which peers receive this rank's slice from the DMA engines (the others from the kernel's stores): the next
         # `copy_peers` ranks, so that every rank also RECEIVES from exactly that many engines
         n_peers = world_size - 1
@@ -352,7 +353,8 @@ class ShardedCoatAdamW:
                     table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
                     int(self.use_expansion), h["betas"][0], h["betas"][1], h["lr"], h["weight_decay"], h["eps"],
                     self.step_count, GROUP, h["expand_min"], L.F32, self.flags, self._peer_deltas,
-                    self._n_store_peers, L.stream_ptr(self.device))
+                    len(self._peer_deltas) if self._n_store_peers is None else self._n_store_peers,
+                    L.stream_ptr(self.device))
             else:
                 rc = L.lib().coat_fp8_adamw_multi_step(
                     table.data_ptr(), prefix.data_ptr(), n_pieces, n_groups,
@@ -395,7 +397,7 @@ class ShardedCoatAdamW:
             base = self._peer_buffer.ptr
             for b in range(self.n_buckets):
                 # the kernel's own stores serve `_store_ranks` (none of them: the plain kernel at full occupancy)
-                self._launch_bucket(b, bcast=self._n_store_peers > 0)
+                self._launch_bucket(b, bcast=bool(self._n_store_peers))
                 self._events[b].record(compute)
                 mine = self._bucket_mine[b]
                 nbytes = mine.numel() * 2
