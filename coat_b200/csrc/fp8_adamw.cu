@@ -812,30 +812,37 @@ fp8_adamw_expand_tiled_kernel(TensorDesc single, const TensorDesc* __restrict__ 
                 w.cw_v[sl][lane] = reinterpret_cast<const uint32_t*>(w.ptr_v[sl])[lane];
             }
         }
-        // 0b: the stored scalars of each group, 1/k, error bounds, range checks (overlaps the copies)
-        if (lane < n_slots) {
-            const TensorDesc& t = MULTI ? table[w.ti[lane]] : single;
-            const int64_t group = w.local[lane];
-            // all six loads leave before the first of them is used (each is a round trip to memory)
-            const float s_m = t.s_m[group], k_m = t.k_m[group], r_m = t.r_m[group];
-            const float s_v = t.s_v[group], k_v = t.k_v[group], r_v = t.r_v[group];
-            const float ik_m = __fdiv_rn(1.0f, k_m), ik_v = __fdiv_rn(1.0f, k_v);
-            float tb_m, tb_v;
-            const float lgs_m = fast_lg2(s_m), lgs_v = fast_lg2(s_v);
-            const float eps_dm = fast_dequant_eps(ik_m, lgs_m, tb_m);
-            const float eps_dv = fast_dequant_eps(ik_v, lgs_v, tb_v);
-            w.c0[lane][0] = __fmul_rn(lgs_m, ik_m);
-            w.c0[lane][1] = __fmul_rn(lgs_v, ik_v);
-            const bool ok = sane_pos(s_m) && sane_pos(r_m) && sane_pos(s_v) && sane_pos(r_v) && ik_m >= 0.015625f &&
-                            ik_m <= 64.0f && ik_v >= 0.015625f && ik_v <= 64.0f && tb_m <= 60.0f && tb_v <= 60.0f;
-            float* sc = w.old_sc[lane];
-            // largest |beta1 * m~| any code of the group can dequantise to (the code 448; the dequantisation is monotone
-            // in the code's magnitude, 2^-20 covers the approximation's own wobble), times the relative bound: the
-            // absolute error the first moment inherits from the dequantisation
-            const float mam = fabsf(h.beta1) * (ex2_ftz(__fmaf_rn(8.8073549f /* lg2 448 */, ik_m, w.c0[lane][0])) * r_m) *
-                              (1.0f + 9.5367432e-07f);
-            sc[0] = s_m; sc[1] = ik_m; sc[2] = r_m; sc[3] = eps_dm * mam; sc[4] = s_v; sc[5] = ik_v; sc[6] = r_v; sc[7] = eps_dv;
-            if (ok) w.flags[lane] |= 1u;
+        // 0b: the stored scalars of each group, 1/k, error bounds, range checks (overlaps the copies); one lane per
+        //     (group, moment), so that the two moments' chains of a group run side by side
+        {
+            const int slot = lane >> 1;
+            const bool second = lane & 1;
+            int ok = 1;
+            if (slot < n_slots) {
+                const TensorDesc& t = MULTI ? table[w.ti[slot]] : single;
+                const int64_t group = w.local[slot];
+                // the three loads leave before the first of them is used (each is a round trip to memory)
+                const float s = (second ? t.s_v : t.s_m)[group];
+                const float k = (second ? t.k_v : t.k_m)[group];
+                const float r = (second ? t.r_v : t.r_m)[group];
+                const float ik = __fdiv_rn(1.0f, k);
+                float tb;
+                const float lgs = fast_lg2(s);
+                const float eps_d = fast_dequant_eps(ik, lgs, tb);
+                const float c0 = __fmul_rn(lgs, ik);
+                w.c0[slot][second] = c0;
+                ok = sane_pos(s) && sane_pos(r) && ik >= 0.015625f && ik <= 64.0f && tb <= 60.0f;
+                float* sc = w.old_sc[slot] + (second ? 4 : 0);
+                // first moment: largest |beta1 * m~| any code of the group can dequantise to (the code 448; the
+                // dequantisation is monotone in the code's magnitude, 2^-20 covers the approximation's own wobble), times
+                // the relative bound: the absolute error the first moment inherits from the dequantisation
+                const float mam = fabsf(h.beta1) * (ex2_ftz(__fmaf_rn(8.8073549f /* lg2 448 */, ik, c0)) * r) *
+                                  (1.0f + 9.5367432e-07f);
+                sc[0] = s; sc[1] = ik; sc[2] = r; sc[3] = second ? eps_d : eps_d * mam;
+            }
+            // (every lane takes part in the shuffle: it must not sit behind a short-circuiting `&&`)
+            const int other = __shfl_xor_sync(COAT_FULL_MASK, ok, 1);
+            if (slot < n_slots && !second && ok && other) w.flags[slot] |= 1u;
         }
         __syncwarp();
         if (bulk) {
