@@ -370,6 +370,17 @@ def quantizer_extras(torch, device, peak):
         "pass2_division": (lambda x: division(x, False), 3.0, 1),
         "pass2_division_transpose": (lambda x: division(x, True), 4.0, 1),
     }
+    # yardstick at THIS size: a device-to-device copy that moves as many bytes as the 1x16 quantizer's algorithmic
+    # traffic (52 MB read + 52 MB written), in the same harness; the measured-peak denominator comes from a copy
+    # hundreds of times larger, which amortises launch and ramp-up
+    copy_src = [torch.empty(M * N * 25 // 16, dtype=torch.uint8, device=device) for _ in range(4)]
+    copy_dst = torch.empty_like(copy_src[0])
+    src_of = {x.data_ptr(): c for x, c in zip(xs, copy_src)}
+
+    def same_size_copy(x):
+        copy_dst.copy_(src_of[x.data_ptr()])
+        return 0
+    cases["copy_of_the_same_bytes_as_quantize_1x16"] = (same_size_copy, 3.125, 1)
     out = {}
     iters = 20
     for name, (fn, bytes_per_elem, launches) in cases.items():
