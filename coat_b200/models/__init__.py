@@ -13,6 +13,7 @@ from .coat_llama_model import (  # noqa: F401
     make_state_dict_compatible,
 )
 from .coat_olmo import (  # noqa: F401
+    CoatOLMo,
     CoatOLMoAfterAttentionResidual,
     CoatOLMoBeforeAttentionResidual,
     CoatOLMoBlock,

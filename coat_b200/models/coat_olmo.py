@@ -16,8 +16,10 @@ and whose backward passes run the mirrored chain on E5M2 gradients; in the MLP t
 the gate halves share ONE per-tensor scale (the reference concatenates them before it quantises, :603-611).
 What differs from the Llama layer: the norm (LayerNorm, no weight, no bias), the fused projections, and OLMo's
 rotary embedding computed in fp32.  `CoatOLMoConfig` is a plain attribute bag with the fields of the host
-trainer's ModelConfig that the block reads (any object with those attributes works); the trainer, its yaml
-configuration and the whole-model class stay with the host framework.
+trainer's ModelConfig that the block reads (any object with those attributes works).  `CoatOLMo` at the end of the
+file is the model around the blocks (embedding, the FP8 stream through the blocks, final norm, output projection) with
+the reference's module names; the trainer, its yaml configuration, checkpointing and FSDP wrapping policies stay with
+the host framework.
 
 Two things are done differently from the reference's composition without changing a bit of the result:
 the up and gate halves of `ff_proj` come from two GEMMs over the two halves of the weight codes (the halves
@@ -25,12 +27,13 @@ of one fused result would be strided views, which every following operator would
 the gated product and its backward run in one kernel each.
 """
 import math
-from typing import Optional
+from typing import NamedTuple, Optional
 
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..activation.real_quantization.func_quantize import Coat_quantize_bgn, Coat_quantize_end
 from ..activation.real_quantization import (
     fp8_add_Ifp_Ifp_Ofp_Og16,
     fp8_add_Ifp_Ifp_Ofp_Opt,
@@ -466,3 +469,107 @@ class CoatOLMoSequentialBlock(CoatOLMoBlock):
         x, qx, sx = self.AfterAttention(x, att)
         x, qx, sx = self.MLPResidual(x, qx, sx)
         return x, qx, sx, cache
+
+
+# =====================================================================================================
+# The model around the blocks
+# =====================================================================================================
+class OLMoOutput(NamedTuple):
+    logits: torch.Tensor
+    attn_key_values: Optional[list]
+    hidden_states: Optional[tuple]
+
+
+class _PlainLayerNorm(nn.Module):
+    """LayerNorm without parameters (the OLMo-7B configuration's `layer_norm_type: default`, no affine part)."""
+
+    def __init__(self, eps=1e-5):
+        super().__init__()
+        self.eps = eps
+
+    def forward(self, x):
+        return _plain_layernorm(x, self.eps)
+
+
+class CoatOLMo(nn.Module):
+    """The model around the blocks (coat_olmo.py:1138-1450): `transformer.wte` -> `Coat_quantize_bgn` -> the blocks
+    passing the (bf16, FP8 codes, scales) triple -> `Coat_quantize_end` -> `transformer.ln_f` -> `transformer.ff_out`
+    (or the tied embedding), with the reference's module names, hence its state-dict keys.  The training model: no KV
+    cache, no ALiBi, no document masking, no activation checkpointing (the host trainer's options around the model);
+    `attention_mask` (1 = attend) and `attention_bias` are turned into one additive bias as in the reference."""
+
+    def __init__(self, config, qargs: QuantizationConfig, init_params: bool = True):
+        super().__init__()
+        self.config = config
+        self.qargs = qargs
+        self._cache = {}
+        if getattr(config, "alibi", False):
+            raise NotImplementedError("ALiBi is not part of the quantised model")
+        if not getattr(config, "rope", True):
+            raise NotImplementedError("learned position embeddings are not part of the quantised model")
+        vocab = getattr(config, "embedding_size", None) or config.vocab_size
+        self.transformer = nn.ModuleDict(dict(
+            wte=nn.Embedding(vocab, config.d_model, device=_device(config)),
+            emb_drop=nn.Dropout(getattr(config, "embedding_dropout", 0.0)),
+            ln_f=_PlainLayerNorm(getattr(config, "layer_norm_eps", 1e-5)),
+            blocks=nn.ModuleList(CoatOLMoBlock.build(i, config, qargs, self._cache) for i in range(config.n_layers)),
+        ))
+        if not getattr(config, "weight_tying", False):
+            self.transformer.update({"ff_out": nn.Linear(config.d_model, vocab, bias=config.include_bias,
+                                                         device=_device(config))})
+        self.quantize_input_before_block = Coat_quantize_bgn(qargs)
+        self.quantize_output_after_block = Coat_quantize_end(qargs)
+        if init_params:
+            self.reset_parameters()
+
+    def reset_parameters(self):
+        """'mitchell' initialisation (the OLMo-7B configuration): embedding and output std 1/sqrt(d_model), cut at 3 std;
+        the blocks as CoatOLMoSequentialBlock.reset_parameters."""
+        std = 1 / math.sqrt(self.config.d_model)
+        nn.init.trunc_normal_(self.transformer.wte.weight, mean=0.0, std=std, a=-3 * std, b=3 * std)
+        if "ff_out" in self.transformer:
+            nn.init.trunc_normal_(self.transformer.ff_out.weight, mean=0.0, std=std, a=-3 * std, b=3 * std)
+        for block in self.transformer.blocks:
+            block.reset_parameters()
+
+    def forward(self, input_ids, input_embeddings=None, attention_mask=None, attention_bias=None,
+                past_key_values=None, use_cache: bool = False, last_logits_only: bool = False,
+                output_hidden_states: Optional[bool] = None, doc_lens=None, max_doc_lens=None):
+        if past_key_values is not None or use_cache:
+            raise NotImplementedError("the training model keeps no KV cache")
+        if doc_lens is not None or max_doc_lens is not None:
+            raise NotImplementedError("document masking needs the host trainer's variable-length attention")
+        x = self.transformer.wte(input_ids) if input_embeddings is None else input_embeddings
+        batch_size, seq_len = x.shape[:2]
+        x = self.transformer.emb_drop(x)
+        if attention_mask is not None or attention_bias is not None:
+            if attention_bias is None:   # causal
+                attention_bias = torch.zeros(1, 1, seq_len, seq_len, dtype=torch.float, device=x.device).masked_fill(
+                    torch.ones(seq_len, seq_len, dtype=torch.bool, device=x.device).triu(1), torch.finfo(torch.float).min)
+            elif attention_bias.dtype in (torch.int8, torch.bool):
+                attention_bias = attention_bias.to(dtype=torch.float)
+                attention_bias = attention_bias.masked_fill(attention_bias == 0.0, torch.finfo(torch.float).min)
+            attention_bias = attention_bias.reshape((-1, 1) + attention_bias.shape[-2:])[:, :, :seq_len, :seq_len].float()
+            if attention_mask is not None:
+                pad = (1.0 - attention_mask.to(torch.float).view(batch_size, -1)[:, None, None, :]) * torch.finfo(torch.float).min
+                attention_bias = (attention_bias + pad).clamp_min(torch.finfo(torch.float).min)
+        hidden = []
+        x, qx, sx = self.quantize_input_before_block(x)
+        for block in self.transformer.blocks:
+            if output_hidden_states:
+                hidden.append(x)
+            x, qx, sx, _ = block(x, qx, sx, attention_bias=attention_bias)
+        x = self.quantize_output_after_block(x, qx, sx)
+        if last_logits_only:
+            x = x[:, -1, :].unsqueeze(1)
+        x = self.transformer.ln_f(x)
+        if output_hidden_states:
+            hidden.append(x)
+        if getattr(self.config, "weight_tying", False):
+            logits = F.linear(x, self.transformer.wte.weight, None)
+        else:
+            logits = self.transformer.ff_out(x)
+        if getattr(self.config, "scale_logits", False):
+            logits = logits * (1 / math.sqrt(self.config.d_model))
+        return OLMoOutput(logits=logits, attn_key_values=None, hidden_states=tuple(hidden) if output_hidden_states else None)
+

@@ -189,3 +189,43 @@ def test_block_equals_the_composition_of_reference_operators(shape, monkeypatch)
     compare("input gradient", ours[1], theirs[1])
     for n in ours[2]:
         compare(f"gradient of {n}", ours[2][n], theirs[2][n])
+
+
+def test_whole_model_trains():
+    """`CoatOLMo` (two blocks) in training mode: loss within 2 % of the same model evaluated without quantisation, and
+    ten FP8-optimizer steps on fp32 masters reduce it."""
+    from types import SimpleNamespace
+
+    from coat_b200.fp8_trainer import MasterWeights, build_coat_optimizer
+    from coat_b200.models.coat_olmo import CoatOLMo
+    cfg = CoatOLMoConfig(d_model=256, n_heads=4, n_layers=2, mlp_hidden_size=1024, vocab_size=512, embedding_size=512,
+                         max_sequence_length=128, weight_tying=False)
+    qargs = QuantizationConfig(group_size=16, weight_memory_efficient=True)
+    torch.manual_seed(7)
+    model = CoatOLMo(cfg, qargs).to("cuda", torch.bfloat16)
+    ids = torch.randint(0, 512, (2, 128), generator=torch.Generator().manual_seed(8)).cuda()
+
+    def loss_of(m):
+        logits = m(ids).logits.float()
+        return torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, 512), ids[:, 1:].reshape(-1))
+
+    model.eval()
+    with torch.no_grad():
+        want = float(loss_of(model))
+    model.train()
+    FP8Manager.is_first_microbatch = True
+    first = float(loss_of(model).detach())
+    assert abs(first - want) <= 0.02 * want, (first, want)
+    args = SimpleNamespace(learning_rate=2e-3, adam_beta1=0.9, adam_beta2=0.95, adam_epsilon=1e-8, weight_decay=0.0)
+    masters = MasterWeights(model)
+    opt = build_coat_optimizer(masters, args, [n for n, p in model.named_parameters() if p.dim() == 2])
+    masters.attach(opt)
+    losses = []
+    for _ in range(10):
+        FP8Manager.is_first_microbatch = True
+        loss = loss_of(model)
+        loss.backward()
+        masters.copy_grads()
+        opt.step()
+        losses.append(float(loss.detach()))
+    assert losses[-1] < 0.8 * losses[0], losses
