@@ -1072,7 +1072,7 @@ def run_gpu_arm(args):
         exchange = "copy" if world == 2 else "p2p"   # ShardedCoatAdamW's own default, spelled out for the record
     try:
         opt = ShardedCoatAdamW(numels, rank=rank, world_size=world, device=device, exchange=exchange,
-                               copy_peers=args.copy_peers, **HYPER)
+                               copy_peers=args.copy_peers, n_buckets=args.buckets, **HYPER)
     except RuntimeError as e:   # raised on every rank alike when the peer mapping is not available
         if exchange not in ("p2p", "copy", "hybrid"):
             raise
@@ -1208,6 +1208,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama2-7b", choices=["llama2-7b", "c1", "quantizers", "fused", "gemm", "layer", "blockscaled", "reference-gpu"],
                     help="c1 = one 4096x4096 tensor, the small case used for ncu captures")
+    ap.add_argument("--buckets", type=int, default=None,
+                    help="bucketed exchanges: number of buckets the shard is cut into (default: 8)")
     ap.add_argument("--copy-peers", type=int, default=None,
                     help="hybrid exchange: how many peers the DMA engines serve (default: about a third)")
     ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl", "copy", "hybrid"],

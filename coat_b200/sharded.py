@@ -230,7 +230,8 @@ class ShardedCoatAdamW:
             raise ValueError(f"the p2p exchange serves at most {_lib.MAX_PEERS + 1} ranks")
         self.exchange = exchange
         if n_buckets is None:
-            n_buckets = 8 if exchange in ("nccl", "copy", "hybrid") else 1
+            # (copy exchange at two ranks, ms per step of the Llama-2-7B set: 4 buckets 23.1, 8: 21.6, 16: 21.0, 32: 20.9)
+            n_buckets = 16 if exchange == "copy" else (8 if exchange in ("nccl", "hybrid") else 1)
         self.bounds = self.plan.bucket_bounds(n_buckets)
         self.n_buckets = len(self.bounds) - 1
         self.my_buckets = self.plan.bucket_pieces(rank, self.n_buckets)
