@@ -220,7 +220,7 @@ class ShardedCoatAdamW:
         self.flags = flags
         self.step_count = 0
         if exchange is None:
-            # two ranks: the DMA engines hide the whole exchange under the plain kernel (21.8 ms against 26.2 ms for the
+            # two ranks: the DMA engines hide the whole exchange under the plain kernel (21.0 ms against 26.2 ms for the
             # fused kernel on the Llama-2-7B set); more ranks: the engines sustain only 350-380 GB/s into several peers
             # (28.7 ms against 17.6 ms at four ranks, 31.0 against 18.8 ms at eight), the fused kernel's stores 570-630
             exchange = "none" if world_size == 1 else ("copy" if world_size == 2 else "p2p")
