@@ -212,7 +212,8 @@ def run_reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32 math / e4m3 state", "data": "synthetic",
-        "config": workload_config(args.gpus, args.exchange),
+        # (the same configuration text as the GPU arm prints: "auto" resolved by the number of GPUs)
+        "config": workload_config(args.gpus, ("copy" if args.gpus == 2 else "p2p") if args.exchange == "auto" else args.exchange),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
                          "pure_pytorch": cpu_pure_pytorch_steps()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
