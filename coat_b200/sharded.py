@@ -182,6 +182,27 @@ def exchange_peer_buffers(make_buffer, rank, world_size, process_group=None):
     return buf
 
 
+def exchange_routes(rank, world_size, exchange, copy_peers=None):
+    """(ranks this rank's DMA engines copy its slice to, ranks its step kernel stores its slice to) for an exchange
+    kind.  "copy": every peer by the engines; "p2p": every peer by the kernel; "hybrid": the next `copy_peers` ranks
+    (about a third of the peers when None) by the engines, so that every rank also RECEIVES from exactly that many
+    engines, and the rest by the kernel; "nccl" / "none": neither (NCCL moves the slices, or nobody does)."""
+    n_peers = world_size - 1
+    if exchange == "copy":
+        k = n_peers
+    elif exchange == "hybrid":
+        k = copy_peers if copy_peers is not None else max(1, round(0.35 * n_peers))
+        k = min(max(int(k), 0), n_peers)
+    else:
+        k = 0
+    copy_ranks = [(rank + 1 + i) % world_size for i in range(k)]
+    if exchange in ("p2p", "hybrid"):
+        store_ranks = [r for r in range(world_size) if r != rank and r not in copy_ranks]
+    else:
+        store_ranks = []
+    return copy_ranks, store_ranks
+
+
 class ShardedCoatAdamW:
     """One rank's slice of the optimizer: flat buffers and one of two ways to get every rank's bf16
     weights everywhere.
@@ -252,18 +273,8 @@ class ShardedCoatAdamW:
         self._peer_buffer = None
         self._peer_deltas = None
         self._n_store_peers = None   # how many entries of _peer_deltas the kernel stores to (None: all of them)
-        # which peers receive this rank's slice from the DMA engines (the others from the kernel's stores): the next
-        # `copy_peers` ranks, so that every rank also RECEIVES from exactly that many engines
-        n_peers = world_size - 1
-        if exchange == "copy":
-            k = n_peers
-        elif exchange == "hybrid":
-            k = copy_peers if copy_peers is not None else max(1, round(0.35 * n_peers))
-            k = min(max(int(k), 0), n_peers)
-        else:
-            k = 0
-        self._copy_ranks = [(rank + 1 + i) % world_size for i in range(k)]
-        self._store_ranks = [r for r in range(world_size) if r != rank and r not in self._copy_ranks]
+        # which peers receive this rank's slice from the DMA engines and which from the kernel's stores
+        self._copy_ranks, self._store_ranks = exchange_routes(rank, world_size, exchange, copy_peers)
         if exchange in ("p2p", "copy", "hybrid"):
             self._setup_peer_buffer(world_size * n * 2)
         else:
@@ -288,8 +299,7 @@ class ShardedCoatAdamW:
                                     self.process_group)
         self._peer_buffer = buf
         self.gathered = torch.as_tensor(buf, device=self.device).view(torch.bfloat16)
-        store_ranks = self._store_ranks if self.exchange != "p2p" else [r for r in range(self.world_size) if r != self.rank]
-        deltas = [buf.peers[r] - buf.ptr for r in store_ranks]
+        deltas = [buf.peers[r] - buf.ptr for r in self._store_ranks]
         self._peer_deltas = (ctypes.c_int64 * max(1, len(deltas)))(*deltas)
         self._n_store_peers = len(deltas)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)

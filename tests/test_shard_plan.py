@@ -224,3 +224,34 @@ def _verify_worker(rank, world, port, corrupt_rank):
 def test_gather_verification_of_the_benchmark_world2_gloo(corrupt_rank):
     port = 35500 + os.getpid() % 2000 + (0 if corrupt_rank is None else 7)
     mp.spawn(_verify_worker, args=(2, port, corrupt_rank), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("exchange,k", [("p2p", None), ("copy", None), ("hybrid", None), ("hybrid", 1), ("hybrid", 3)])
+def test_exchange_routes_cover_every_pair_once(world, exchange, k):
+    """Every ordered pair (sender, receiver) is served by exactly one transport, and under "hybrid" every rank
+    receives from as many DMA engines as it feeds."""
+    from coat_b200.sharded import exchange_routes
+    served = {}
+    copies_into = {r: 0 for r in range(world)}
+    for rank in range(world):
+        copy_ranks, store_ranks = exchange_routes(rank, world, exchange, k)
+        assert rank not in copy_ranks and rank not in store_ranks
+        assert not set(copy_ranks) & set(store_ranks)
+        for r in copy_ranks + store_ranks:
+            assert (rank, r) not in served
+            served[(rank, r)] = True
+        for r in copy_ranks:
+            copies_into[r] += 1
+        if exchange == "p2p":
+            assert not copy_ranks
+        if exchange == "copy":
+            assert not store_ranks
+    assert len(served) == world * (world - 1)
+    assert len(set(copies_into.values())) == 1   # the engines' traffic is spread evenly over the receivers
+
+
+def test_exchange_routes_without_peer_transport():
+    from coat_b200.sharded import exchange_routes
+    assert exchange_routes(1, 4, "nccl") == ([], [])
+    assert exchange_routes(0, 1, "none") == ([], [])
